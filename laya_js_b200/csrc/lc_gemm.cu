@@ -1,0 +1,491 @@
+// Tensor-core GEMM for sm_100a: y[M, N] = x[M, K] · w[N, K]ᵀ with a fused epilogue.
+//
+// Replaces the reference's linear kernels (WGSL gemm*Kernel,
+// packages/backend-webgpu/src/kernels.ts:648-918; MLX addmm/matmul,
+// packages/backend-mlx/src/index.ts:576-587) for the contract op `linear`
+// (packages/tensor-backend/src/index.ts:211-215: f32 accumulation).
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: 128x64 tiles of x and BNx64 tiles of w, 128-byte
+//               swizzle, into a STAGES-deep shared-memory ring (mbarrier full/empty);
+//   warp 1      allocates TMEM and issues tcgen05.mma (M=128, N=BN, K=16,
+//               fp16/bf16 in, f32 accumulate) from one elected thread; commits
+//               free the ring slot and, per tile, signal the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator (each warp owns 32
+//               TMEM lanes = 32 rows), fused bias / residual / RoPE / GeGLU,
+//               16-byte stores.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the main loop of tile i+1. Every mbarrier wait is bounded
+// (2 s of %globaltimer); on timeout the kernel records an error word, drains
+// its own in-flight copies and MMAs, frees TMEM and returns.
+// No cluster launch and no multicast: each CTA loads its own tiles.
+#include "lc_api.h"
+#include "lc_gemm.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <tuple>
+
+__device__ unsigned int g_gemm_err;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for phase `parity` of `bar`; false on timeout or when another
+// role has aborted (then the caller unwinds).
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = gtimer();
+  for (uint32_t it = 0;; it++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63) == 63) {
+      if (*abort) return false;
+      if (gtimer() - t0 > kWaitNs) {
+        *abort = 1;
+        atomicOr(&g_gemm_err, 1u);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row
+// groups 1024 bytes apart (tcgen05 "matrix descriptor", version 1).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                   // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
+  return d;
+}
+
+template <typename T> struct TcFmt;
+template <> struct TcFmt<__half> {
+  static constexpr uint32_t ab = 0;
+  __device__ static __half cvt(float v) { return __float2half_rn(v); }
+  __device__ static float back(__half v) { return __half2float(v); }
+};
+template <> struct TcFmt<__nv_bfloat16> {
+  static constexpr uint32_t ab = 1;
+  __device__ static __nv_bfloat16 cvt(float v) { return __float2bfloat16_rn(v); }
+  __device__ static float back(__nv_bfloat16 v) { return __bfloat162float(v); }
+};
+
+// Instruction descriptor for kind::f16: D=f32, A=B=T, both K-major, M=128, N=BN.
+template <typename T, int BN>
+__device__ __forceinline__ uint32_t idesc_f16() {
+  return (1u << 4) | (TcFmt<T>::ab << 7) | (TcFmt<T>::ab << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+struct GemmArgs {
+  int M, N, K;
+  int ntile_n, ntiles;
+  void* y;
+  int64_t ldy;
+  int vec_ok;  // 16-byte stores allowed (ldy % 8 == 0)
+  const void* bias;
+  int bias_dtype;
+  GemmEpilogue ep;
+};
+
+__device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
+
+// store 32 consecutive values v[0..31] at columns [col, col+32) of row `row`, valid columns < ncols
+template <typename T>
+__device__ __forceinline__ void store32(T* rowp, int col, int ncols, const float* v, bool vec) {
+  if (vec && col + 32 <= ncols) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      uint4 u;
+      T* h = (T*)&u;
+#pragma unroll
+      for (int j = 0; j < 8; j++) h[j] = TcFmt<T>::cvt(v[q * 8 + j]);
+      *(uint4*)(rowp + col + q * 8) = u;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      if (col + j < ncols) rowp[col + j] = TcFmt<T>::cvt(v[j]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void load32f(const T* p, int col, int ncols, float* v, bool vec) {
+  if (vec && col + 32 <= ncols) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      uint4 u = *(const uint4*)(p + col + q * 8);
+      const T* h = (const T*)&u;
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[q * 8 + j] = TcFmt<T>::back(h[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = (col + j < ncols) ? TcFmt<T>::back(p[col + j]) : 0.f;
+  }
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                                    const __grid_constant__ GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = (uint64_t*)(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
+  volatile int* abort = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int issued[STAGES];
+      uint32_t iss_phase[STAGES];
+      for (int s = 0; s < STAGES; s++) issued[s] = 0, iss_phase[s] = 0;
+      for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
+        int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
+        for (int kb = 0; kb < KB; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, m0);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, n0);
+          issued[stage] = 1;
+          iss_phase[stage] = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: every copy this thread issued must have landed before the CTA exits
+      for (int s = 0; s < STAGES; s++)
+        if (issued[s]) {
+          uint64_t t0 = gtimer();
+          while (!mbar_try_wait(&full[s], iss_phase[s]) && gtimer() - t0 < kWaitNs) {}
+        }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16<T, BN>();
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool committed = false;
+      uint64_t* last = nullptr;
+      uint32_t last_phase = 0;
+      for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < KB; kb++) {
+          if (!mbar_wait(&full[stage], phase, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES), b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)
+            tc_mma(d, sdesc_sw128(a0 + k * 32), sdesc_sw128(b0 + k * 32), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit(&empty[stage]);
+          committed = true;
+          last = &empty[stage];
+          last_phase = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      // drain: the MMAs this thread issued must finish before TMEM is freed
+      if (committed) {
+        uint64_t t0 = gtimer();
+        while (!mbar_try_wait(last, last_phase) && gtimer() - t0 < kWaitNs) {}
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 -> TMEM lane quarter warp % 4)
+    const int quarter = warp & 3;
+    const bool vec = args.vec_ok != 0;
+    T* Y = (T*)args.y;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < args.ntiles; t += gridDim.x) {
+      if (!mbar_wait(&tfull[acc], acc_phase, abort)) break;
+      tc_fence_after();
+      const int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const bool live = row < args.M;
+      T* rowp = Y + (int64_t)row * args.ldy;
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int u = 0; u < BN / 64; u++) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tbase + u * 64, ra);
+        tmem_ld32(tbase + u * 64 + 32, rb);
+        tmem_wait_ld();
+        float a[32], b[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) a[j] = __uint_as_float(ra[j]), b[j] = __uint_as_float(rb[j]);
+        const int col = n0 + u * 64;
+        if (!live || col >= (args.ep.kind == EPI_GEGLU ? 2 * args.N : args.N)) continue;
+        const GemmEpilogue& ep = args.ep;
+        if (ep.kind == EPI_GEGLU) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) a[j] = gelu_exact(a[j]) * b[j];
+          store32<T>(rowp, col / 2, args.N, a, vec);
+          continue;
+        }
+        if (ep.kind == EPI_ROPE_QKV && col < ep.rope_cols) {
+          const int p = ep.pos[row];
+          const float* cs = ep.rope_cs + (int64_t)p * 32;
+          const float* sn = ep.rope_cs + (int64_t)ep.rope_cap * 32 + (int64_t)p * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            float c = cs[j], s = sn[j];
+            float x1 = a[j], x2 = b[j];
+            a[j] = x1 * c - x2 * s;
+            b[j] = x2 * c + x1 * s;
+          }
+        }
+        if (args.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            if (col + j < args.N) a[j] += ld_as<float>((const char*)args.bias, args.bias_dtype, col + j);
+            if (col + 32 + j < args.N) b[j] += ld_as<float>((const char*)args.bias, args.bias_dtype, col + 32 + j);
+          }
+        }
+        if (ep.kind == EPI_RESIDUAL) {
+          const T* rp = (const T*)ep.resid + (int64_t)row * ep.ldr;
+          float r[32];
+          load32f<T>(rp, col, args.N, r, vec);
+#pragma unroll
+          for (int j = 0; j < 32; j++) a[j] += r[j];
+          load32f<T>(rp, col + 32, args.N, r, vec);
+#pragma unroll
+          for (int j = 0; j < 32; j++) b[j] += r[j];
+        }
+        store32<T>(rowp, col, args.N, a, vec);
+        store32<T>(rowp, col + 32, args.N, b, vec);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CUDA_OK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    LC_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled is not available from the driver");
+    fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  }
+  return fn;
+}
+
+using MapKey = std::tuple<uintptr_t, int64_t, int64_t, int, int>;
+std::map<MapKey, CUtensorMap>& map_cache() {
+  static std::map<MapKey, CUtensorMap> m;
+  return m;
+}
+
+// Row-major [rows, K] matrix, boxes of box_rows x 64, 128-byte swizzle.
+const CUtensorMap& tensor_map(const void* ptr, int64_t rows, int64_t K, int box_rows, int dtype) {
+  MapKey key{(uintptr_t)ptr, rows, K, box_rows, dtype};
+  auto& c = map_cache();
+  auto it = c.find(key);
+  if (it != c.end()) return it->second;
+  if (c.size() > 8192) c.clear();
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(&m, dtype == LC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr),
+                           dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LC_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return c.emplace(key, m).first->second;
+}
+
+template <typename T, int BN, int STAGES>
+void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st) {
+  constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  static bool attr = false;
+  if (!attr) {
+    CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<T, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = true;
+  }
+  int grid = std::min(a.ntiles, lc::num_sms());
+  k_gemm_tc<T, BN, STAGES><<<grid, 192, smem, st>>>(ma, mb, a);
+}
+
+}  // namespace
+
+namespace lc {
+
+bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, const void* bias, int bias_dtype, void* y, int64_t ldy,
+              int dtype, const GemmEpilogue& ep, cudaStream_t st) {
+  if (!(dtype == LC_F16 || dtype == LC_BF16)) return false;
+  if (M <= 0 || N <= 0 || K < 16 || K % 8) return false;
+  if (((uintptr_t)x | (uintptr_t)w) & 15) return false;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
+  // the accumulator width covered by the weight rows: GeGLU produces N outputs from 2N rows
+  int64_t Nacc = ep.kind == EPI_GEGLU ? 2 * N : N;
+  int BN = (Nacc % 256 == 0 || Nacc > 1024) ? 256 : 128;
+  if (ep.kind == EPI_GEGLU && Nacc % BN) BN = 128;
+  if (ep.kind == EPI_ROPE_QKV && (ep.rope_cols % 64)) return false;
+  GemmArgs a{};
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.ntile_n = (int)((Nacc + BN - 1) / BN);
+  int64_t tiles = ((M + BM - 1) / BM) * a.ntile_n;
+  if (tiles > INT32_MAX) return false;
+  a.ntiles = (int)tiles;
+  a.y = y;
+  a.ldy = ldy;
+  a.vec_ok = (ldy % 8 == 0 && ((uintptr_t)y & 15) == 0 && (ep.kind != EPI_RESIDUAL || (ep.ldr % 8 == 0 && ((uintptr_t)ep.resid & 15) == 0))) ? 1 : 0;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.ep = ep;
+  const CUtensorMap& ma = tensor_map(x, M, K, BM, dtype);
+  const CUtensorMap& mb = tensor_map(w, Nacc, K, BN, dtype);
+  if (dtype == LC_F16) {
+    if (BN == 256) launch_gemm<__half, 256, 4>(ma, mb, a, st);
+    else launch_gemm<__half, 128, 6>(ma, mb, a, st);
+  } else {
+    if (BN == 256) launch_gemm<__nv_bfloat16, 256, 4>(ma, mb, a, st);
+    else launch_gemm<__nv_bfloat16, 128, 6>(ma, mb, a, st);
+  }
+  LC_LAUNCHED(1);
+  return true;
+}
+
+bool gemm_linear(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y, const GemmEpilogue& ep) {
+  int64_t M = x2->shape[0], K = x2->shape[1], N = w->shape[0];
+  if (K < 64) return false;  // tiny reductions stay on the SIMT path
+  return gemm_raw(x2->data(), M, K, w->data(), N, bias ? bias->data() : nullptr, bias ? bias->dtype : 0, y->data(), N, y->dtype, ep,
+                  stream());
+}
+
+std::string take_device_errors() {
+  unsigned int e = 0, z = 0;
+  CUDA_OK(cudaMemcpyFromSymbol(&e, g_gemm_err, sizeof(e)));
+  if (!e) return "";
+  CUDA_OK(cudaMemcpyToSymbol(g_gemm_err, &z, sizeof(z)));
+  return "tcgen05 GEMM: a pipeline wait timed out (kernel aborted its tile loop)";
+}
+
+}  // namespace lc
+
+void lc_gemm_destroy_caches() { map_cache().clear(); }

@@ -1,0 +1,722 @@
+// NN ops of the contract that are not the tensor-core GEMM:
+// layerNorm, embedding, gatherRows, rope, sdpa (generic), geglu, meanPool,
+// matmul and the exact-f32 SIMT linear used for f32/f64 and shapes the
+// tcgen05 GEMM does not take (packages/tensor-backend/src/index.ts:208-243).
+#include "lc_api.h"
+#include "lc_gemm.h"
+
+#include <cmath>
+#include <map>
+#include <tuple>
+
+using namespace lc;
+
+// ------------------------------------------------------------- layerNorm
+// index.ts:216-217: normalise over the last axis, stats in f32, optional weight/bias.
+
+// Vectorised fast path: dense f16/bf16/f32 rows, N % 8 == 0 (f32: % 4), N <= 256 vectors.
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, const char* w, int wdt, const char* b, int bdt,
+                                                       T* __restrict__ y, int64_t rows, int N, float eps) {
+  constexpr int VN = 16 / sizeof(T);
+  int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  int nv = N / VN;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    float v[MAXV][VN];
+    float s = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      int c = t * 32 + lane;
+      if (c < nv) {
+        uint4 raw = *(const uint4*)(x + r * N + (int64_t)c * VN);
+        const T* e = (const T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VN; j++) {
+          float f;
+          if constexpr (sizeof(T) == 4) f = ((const float*)e)[j];
+          else if constexpr (std::is_same<T, __half>::value) f = __half2float(e[j]);
+          else f = __bfloat162float(e[j]);
+          v[t][j] = f;
+          s += f;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    float mu = s / N;
+    float q = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      if (t * 32 + lane < nv) {
+#pragma unroll
+        for (int j = 0; j < VN; j++) {
+          float d = v[t][j] - mu;
+          q += d * d;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    float rs = rsqrtf(q / N + eps);
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      int c = t * 32 + lane;
+      if (c < nv) {
+        uint4 raw;
+        T* e = (T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VN; j++) {
+          int col = c * VN + j;
+          float o = (v[t][j] - mu) * rs;
+          if (w) o *= ld_as<float>(w, wdt, col);
+          if (b) o += ld_as<float>(b, bdt, col);
+          if constexpr (sizeof(T) == 4) ((float*)e)[j] = o;
+          else if constexpr (std::is_same<T, __half>::value) e[j] = __float2half_rn(o);
+          else e[j] = __float2bfloat16_rn(o);
+        }
+        *(uint4*)(y + r * N + (int64_t)c * VN) = raw;
+      }
+    }
+  }
+}
+
+template <typename CT>
+__global__ void k_layernorm_generic(const char* x, int xdt, const char* w, int wdt, const char* b, int bdt, char* y, int ydt,
+                                    int64_t rows, int64_t N, double eps) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    CT s = 0;
+    for (int64_t j = lane; j < N; j += 32) s += ld_as<CT>(x, xdt, r * N + j);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    CT mu = s / (CT)N;
+    CT q = 0;
+    for (int64_t j = lane; j < N; j += 32) {
+      CT d = ld_as<CT>(x, xdt, r * N + j) - mu;
+      q += d * d;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    CT rs = (CT)1 / sqrt(q / (CT)N + (CT)eps);
+    for (int64_t j = lane; j < N; j += 32) {
+      CT o = (ld_as<CT>(x, xdt, r * N + j) - mu) * rs;
+      if (w) o *= ld_as<CT>(w, wdt, j);
+      if (b) o += ld_as<CT>(b, bdt, j);
+      st_as<CT>(y, ydt, r * N + j, o);
+    }
+  }
+}
+
+// ------------------------------------------------------------- gathers
+
+// out row r = table[ids[r]] (zeros for an out-of-range id)
+__global__ void k_gather_rows(const char* table, int64_t V, int64_t rowbytes, const char* ids, int iddt, char* out, int64_t n,
+                              int64_t group, const int64_t group_rows) {
+  // group/group_rows: for gatherRows, row r reads from batch r / group, offset batch*group_rows
+  int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  bool vec = (rowbytes % 16 == 0) && (((uintptr_t)table & 15) == 0) && (((uintptr_t)out & 15) == 0);
+  for (int64_t r = warp; r < n; r += nwarps) {
+    int64_t id = ld_as<int64_t>(ids, iddt, r);
+    int64_t base = group > 0 ? (r / group) * group_rows : 0;
+    bool ok = id >= 0 && id < V;
+    const char* src = table + (base + (ok ? id : 0)) * rowbytes;
+    char* dst = out + r * rowbytes;
+    if (vec) {
+      for (int64_t c = lane; c < rowbytes / 16; c += 32)
+        ((uint4*)dst)[c] = ok ? ((const uint4*)src)[c] : make_uint4(0, 0, 0, 0);
+    } else {
+      for (int64_t c = lane; c < rowbytes; c += 32) dst[c] = ok ? src[c] : 0;
+    }
+  }
+}
+
+// ------------------------------------------------------------- rope
+// index.ts:225-229: split-half rotation over x [..., L, D], positions 0..L-1.
+// cos/sin come from a table built on the host with MLX's f32 angle rounding
+// (packages/backend-webgpu/src/backend.ts:1179-1195).
+
+__global__ void k_rope(TV x, const float* __restrict__ cs, int64_t rows, int64_t L, int half, int cap, char* out) {
+  // cs: [cap, half] cos then [cap, half] sin
+  LC_GRID_STRIDE(t, rows * half) {
+    int64_t r = t / half;
+    int i = (int)(t % half);
+    int64_t l = r % L;
+    // offset of row r (dims 0..ndim-2) in x
+    int64_t rr = r, off = 0;
+    for (int d = x.ndim - 2; d >= 0; d--) {
+      off += (rr % x.shape[d]) * x.strides[d];
+      rr /= x.shape[d];
+    }
+    int64_t sd = x.strides[x.ndim - 1];
+    float a = ld_as<float>(x.ptr, x.dtype, off + i * sd);
+    float b = ld_as<float>(x.ptr, x.dtype, off + (i + half) * sd);
+    float c = cs[l * half + i], s = cs[(int64_t)cap * half + l * half + i];
+    int64_t o = r * 2 * half;
+    st_as<float>(out, x.dtype, o + i, a * c - b * s);
+    st_as<float>(out, x.dtype, o + i + half, b * c + a * s);
+  }
+}
+
+namespace {
+struct RopeTable {
+  float* d = nullptr;
+  int cap = 0;
+};
+std::map<std::pair<int, double>, RopeTable>& rope_cache() {
+  static std::map<std::pair<int, double>, RopeTable> m;
+  return m;
+}
+}  // namespace
+
+namespace lc {
+// cos/sin table [cap][half] ++ [cap][half] (f32) for head dim D and `base`, cap >= L.
+const float* rope_table(int D, double base, int L, int* cap_out) {
+  auto& t = rope_cache()[{D, base}];
+  if (t.cap < L) {
+    int cap = 64;
+    while (cap < L) cap <<= 1;
+    int half = D / 2;
+    std::vector<float> h((size_t)2 * cap * half);
+    float lb = (float)std::log2(base);
+    for (int i = 0; i < half; i++) {
+      float e = (float)(-(double)(float)((double)i / half) * (double)lb);
+      float inv = (float)std::pow(2.0, (double)e);
+      for (int l = 0; l < cap; l++) {
+        float th = (float)((double)l * (double)inv);
+        h[(size_t)l * half + i] = (float)std::cos((double)th);
+        h[(size_t)cap * half + (size_t)l * half + i] = (float)std::sin((double)th);
+      }
+    }
+    if (t.d) CUDA_OK(cudaFree(t.d));
+    CUDA_OK(cudaMalloc(&t.d, h.size() * sizeof(float)));
+    CUDA_OK(cudaMemcpy(t.d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+    t.cap = cap;
+  }
+  *cap_out = t.cap;
+  return t.d;
+}
+}  // namespace lc
+
+void lc_internal_destroy_caches() {
+  for (auto& kv : rope_cache())
+    if (kv.second.d) cudaFree(kv.second.d);
+  rope_cache().clear();
+  lc_gemm_destroy_caches();
+}
+
+// ------------------------------------------------------------- sdpa (generic)
+// index.ts:230-237. One warp per query row; keys in chunks of 32 with an
+// online softmax in f32. Any dtype/strides, D and Dv <= 256, bool mask
+// broadcast to [B, H, Lq, Lk] (strides 0 on broadcast axes).
+
+#define SDPA_MAXD 256
+__global__ void __launch_bounds__(128) k_sdpa_generic(TV q, TV k, TV v, TV m, int has_mask, float scale, char* out, int odt,
+                                                      int64_t B, int64_t H, int64_t Lq, int64_t Lk, int D, int Dv) {
+  __shared__ float qs[4][SDPA_MAXD];
+  int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int64_t row = (int64_t)blockIdx.x * 4 + w;
+  if (row >= B * H * Lq) return;
+  int64_t i = row % Lq, bh = row / Lq, h = bh % H, b = bh / H;
+  int64_t qo = b * q.strides[0] + h * q.strides[1] + i * q.strides[2];
+  for (int d = lane; d < D; d += 32) qs[w][d] = ld_as<float>(q.ptr, q.dtype, qo + d * q.strides[3]) * scale;
+  __syncwarp();
+  int64_t kb = b * k.strides[0] + h * k.strides[1];
+  int64_t vb = b * v.strides[0] + h * v.strides[1];
+  int64_t mb = has_mask ? b * m.strides[0] + h * m.strides[1] + i * m.strides[2] : 0;
+  float acc[SDPA_MAXD / 32];
+#pragma unroll
+  for (int t = 0; t < SDPA_MAXD / 32; t++) acc[t] = 0.f;
+  float mx = -INFINITY, l = 0.f;
+  for (int64_t j0 = 0; j0 < Lk; j0 += 32) {
+    int64_t j = j0 + lane;
+    float s = -INFINITY;
+    if (j < Lk) {
+      bool keep = true;
+      if (has_mask) keep = ((const uint8_t*)m.ptr)[mb + j * m.strides[3]] != 0;
+      if (keep) {
+        float dot = 0.f;
+        int64_t ko = kb + j * k.strides[2];
+        for (int d = 0; d < D; d++) dot += qs[w][d] * ld_as<float>(k.ptr, k.dtype, ko + d * k.strides[3]);
+        s = dot;
+      }
+    }
+    float cm = s;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+    float nm = fmaxf(mx, cm);
+    if (nm == -INFINITY) continue;  // every key so far masked
+    float corr = __expf(mx - nm);
+    float p = (s == -INFINITY) ? 0.f : __expf(s - nm);
+    float ps = p;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    l = l * corr + ps;
+#pragma unroll
+    for (int t = 0; t < SDPA_MAXD / 32; t++) acc[t] *= corr;
+    int cnt = (Lk - j0) < 32 ? (int)(Lk - j0) : 32;
+    for (int jj = 0; jj < cnt; jj++) {
+      float pj = __shfl_sync(0xffffffffu, p, jj);
+      if (pj == 0.f) continue;
+      int64_t vo = vb + (j0 + jj) * v.strides[2];
+#pragma unroll
+      for (int t = 0; t < SDPA_MAXD / 32; t++) {
+        int d = t * 32 + lane;
+        if (d < Dv) acc[t] += pj * ld_as<float>(v.ptr, v.dtype, vo + d * v.strides[3]);
+      }
+    }
+    mx = nm;
+  }
+  float inv = 1.f / l;
+  int64_t oo = row * Dv;
+#pragma unroll
+  for (int t = 0; t < SDPA_MAXD / 32; t++) {
+    int d = t * 32 + lane;
+    if (d < Dv) st_as<float>(out, odt, oo + d, acc[t] * inv);
+  }
+}
+
+// ------------------------------------------------------------- geglu / meanPool
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_geglu_vec(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int64_t F) {
+  constexpr int VN = 16 / sizeof(T);
+  int64_t nv = F / VN;
+  LC_GRID_STRIDE(t, rows * nv) {
+    int64_t r = t / nv, c = (t % nv) * VN;
+    uint4 ra = *(const uint4*)(x + r * 2 * F + c);
+    uint4 rb = *(const uint4*)(x + r * 2 * F + F + c);
+    uint4 ro;
+    const T* a = (const T*)&ra;
+    const T* g = (const T*)&rb;
+    T* o = (T*)&ro;
+#pragma unroll
+    for (int j = 0; j < VN; j++) {
+      float av, gv;
+      if constexpr (sizeof(T) == 4) { av = ((const float*)a)[j]; gv = ((const float*)g)[j]; }
+      else if constexpr (std::is_same<T, __half>::value) { av = __half2float(a[j]); gv = __half2float(g[j]); }
+      else { av = __bfloat162float(a[j]); gv = __bfloat162float(g[j]); }
+      float r2 = 0.5f * av * (1.0f + erff(av * 0.7071067811865476f)) * gv;
+      if constexpr (sizeof(T) == 4) ((float*)o)[j] = r2;
+      else if constexpr (std::is_same<T, __half>::value) o[j] = __float2half_rn(r2);
+      else o[j] = __float2bfloat16_rn(r2);
+    }
+    *(uint4*)(y + r * F + c) = ro;
+  }
+}
+
+template <typename CT>
+__global__ void k_geglu_generic(const char* x, int xdt, char* y, int ydt, int64_t rows, int64_t F) {
+  LC_GRID_STRIDE(t, rows * F) {
+    int64_t r = t / F, c = t % F;
+    CT a = ld_as<CT>(x, xdt, r * 2 * F + c), g = ld_as<CT>(x, xdt, r * 2 * F + F + c);
+    st_as<CT>(y, ydt, t, (CT)0.5 * a * ((CT)1 + erf(a * (CT)0.7071067811865476)) * g);
+  }
+}
+
+__global__ void k_mean_pool(const char* x, int xdt, const char* mask, int mdt, float* out, int64_t B, int64_t L, int64_t D) {
+  LC_GRID_STRIDE(t, B * D) {
+    int64_t b = t / D, d = t % D;
+    float s = 0.f, n = 0.f;
+    for (int64_t l = 0; l < L; l++) {
+      if (ld_as<int64_t>(mask, mdt, b * L + l) != 0) {
+        s += ld_as<float>(x, xdt, (b * L + l) * D + d);
+        n += 1.f;
+      }
+    }
+    out[t] = s / fmaxf(n, 1.f);
+  }
+}
+
+// ------------------------------------------------------------- matmul / SIMT linear
+
+// C[b] = A[b] (m x k) · B[b] (k x n) (B given by strides so w[N,K] works as Bᵀ),
+// 64x64 tiles, 16-deep k steps, 4x4 outputs per thread, CT accumulation.
+struct MM {
+  const char* a;
+  const char* b;
+  char* c;
+  const char* bias;
+  int adt, bdt, cdt, biasdt;
+  int64_t m, n, k;
+  int64_t sam, sak, sbk, sbn;  // element strides inside one matrix
+  // batch addressing: up to 6 batch dims, broadcast strides for a and b
+  int nb;
+  int64_t bshape[6], bsa[6], bsb[6];
+};
+
+template <typename CT>
+__global__ void __launch_bounds__(256) k_matmul(MM p) {
+  __shared__ CT As[16][64 + 1];
+  __shared__ CT Bs[16][64 + 1];
+  int64_t bz = blockIdx.z;
+  int64_t offa = 0, offb = 0, rem = bz;
+  for (int d = p.nb - 1; d >= 0; d--) {
+    int64_t c = rem % p.bshape[d];
+    rem /= p.bshape[d];
+    offa += c * p.bsa[d];
+    offb += c * p.bsb[d];
+  }
+  int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  int64_t m0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
+  CT acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j] = 0;
+  for (int64_t k0 = 0; k0 < p.k; k0 += 16) {
+    for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+      int kk = e % 16, mm = e / 16;
+      int64_t gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < p.m && gk < p.k) ? ld_as<CT>(p.a, p.adt, offa + gm * p.sam + gk * p.sak) : (CT)0;
+      int nn = e / 16;
+      int64_t gn = n0 + nn;
+      Bs[kk][nn] = (gn < p.n && gk < p.k) ? ld_as<CT>(p.b, p.bdt, offb + gk * p.sbk + gn * p.sbn) : (CT)0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; kk++) {
+      CT av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; j++) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] += av[i] * bv[j];
+    }
+    __syncthreads();
+  }
+  int64_t offc = (int64_t)bz * p.m * p.n;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    int64_t gm = m0 + ty * 4 + i;
+    if (gm >= p.m) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      int64_t gn = n0 + tx * 4 + j;
+      if (gn >= p.n) continue;
+      CT v = acc[i][j];
+      if (p.bias) v += ld_as<CT>(p.bias, p.biasdt, gn);
+      st_as<CT>(p.c, p.cdt, offc + gm * p.n + gn, v);
+    }
+  }
+}
+
+namespace {
+
+void launch_mm(const MM& p, int64_t batch, bool dbl) {
+  dim3 grid((unsigned)((p.n + 63) / 64), (unsigned)((p.m + 63) / 64), (unsigned)batch);
+  LC_CHECK(batch <= 65535 && grid.y <= 65535, "matmul: batch or row count too large for the SIMT path");
+  if (dbl) k_matmul<double><<<grid, 256, 0, stream()>>>(p);
+  else k_matmul<float><<<grid, 256, 0, stream()>>>(p);
+  LC_LAUNCHED(1);
+}
+
+int float_out(int a, int b) {
+  int d = promote(a, b);
+  return is_float(d) ? d : LC_F32;
+}
+
+}  // namespace
+
+namespace lc {
+// y [M, N] = x [M, K] · w[N, K]ᵀ (+ bias) on the SIMT path (exact f32 / f64 accumulation).
+void linear_simt(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y) {
+  MM p{};
+  p.a = x2->data(); p.adt = x2->dtype;
+  p.b = w->data(); p.bdt = w->dtype;
+  p.c = y->data(); p.cdt = y->dtype;
+  p.bias = bias ? bias->data() : nullptr; p.biasdt = bias ? bias->dtype : 0;
+  p.m = x2->shape[0]; p.k = x2->shape[1]; p.n = w->shape[0];
+  p.sam = p.k; p.sak = 1;
+  p.sbk = 1; p.sbn = p.k;  // w[n, k]
+  p.nb = 0;
+  if (p.m && p.n) launch_mm(p, 1, y->dtype == LC_F64 || x2->dtype == LC_F64);
+}
+}  // namespace lc
+
+extern "C" {
+
+int lc_layer_norm(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh, double eps) {
+  LC_API_BEGIN
+  LcTensor* x0 = check(xh, "layerNorm");
+  LC_CHECK(x0->ndim >= 1, "layerNorm: scalar input");
+  int64_t N = x0->shape[x0->ndim - 1];
+  LcTensor* w0 = wh ? check(wh, "layerNorm weight") : nullptr;
+  LcTensor* b0 = bh ? check(bh, "layerNorm bias") : nullptr;
+  if (w0) LC_CHECK(w0->numel() == N, "layerNorm: weight size differs from the last axis");
+  if (b0) LC_CHECK(b0->numel() == N, "layerNorm: bias size differs from the last axis");
+  int odt = is_float(x0->dtype) ? x0->dtype : LC_F32;
+  LcTensor* y = alloc(odt, x0->dims());
+  int64_t rows = N ? x0->numel() / N : 0;
+  if (rows) {
+    LcTensor* x = contiguous(x0);
+    LcTensor* w = w0 ? contiguous(w0) : nullptr;
+    LcTensor* b = b0 ? contiguous(b0) : nullptr;
+    const char* wp = w ? w->data() : nullptr;
+    const char* bp = b ? b->data() : nullptr;
+    int wdt = w ? w->dtype : 0, bdt = b ? b->dtype : 0;
+    unsigned blocks = blocks_for(rows * 32, 256);
+    cudaStream_t st = stream();
+    bool aligned = (((uintptr_t)x->data() | (uintptr_t)y->data()) & 15) == 0;
+    int vn = x->dtype == LC_F32 ? 4 : 8;
+    bool vec = aligned && x->dtype == odt && (odt == LC_F32 || is_half(odt)) && N % vn == 0 && N / vn <= 32 * 8;
+    if (vec) {
+      if (odt == LC_F16) k_layernorm_vec<__half, 8><<<blocks, 256, 0, st>>>((const __half*)x->data(), wp, wdt, bp, bdt, (__half*)y->data(), rows, (int)N, (float)eps);
+      else if (odt == LC_BF16) k_layernorm_vec<__nv_bfloat16, 8><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)x->data(), wp, wdt, bp, bdt, (__nv_bfloat16*)y->data(), rows, (int)N, (float)eps);
+      else k_layernorm_vec<float, 8><<<blocks, 256, 0, st>>>((const float*)x->data(), wp, wdt, bp, bdt, (float*)y->data(), rows, (int)N, (float)eps);
+    } else if (x->dtype == LC_F64) {
+      k_layernorm_generic<double><<<blocks, 256, 0, st>>>(x->data(), x->dtype, wp, wdt, bp, bdt, y->data(), odt, rows, N, eps);
+    } else {
+      k_layernorm_generic<float><<<blocks, 256, 0, st>>>(x->data(), x->dtype, wp, wdt, bp, bdt, y->data(), odt, rows, N, eps);
+    }
+    LC_LAUNCHED(1);
+    if (x != x0) release(x);
+    if (w && w != w0) release(w);
+    if (b && b != b0) release(b);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_embedding(lc_tensor* out, lc_tensor th, lc_tensor ih) {
+  LC_API_BEGIN
+  LcTensor* t0 = check(th, "embedding table");
+  LcTensor* i0 = check(ih, "embedding ids");
+  LC_CHECK(t0->ndim == 2, "embedding: table must be [V, D]");
+  LC_CHECK(!is_float(i0->dtype), "embedding: ids must be an integer tensor");
+  std::vector<int64_t> sh = i0->dims();
+  sh.push_back(t0->shape[1]);
+  LcTensor* y = alloc(t0->dtype, sh);
+  int64_t n = i0->numel();
+  if (n && t0->shape[1]) {
+    LcTensor* t = contiguous(t0);
+    LcTensor* ids = contiguous(i0);
+    k_gather_rows<<<blocks_for(n * 32, 256), 256, 0, stream()>>>(t->data(), t->shape[0], t->shape[1] * dtype_size(t->dtype),
+                                                                 ids->data(), ids->dtype, y->data(), n, 0, 0);
+    LC_LAUNCHED(1);
+    if (t != t0) release(t);
+    if (ids != i0) release(ids);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_gather_rows(lc_tensor* out, lc_tensor xh, lc_tensor ih) {
+  LC_API_BEGIN
+  LcTensor* x0 = check(xh, "gatherRows x");
+  LcTensor* i0 = check(ih, "gatherRows idx");
+  LC_CHECK(x0->ndim == 3 && i0->ndim == 2 && i0->shape[0] == x0->shape[0], "gatherRows: x [B, L, D] and idx [B, M] expected");
+  int64_t B = x0->shape[0], L = x0->shape[1], D = x0->shape[2], M = i0->shape[1];
+  LcTensor* y = alloc(x0->dtype, {B, M, D});
+  if (B * M && D) {
+    LcTensor* x = contiguous(x0);
+    LcTensor* ids = contiguous(i0);
+    k_gather_rows<<<blocks_for(B * M * 32, 256), 256, 0, stream()>>>(x->data(), L, D * dtype_size(x->dtype), ids->data(), ids->dtype,
+                                                                     y->data(), B * M, M, L);
+    LC_LAUNCHED(1);
+    if (x != x0) release(x);
+    if (ids != i0) release(ids);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_rope(lc_tensor* out, lc_tensor xh, double base) {
+  LC_API_BEGIN
+  LcTensor* x = check(xh, "rope");
+  LC_CHECK(x->ndim >= 2, "rope: x must be [..., L, D]");
+  int64_t L = x->shape[x->ndim - 2], D = x->shape[x->ndim - 1];
+  LC_CHECK(D % 2 == 0, "rope: head dim must be even");
+  int odt = is_float(x->dtype) ? x->dtype : LC_F32;
+  LcTensor* y = alloc(odt, x->dims());
+  int64_t rows = L ? x->numel() / D : 0;
+  if (rows && D) {
+    int cap = 0;
+    const float* cs = rope_table((int)D, base, (int)L, &cap);
+    TV v = tv(x);
+    if (x->dtype != odt) {  // integer input: convert first
+      LcTensor* f = alloc(odt, x->dims());
+      copy_into(x, f);
+      v = tv(f);
+      k_rope<<<blocks_for(rows * (D / 2), 256), 256, 0, stream()>>>(v, cs, rows, L, (int)(D / 2), cap, y->data());
+      release(f);
+    } else {
+      k_rope<<<blocks_for(rows * (D / 2), 256), 256, 0, stream()>>>(v, cs, rows, L, (int)(D / 2), cap, y->data());
+    }
+    LC_LAUNCHED(1);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_sdpa(lc_tensor* out, lc_tensor qh, lc_tensor kh, lc_tensor vh, lc_tensor mh, double scale) {
+  LC_API_BEGIN
+  LcTensor* q = check(qh, "sdpa q");
+  LcTensor* k = check(kh, "sdpa k");
+  LcTensor* v = check(vh, "sdpa v");
+  LcTensor* m = mh ? check(mh, "sdpa mask") : nullptr;
+  LC_CHECK(q->ndim == 4 && k->ndim == 4 && v->ndim == 4, "sdpa: q/k/v must be [B, H, L, D]");
+  int64_t B = q->shape[0], H = q->shape[1], Lq = q->shape[2], D = q->shape[3];
+  int64_t Lk = k->shape[2], Dv = v->shape[3];
+  LC_CHECK(k->shape[0] == B && v->shape[0] == B && k->shape[1] == H && v->shape[1] == H, "sdpa: batch/head mismatch");
+  LC_CHECK(k->shape[3] == D && v->shape[2] == Lk, "sdpa: k/v shapes do not match q");
+  if (m) LC_CHECK(m->dtype == LC_BOOL, "sdpa: the mask must be bool (additive float masks are not part of the contract)");
+  int odt = is_float(q->dtype) ? q->dtype : LC_F32;
+  LcTensor* y = alloc(odt, {B, H, Lq, Dv});
+  if (B * H * Lq && Dv) {
+    TV mv{};
+    if (m) mv = tv_broadcast(m, {B, H, Lq, Lk});
+    if (!lc::attention_try_fast(q, k, v, m, (float)scale, y)) {
+      LC_CHECK(D <= SDPA_MAXD && Dv <= SDPA_MAXD, "sdpa: head dim above 256 is not supported");
+      unsigned blocks = (unsigned)((B * H * Lq + 3) / 4);
+      k_sdpa_generic<<<blocks, 128, 0, stream()>>>(tv(q), tv(k), tv(v), mv, m ? 1 : 0, (float)scale, y->data(), odt, B, H, Lq, Lk,
+                                                  (int)D, (int)Dv);
+      LC_LAUNCHED(1);
+    }
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_geglu(lc_tensor* out, lc_tensor xh) {
+  LC_API_BEGIN
+  LcTensor* x0 = check(xh, "geglu");
+  LC_CHECK(x0->ndim >= 1 && x0->shape[x0->ndim - 1] % 2 == 0, "geglu: last axis must be even");
+  int64_t F = x0->shape[x0->ndim - 1] / 2;
+  std::vector<int64_t> sh = x0->dims();
+  sh.back() = F;
+  int odt = is_float(x0->dtype) ? x0->dtype : LC_F32;
+  LcTensor* y = alloc(odt, sh);
+  int64_t rows = F ? y->numel() / F : 0;
+  if (rows) {
+    LcTensor* x = contiguous(x0);
+    int vn = x->dtype == LC_F32 ? 4 : 8;
+    bool vec = x->dtype == odt && (odt == LC_F32 || is_half(odt)) && F % vn == 0 &&
+               ((((uintptr_t)x->data()) | ((uintptr_t)y->data())) & 15) == 0;
+    cudaStream_t st = stream();
+    if (vec) {
+      unsigned blocks = blocks_for(rows * F / vn, 256);
+      if (odt == LC_F16) k_geglu_vec<__half><<<blocks, 256, 0, st>>>((const __half*)x->data(), (__half*)y->data(), rows, F);
+      else if (odt == LC_BF16) k_geglu_vec<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)x->data(), (__nv_bfloat16*)y->data(), rows, F);
+      else k_geglu_vec<float><<<blocks, 256, 0, st>>>((const float*)x->data(), (float*)y->data(), rows, F);
+    } else if (x->dtype == LC_F64) {
+      k_geglu_generic<double><<<blocks_for(rows * F, 256), 256, 0, st>>>(x->data(), x->dtype, y->data(), odt, rows, F);
+    } else {
+      k_geglu_generic<float><<<blocks_for(rows * F, 256), 256, 0, st>>>(x->data(), x->dtype, y->data(), odt, rows, F);
+    }
+    LC_LAUNCHED(1);
+    if (x != x0) release(x);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_mean_pool(lc_tensor* out, lc_tensor xh, lc_tensor mh) {
+  LC_API_BEGIN
+  LcTensor* x0 = check(xh, "meanPool x");
+  LcTensor* m0 = check(mh, "meanPool mask");
+  LC_CHECK(x0->ndim == 3 && m0->ndim == 2 && m0->shape[0] == x0->shape[0] && m0->shape[1] == x0->shape[1],
+           "meanPool: x [B, L, D] and mask [B, L] expected");
+  int64_t B = x0->shape[0], L = x0->shape[1], D = x0->shape[2];
+  LcTensor* y = alloc(LC_F32, {B, D});
+  if (B * D) {
+    LcTensor* x = contiguous(x0);
+    LcTensor* m = contiguous(m0);
+    k_mean_pool<<<blocks_for(B * D, 256), 256, 0, stream()>>>(x->data(), x->dtype, m->data(), m->dtype, (float*)y->data(), B, L, D);
+    LC_LAUNCHED(1);
+    if (x != x0) release(x);
+    if (m != m0) release(m);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_matmul(lc_tensor* out, lc_tensor ah, lc_tensor bh) {
+  LC_API_BEGIN
+  LcTensor* a0 = check(ah, "matmul a");
+  LcTensor* b0 = check(bh, "matmul b");
+  LC_CHECK(a0->ndim >= 2 && b0->ndim >= 2, "matmul: operands must be at least 2-D");
+  int64_t m = a0->shape[a0->ndim - 2], k = a0->shape[a0->ndim - 1];
+  int64_t k2 = b0->shape[b0->ndim - 2], n = b0->shape[b0->ndim - 1];
+  LC_CHECK(k == k2, "matmul: inner dimensions differ");
+  std::vector<int64_t> ba(a0->shape, a0->shape + a0->ndim - 2), bb(b0->shape, b0->shape + b0->ndim - 2);
+  std::vector<int64_t> bs = broadcast_shapes({ba, bb});
+  LC_CHECK(bs.size() <= 6, "matmul: at most 6 batch dims");
+  std::vector<int64_t> osh = bs;
+  osh.push_back(m);
+  osh.push_back(n);
+  int odt = float_out(a0->dtype, b0->dtype);
+  LcTensor* y = alloc(odt, osh);
+  int64_t batch = 1;
+  for (auto d : bs) batch *= d;
+  if (batch && m && n) {
+    MM p{};
+    p.a = a0->data(); p.adt = a0->dtype;
+    p.b = b0->data(); p.bdt = b0->dtype;
+    p.c = y->data(); p.cdt = odt;
+    p.m = m; p.n = n; p.k = k;
+    p.sam = a0->strides[a0->ndim - 2]; p.sak = a0->strides[a0->ndim - 1];
+    p.sbk = b0->strides[b0->ndim - 2]; p.sbn = b0->strides[b0->ndim - 1];
+    p.nb = (int)bs.size();
+    for (int i = 0; i < p.nb; i++) {
+      p.bshape[i] = bs[i];
+      int ia = i - (p.nb - (a0->ndim - 2)), ib = i - (p.nb - (b0->ndim - 2));
+      p.bsa[i] = (ia >= 0 && a0->shape[ia] != 1) ? a0->strides[ia] : 0;
+      p.bsb[i] = (ib >= 0 && b0->shape[ib] != 1) ? b0->strides[ib] : 0;
+    }
+    // data() already includes the view offset
+    launch_mm(p, batch, odt == LC_F64);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_linear(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh) {
+  LC_API_BEGIN
+  LcTensor* x0 = check(xh, "linear x");
+  LcTensor* w0 = check(wh, "linear w");
+  LcTensor* b0 = bh ? check(bh, "linear bias") : nullptr;
+  LC_CHECK(x0->ndim >= 1 && w0->ndim == 2, "linear: x [..., in] and w [out, in] expected");
+  int64_t K = x0->shape[x0->ndim - 1], N = w0->shape[0];
+  LC_CHECK(w0->shape[1] == K, "linear: x [" + std::to_string(K) + "] vs w " + shape_str(w0->dims()));
+  if (b0) LC_CHECK(b0->numel() == N, "linear: bias size differs from out features");
+  std::vector<int64_t> sh = x0->dims();
+  sh.back() = N;
+  int odt = is_float(x0->dtype) ? x0->dtype : LC_F32;
+  LcTensor* y = alloc(odt, sh);
+  int64_t M = K ? x0->numel() / K : 0;
+  if (M && N) {
+    LcTensor* x = contiguous(x0);
+    LcTensor* w = contiguous(w0);
+    LcTensor* b = b0 ? contiguous(b0) : nullptr;
+    LcTensor* x2 = view_of(x, {M, K}, {K, 1}, x->offset);
+    bool done = false;
+    if (is_half(odt) && x->dtype == odt && w->dtype == odt && (!b || is_float(b->dtype)))
+      done = gemm_linear(x2, w, b, y, GemmEpilogue{});
+    if (!done) {
+      LcTensor* y2 = view_of(y, {M, N}, {N, 1}, 0);
+      linear_simt(x2, w, b, y2);
+      release(y2);
+    }
+    release(x2);
+    if (x != x0) release(x);
+    if (w != w0) release(w);
+    if (b && b != b0) release(b);
+  } else if (M && N == 0) {
+  } else if (N) {
+    // K == 0: y = bias (or zeros)
+    CUDA_OK(cudaMemsetAsync(y->data(), 0, y->numel() * dtype_size(odt), stream()));
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+}  // extern "C"

@@ -1,0 +1,369 @@
+// Axis reductions, softmax, scans and sort
+// (packages/tensor-backend/src/index.ts:200-206 and 300-315).
+//
+// The input is viewed as [outer, n, inner] around the reduced axis. When
+// inner == 1 one warp reduces one row with shuffles; otherwise one thread
+// walks one (outer, inner) column, which keeps loads coalesced across the
+// threads of a warp.
+#include "lc_api.h"
+
+#include <cfloat>
+#include <climits>
+
+enum RedOp : int { R_SUM, R_MAX, R_MIN, R_MEAN, R_ARGMAX, R_ARGMIN };
+
+template <typename CT> __device__ __forceinline__ bool is_nan_v(CT) { return false; }
+template <> __device__ __forceinline__ bool is_nan_v<float>(float v) { return isnan(v); }
+template <> __device__ __forceinline__ bool is_nan_v<double>(double v) { return isnan(v); }
+
+// a "beats" b for max (NaN propagates, ties keep the earlier index)
+template <typename CT>
+__device__ __forceinline__ bool better(int op, CT a, int64_t ia, CT b, int64_t ib) {
+  bool na = is_nan_v(a), nb = is_nan_v(b);
+  if (na || nb) return na && (!nb || ia < ib);
+  bool mx = (op == R_MAX || op == R_ARGMAX);
+  if (a == b) return ia < ib;
+  return mx ? (a > b) : (a < b);
+}
+
+template <typename CT, typename AT>
+__device__ void reduce_store(int op, char* out, int out_dtype, int64_t oi, AT acc, CT best, int64_t bi, int64_t n) {
+  switch (op) {
+    case R_SUM: st_as<AT>(out, out_dtype, oi, acc); break;
+    case R_MEAN: st_as<double>(out, out_dtype, oi, (double)acc / (double)n); break;
+    case R_MAX: case R_MIN: st_as<CT>(out, out_dtype, oi, best); break;
+    default: st_as<int64_t>(out, out_dtype, oi, bi); break;
+  }
+}
+
+// one warp per row (inner == 1)
+template <typename CT, typename AT>
+__global__ void k_reduce_rows(const char* x, int dtype, char* out, int out_dtype, int op, int64_t rows, int64_t n) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    AT acc = 0;
+    CT best = 0;
+    int64_t bi = -1;
+    for (int64_t j = lane; j < n; j += 32) {
+      CT v = ld_as<CT>(x, dtype, r * n + j);
+      if (op == R_SUM || op == R_MEAN) acc += (AT)v;
+      else if (bi < 0 || better<CT>(op, v, j, best, bi)) { best = v; bi = j; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      AT a2 = __shfl_xor_sync(0xffffffffu, acc, o);
+      CT b2 = __shfl_xor_sync(0xffffffffu, best, o);
+      int64_t i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (op == R_SUM || op == R_MEAN) acc += a2;
+      else if (i2 >= 0 && (bi < 0 || better<CT>(op, b2, i2, best, bi))) { best = b2; bi = i2; }
+    }
+    if (lane == 0) reduce_store<CT, AT>(op, out, out_dtype, r, acc, best, bi, n);
+  }
+}
+
+// one thread per (outer, inner) column
+template <typename CT, typename AT>
+__global__ void k_reduce_cols(const char* x, int dtype, char* out, int out_dtype, int op, int64_t outer, int64_t n, int64_t inner) {
+  LC_GRID_STRIDE(c, outer * inner) {
+    int64_t o = c / inner, i = c % inner;
+    int64_t base = o * n * inner + i;
+    AT acc = 0;
+    CT best = 0;
+    int64_t bi = -1;
+    for (int64_t j = 0; j < n; j++) {
+      CT v = ld_as<CT>(x, dtype, base + j * inner);
+      if (op == R_SUM || op == R_MEAN) acc += (AT)v;
+      else if (bi < 0 || better<CT>(op, v, j, best, bi)) { best = v; bi = j; }
+    }
+    reduce_store<CT, AT>(op, out, out_dtype, c, acc, best, bi, n);
+  }
+}
+
+// softmax: f32 math (f64 for f64)
+template <typename CT>
+__global__ void k_softmax_rows(const char* x, int dtype, char* out, int out_dtype, int64_t rows, int64_t n) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    CT m = -INFINITY;
+    for (int64_t j = lane; j < n; j += 32) m = fmax(m, ld_as<CT>(x, dtype, r * n + j));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+    CT s = 0;
+    for (int64_t j = lane; j < n; j += 32) s += exp(ld_as<CT>(x, dtype, r * n + j) - m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    CT inv = (CT)1 / s;
+    for (int64_t j = lane; j < n; j += 32) st_as<CT>(out, out_dtype, r * n + j, exp(ld_as<CT>(x, dtype, r * n + j) - m) * inv);
+  }
+}
+
+template <typename CT>
+__global__ void k_softmax_cols(const char* x, int dtype, char* out, int out_dtype, int64_t outer, int64_t n, int64_t inner) {
+  LC_GRID_STRIDE(c, outer * inner) {
+    int64_t o = c / inner, i = c % inner;
+    int64_t base = o * n * inner + i;
+    CT m = -INFINITY;
+    for (int64_t j = 0; j < n; j++) m = fmax(m, ld_as<CT>(x, dtype, base + j * inner));
+    CT s = 0;
+    for (int64_t j = 0; j < n; j++) s += exp(ld_as<CT>(x, dtype, base + j * inner) - m);
+    CT inv = (CT)1 / s;
+    for (int64_t j = 0; j < n; j++) st_as<CT>(out, out_dtype, base + j * inner, exp(ld_as<CT>(x, dtype, base + j * inner) - m) * inv);
+  }
+}
+
+// inclusive prefix sum, one thread per column, wrapping in the output dtype
+template <typename CT>
+__global__ void k_cumsum(const char* x, int dtype, char* out, int out_dtype, int64_t outer, int64_t n, int64_t inner) {
+  LC_GRID_STRIDE(c, outer * inner) {
+    int64_t o = c / inner, i = c % inner;
+    int64_t base = o * n * inner + i;
+    CT acc = 0;
+    for (int64_t j = 0; j < n; j++) {
+      acc += ld_as<CT>(x, dtype, base + j * inner);
+      if (out_dtype != LC_F32 && out_dtype != LC_F64 && out_dtype != LC_F16 && out_dtype != LC_BF16 && out_dtype != LC_U64 && out_dtype != LC_I64) {
+        // wrap to the output width so later sums continue from the wrapped value
+        st_as<CT>(out, out_dtype, base + j * inner, acc);
+        acc = ld_as<CT>(out, out_dtype, base + j * inner);
+      } else {
+        st_as<CT>(out, out_dtype, base + j * inner, acc);
+        if (out_dtype == LC_F16 || out_dtype == LC_BF16) acc = ld_as<CT>(out, out_dtype, base + j * inner);
+      }
+    }
+  }
+}
+
+// ascending bitonic sort of one row per block in shared memory (NaN last)
+template <typename CT> __device__ __forceinline__ CT sort_pad();
+template <> __device__ __forceinline__ float sort_pad<float>() { return __int_as_float(0x7fc00000); }
+template <> __device__ __forceinline__ double sort_pad<double>() { return __longlong_as_double(0x7ff8000000000000ll); }
+template <> __device__ __forceinline__ int64_t sort_pad<int64_t>() { return LLONG_MAX; }
+template <> __device__ __forceinline__ uint64_t sort_pad<uint64_t>() { return ULLONG_MAX; }
+
+template <typename CT>
+__device__ __forceinline__ bool sort_lt(CT a, CT b) {
+  bool na = is_nan_v(a), nb = is_nan_v(b);
+  if (na || nb) return !na && nb;
+  return a < b;
+}
+
+template <typename CT>
+__global__ void k_sort_rows(const char* x, int dtype, char* out, int64_t n, int P) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  CT* s = (CT*)smem_raw;
+  int64_t r = blockIdx.x;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) s[i] = i < n ? ld_as<CT>(x, dtype, r * n + i) : sort_pad<CT>();
+  __syncthreads();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        int p = i ^ j;
+        if (p > i) {
+          bool up = (i & k) == 0;
+          CT a = s[i], b = s[p];
+          if (up ? sort_lt(b, a) : sort_lt(a, b)) {
+            s[i] = b;
+            s[p] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) st_as<CT>(out, dtype, r * n + i, s[i]);
+}
+
+using namespace lc;
+
+namespace {
+
+struct Axis3 {
+  int64_t outer, n, inner;
+};
+Axis3 split_axis(const LcTensor* x, int a) {
+  Axis3 s{1, x->shape[a], 1};
+  for (int i = 0; i < a; i++) s.outer *= x->shape[i];
+  for (int i = a + 1; i < x->ndim; i++) s.inner *= x->shape[i];
+  return s;
+}
+
+std::vector<int64_t> reduced_shape(const LcTensor* x, int a, bool keep) {
+  std::vector<int64_t> sh;
+  for (int i = 0; i < x->ndim; i++) {
+    if (i == a) {
+      if (keep) sh.push_back(1);
+    } else sh.push_back(x->shape[i]);
+  }
+  return sh;
+}
+
+template <typename CT, typename AT>
+void launch_reduce(LcTensor* c, LcTensor* y, int op, Axis3 s) {
+  cudaStream_t st = stream();
+  if (s.inner == 1) {
+    unsigned blocks = blocks_for(s.outer * 32, 256);
+    k_reduce_rows<CT, AT><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), y->dtype, op, s.outer, s.n);
+  } else {
+    unsigned blocks = blocks_for(s.outer * s.inner, 256);
+    k_reduce_cols<CT, AT><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), y->dtype, op, s.outer, s.n, s.inner);
+  }
+  LC_LAUNCHED(1);
+}
+
+LcTensor* reduce(int op, uint64_t xh, int axis, bool keep, const char* name) {
+  LcTensor* x = check(xh, name);
+  LC_CHECK(x->ndim >= 1, std::string(name) + ": scalar input");
+  int a = norm_axis(axis, x->ndim);
+  Axis3 s = split_axis(x, a);
+  LC_CHECK(s.n > 0 || op == R_SUM, std::string(name) + ": reduction over an empty axis");
+  int odt;
+  switch (op) {
+    case R_SUM: odt = x->dtype == LC_BOOL ? LC_I32 : x->dtype; break;
+    case R_MEAN: odt = x->dtype == LC_F64 ? LC_F64 : LC_F32; break;
+    case R_ARGMAX: case R_ARGMIN: odt = LC_I32; break;
+    default: odt = x->dtype;
+  }
+  LcTensor* y = alloc(odt, reduced_shape(x, a, keep));
+  if (y->numel() == 0) return y;
+  LcTensor* c = contiguous(x);
+  int d = x->dtype;
+  if (op == R_MEAN) {
+    if (d == LC_U64) launch_reduce<uint64_t, double>(c, y, op, s);
+    else if (is_float(d)) launch_reduce<double, double>(c, y, op, s);
+    else launch_reduce<int64_t, double>(c, y, op, s);
+  } else if (d == LC_F64) launch_reduce<double, double>(c, y, op, s);
+  else if (is_float(d)) launch_reduce<float, float>(c, y, op, s);
+  else if (d == LC_U64) launch_reduce<uint64_t, uint64_t>(c, y, op, s);
+  else launch_reduce<int64_t, int64_t>(c, y, op, s);
+  if (c != x) release(c);
+  return y;
+}
+
+}  // namespace
+
+#define RED_ENTRY(fn, op, nm)                                                      \
+  int fn(lc_tensor* out, lc_tensor x, int axis, int keep) {                        \
+    LC_API_BEGIN *out = handle(reduce(op, x, axis, keep != 0, nm));                \
+    LC_API_END                                                                     \
+  }
+
+extern "C" {
+RED_ENTRY(lc_sum, R_SUM, "sum")
+RED_ENTRY(lc_max, R_MAX, "max")
+RED_ENTRY(lc_min, R_MIN, "min")
+RED_ENTRY(lc_mean, R_MEAN, "mean")
+RED_ENTRY(lc_argmax, R_ARGMAX, "argmax")
+RED_ENTRY(lc_argmin, R_ARGMIN, "argmin")
+
+int lc_softmax(lc_tensor* out, lc_tensor xh, int axis) {
+  LC_API_BEGIN
+  LcTensor* x = check(xh, "softmax");
+  int a = norm_axis(axis, x->ndim);
+  Axis3 s = split_axis(x, a);
+  int odt = is_float(x->dtype) ? x->dtype : LC_F32;
+  LcTensor* y = alloc(odt, x->dims());
+  if (y->numel()) {
+    LcTensor* c = contiguous(x);
+    cudaStream_t st = stream();
+    bool dbl = x->dtype == LC_F64;
+    if (s.inner == 1) {
+      unsigned blocks = blocks_for(s.outer * 32, 256);
+      if (dbl) k_softmax_rows<double><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), odt, s.outer, s.n);
+      else k_softmax_rows<float><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), odt, s.outer, s.n);
+    } else {
+      unsigned blocks = blocks_for(s.outer * s.inner, 256);
+      if (dbl) k_softmax_cols<double><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), odt, s.outer, s.n, s.inner);
+      else k_softmax_cols<float><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), odt, s.outer, s.n, s.inner);
+    }
+    LC_LAUNCHED(1);
+    if (c != x) release(c);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_cumsum(lc_tensor* out, lc_tensor xh, int axis) {
+  LC_API_BEGIN
+  LcTensor* x = check(xh, "cumsum");
+  int a = norm_axis(axis, x->ndim);
+  Axis3 s = split_axis(x, a);
+  int odt = x->dtype == LC_BOOL ? LC_I32 : x->dtype;
+  LcTensor* y = alloc(odt, x->dims());
+  if (y->numel()) {
+    LcTensor* c = contiguous(x);
+    unsigned blocks = blocks_for(s.outer * s.inner, 256);
+    cudaStream_t st = stream();
+    int d = x->dtype;
+    if (d == LC_F64) k_cumsum<double><<<blocks, 256, 0, st>>>(c->data(), d, y->data(), odt, s.outer, s.n, s.inner);
+    else if (is_float(d)) k_cumsum<float><<<blocks, 256, 0, st>>>(c->data(), d, y->data(), odt, s.outer, s.n, s.inner);
+    else if (d == LC_U64) k_cumsum<uint64_t><<<blocks, 256, 0, st>>>(c->data(), d, y->data(), odt, s.outer, s.n, s.inner);
+    else k_cumsum<int64_t><<<blocks, 256, 0, st>>>(c->data(), d, y->data(), odt, s.outer, s.n, s.inner);
+    LC_LAUNCHED(1);
+    if (c != x) release(c);
+  }
+  *out = handle(y);
+  LC_API_END
+}
+
+int lc_sort(lc_tensor* out, lc_tensor xh, int axis) {
+  LC_API_BEGIN
+  LcTensor* x = check(xh, "sort");
+  int r = x->ndim;
+  int a = norm_axis(axis, r);
+  // move the axis last (a strided view), sort dense rows, then permute back
+  std::vector<int64_t> sh, st;
+  std::vector<int> perm;
+  for (int i = 0; i < r; i++)
+    if (i != a) perm.push_back(i);
+  perm.push_back(a);
+  for (int p : perm) {
+    sh.push_back(x->shape[p]);
+    st.push_back(x->strides[p]);
+  }
+  LcTensor* moved = view_of(x, sh, st, x->offset);
+  LcTensor* rows = alloc(x->dtype, sh);
+  copy_into(moved, rows);
+  release(moved);
+  int64_t n = x->shape[a], nrows = n ? x->numel() / n : 0;
+  if (nrows && n > 1) {
+    int P = 1;
+    while (P < n) P <<= 1;
+    int d = x->dtype;
+    size_t esz = (d == LC_F64 || d == LC_U64 || d == LC_I64 || !is_float(d)) ? 8 : 4;
+    size_t smem = (size_t)P * esz;
+    LC_CHECK(smem <= 96 * 1024, "sort: axis of length " + std::to_string(n) + " is longer than the supported 12288 (8-byte) / 24576 (4-byte) elements");
+    cudaStream_t s = stream();
+    int threads = P >= 1024 ? 1024 : (P < 32 ? 32 : P);
+    if (d == LC_F64) {
+      cudaFuncSetAttribute(k_sort_rows<double>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      k_sort_rows<double><<<(unsigned)nrows, threads, smem, s>>>(rows->data(), d, rows->data(), n, P);
+    } else if (is_float(d)) {
+      cudaFuncSetAttribute(k_sort_rows<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      k_sort_rows<float><<<(unsigned)nrows, threads, smem, s>>>(rows->data(), d, rows->data(), n, P);
+    } else if (d == LC_U64) {
+      cudaFuncSetAttribute(k_sort_rows<uint64_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      k_sort_rows<uint64_t><<<(unsigned)nrows, threads, smem, s>>>(rows->data(), d, rows->data(), n, P);
+    } else {
+      cudaFuncSetAttribute(k_sort_rows<int64_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      k_sort_rows<int64_t><<<(unsigned)nrows, threads, smem, s>>>(rows->data(), d, rows->data(), n, P);
+    }
+    LC_LAUNCHED(1);
+  }
+  // inverse permutation back to the input layout
+  std::vector<int64_t> bsh(r), bst(r);
+  for (int i = 0; i < r; i++) {
+    bsh[perm[i]] = rows->shape[i];
+    bst[perm[i]] = rows->strides[i];
+  }
+  LcTensor* back = view_of(rows, bsh, bst, 0);
+  LcTensor* y = alloc(x->dtype, x->dims());
+  copy_into(back, y);
+  release(back);
+  release(rows);
+  *out = handle(y);
+  LC_API_END
+}
+}  // extern "C"

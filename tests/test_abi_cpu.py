@@ -1,0 +1,59 @@
+"""C-ABI checks that need no GPU: the library loads and exports every
+function include/*.h declares, and the host helpers mirror host.ts."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from laya_js_b200 import _lib
+from laya_js_b200.host import HostQuantized, host, pack_quantized, to_f32, unpack_quantized, validate_quantized
+from oracle import ops as O
+
+
+def test_library_exports_every_declared_symbol():
+    decls = _lib.header_declarations()
+    assert len(decls) >= 60
+    lib = ctypes.CDLL(str(_lib.lib_path()))
+    missing = [n for n in decls if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_signatures_resolve():
+    lib = _lib.load()
+    for name in _lib.header_declarations():
+        assert getattr(lib, name).argtypes is not None or name in ("lc_destroy", "lc_last_error", "lc_flush")
+
+
+def test_lc_supports_without_device():
+    lib = _lib.load()
+    out = ctypes.c_int()
+    assert lib.lc_supports(0, ctypes.byref(out)) == 0 and out.value == 1
+    assert lib.lc_supports(99, ctypes.byref(out)) == 0 and out.value == 0
+
+
+def test_calls_before_init_fail_with_message():
+    lib = _lib.load()
+    out = ctypes.c_uint64()
+    rc = lib.lc_exp(ctypes.byref(out), ctypes.c_uint64(0))
+    assert rc != 0
+    assert b"lc_init" in lib.lc_last_error() or b"null" in lib.lc_last_error()
+
+
+def test_pack_unpack_match_oracle():
+    rng = np.random.default_rng(1)
+    for bits, mode in ((8, "symmetric"), (4, "affine"), (4, "symmetric"), (8, "affine")):
+        lo, hi = ((-128, 127) if bits == 8 else (-8, 7)) if mode == "symmetric" else (0, (1 << bits) - 1)
+        q = rng.integers(lo, hi + 1, size=(6, 64))
+        packed = pack_quantized(q, bits)
+        assert np.array_equal(packed, O.pack_quantized(q, bits))
+        h = HostQuantized((6, 64), bits, 32, mode, packed, host("f32", (6, 2)), host("f32", (6, 2)) if mode == "affine" else None)
+        validate_quantized(h)
+        assert np.array_equal(unpack_quantized(h).reshape(6, 64), q)
+
+
+def test_bf16_host_rounding():
+    x = np.array([1.0, 1.00390625, -3.3, np.nan], np.float32)
+    h = host("bf16", (4,), x)
+    back = to_f32(h)
+    assert back[0] == 1.0 and back[2] == np.float32(-3.296875) and np.isnan(back[3])
