@@ -28,7 +28,7 @@ _TYPES = {
     "uint64_t": C.c_uint64, "uint64_t*": C.POINTER(C.c_uint64), "lc_tensor": C.c_uint64,
     "lc_tensor*": C.POINTER(C.c_uint64), "constlc_tensor*": C.POINTER(C.c_uint64), "void": None,
     "constchar*": C.c_char_p, "float*": C.POINTER(C.c_float), "constfloat*": C.POINTER(C.c_float),
-    "int32_t*": C.POINTER(C.c_int32),
+    "int32_t*": C.POINTER(C.c_int32), "constlc_encoder_config*": C.c_void_p, "double*": C.POINTER(C.c_double),
 }
 
 

@@ -6,6 +6,7 @@
 // flush/destroy and reshape/transpose/slice/split/concat/cast.
 #include "lc_common.cuh"
 #include "lc_api.h"
+#include "lc_gemm.h"
 
 #include <algorithm>
 #include <mutex>
@@ -430,6 +431,8 @@ int lc_flush(void) {
   LC_API_BEGIN
   ensure_init();
   CUDA_OK(cudaStreamSynchronize(stream()));
+  std::string err = take_device_errors();
+  LC_CHECK(err.empty(), err);
   LC_API_END
 }
 

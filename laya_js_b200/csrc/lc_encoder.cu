@@ -1,0 +1,634 @@
+// Fused ModernBERT encoder over packed variable-length sequences.
+//
+// Computes ModernBert.encode (packages/modernbert/src/index.ts:407-429) for
+// every valid token, layer by layer as ModernBert.layer (index.ts:342-357)
+// does, with these fusions:
+//   embedding + LayerNorm                          -> k_embed_ln
+//   Wqkv linear + reshape/transpose/split + RoPE   -> GEMM, EPI_ROPE_QKV (q/k rotated at each token's position)
+//   masks + sdpa + transpose/reshape               -> attention_varlen (window rule in-kernel)
+//   Wo linear + residual add                       -> GEMM, EPI_RESIDUAL (in place on x)
+//   Wi linear + geglu                              -> GEMM, EPI_GEGLU (Wi rows interleaved in 32-row blocks at load)
+//   mlp.Wo linear + residual add                   -> GEMM, EPI_RESIDUAL (in place on x)
+// plus the CLS classifier head + softmax (packages/laya/src/model.ts:228 pattern).
+// Quantized Linear weights (4/8-bit, laya-js packing) stay packed in HBM and
+// are dequantised per GEMM into one reusable f16/bf16 scratch matrix.
+#include "lc_api.h"
+#include "lc_gemm.h"
+#include "lc_quant.cuh"
+#include "laya_cuda_encoder.h"
+
+#include <algorithm>
+#include <memory>
+#include <unordered_set>
+
+using namespace lc;
+
+namespace lc {
+void layernorm_raw(const void* x, const float* w, void* y, int64_t rows, int N, float eps, int dtype, cudaStream_t st);
+void copy_into(const LcTensor* src, LcTensor* dst_dense);
+std::vector<int4> attention_tiles(const int32_t* cu, int nseq);
+void attention_varlen(const void* qkv, void* out, const int4* tiles_dev, int ntiles, int64_t T, int H, int half_window, float scale,
+                      int dtype, cudaStream_t st);
+void dequant_into(const LcTensor* w, const LcTensor* s, const LcTensor* b, int bits, int g, int mode, LcTensor* out);
+}  // namespace lc
+
+namespace {
+
+__global__ void k_positions(const int32_t* __restrict__ cu, int nseq, int32_t* __restrict__ pos) {
+  for (int s = blockIdx.x; s < nseq; s += gridDim.x) {
+    int a = cu[s], b = cu[s + 1];
+    for (int t = a + threadIdx.x; t < b; t += blockDim.x) pos[t] = t - a;
+  }
+}
+
+// x[t] = LayerNorm(table[ids[t]]) * w, one warp per token, H <= 2048, H % 8 == 0
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) k_embed_ln(const T* __restrict__ table, int64_t V, const int32_t* __restrict__ ids,
+                                                  const float* __restrict__ w, T* __restrict__ y, int64_t rows, int H, float eps) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int nv = H / 8;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    int64_t id = ids[r];
+    if (id < 0 || id >= V) id = 0;  // out-of-range ids read row 0 (never fault)
+    const T* src = table + id * H;
+    float v[MAXV][8];
+    float s = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      int c = t * 32 + lane;
+      if (c < nv) {
+        uint4 raw = *(const uint4*)(src + c * 8);
+        const T* e = (const T*)&raw;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          float f = std::is_same<T, __half>::value ? __half2float(((const __half*)e)[j]) : __bfloat162float(((const __nv_bfloat16*)e)[j]);
+          v[t][j] = f;
+          s += f;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    float mu = s / H, q = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++)
+      if (t * 32 + lane < nv)
+#pragma unroll
+        for (int j = 0; j < 8; j++) q += (v[t][j] - mu) * (v[t][j] - mu);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    float rs = rsqrtf(q / H + eps);
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      int c = t * 32 + lane;
+      if (c < nv) {
+        uint4 raw;
+        T* e = (T*)&raw;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          float o = (v[t][j] - mu) * rs * __ldg(w + c * 8 + j);
+          if constexpr (std::is_same<T, __half>::value) e[j] = __float2half_rn(o);
+          else e[j] = __float2bfloat16_rn(o);
+        }
+        *(uint4*)(y + r * H + c * 8) = raw;
+      }
+    }
+  }
+}
+
+// probs[s] = softmax(hidden[cu[s]] · Wᵀ + b), one block per sequence, f32 accumulation
+template <typename T>
+__global__ void k_cls_head(const T* __restrict__ hidden, int H, const int32_t* __restrict__ cu, int nseq, const char* w, int wdt,
+                           const char* b, int bdt, int C, float* __restrict__ probs) {
+  extern __shared__ float logits[];
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int s = blockIdx.x; s < nseq; s += gridDim.x) {
+    const T* row = hidden + (int64_t)cu[s] * H;
+    for (int c = warp; c < C; c += nw) {
+      float acc = 0.f;
+      for (int k = lane; k < H; k += 32) acc += ld_as<float>((const char*)row, std::is_same<T, __half>::value ? LC_F16 : LC_BF16, k) * ld_as<float>(w, wdt, (int64_t)c * H + k);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) logits[c] = acc + (b ? ld_as<float>(b, bdt, c) : 0.f);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float m = -INFINITY;
+      for (int c = 0; c < C; c++) m = fmaxf(m, logits[c]);
+      float z = 0.f;
+      for (int c = 0; c < C; c++) z += expf(logits[c] - m);
+      for (int c = 0; c < C; c++) probs[(int64_t)s * C + c] = expf(logits[c] - m) / z;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void k_permute_rows(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t rowbytes, const int32_t* __restrict__ perm,
+                               int64_t rows) {
+  LC_GRID_STRIDE(i, rows * rowbytes) {
+    int64_t r = i / rowbytes, c = i % rowbytes;
+    dst[i] = src[(int64_t)perm[r] * rowbytes + c];
+  }
+}
+
+struct Mat {
+  LcTensor* dense = nullptr;  // [N, K] in the compute dtype
+  LcTensor* q = nullptr;      // packed [N, K*bits/8]
+  LcTensor* s = nullptr;
+  LcTensor* b = nullptr;
+  int64_t N = 0, K = 0;
+};
+
+struct Layer {
+  int kind = 0;
+  LcTensor* attn_norm = nullptr;
+  LcTensor* mlp_norm = nullptr;
+  Mat Wqkv, Wo, Wi, WoMlp;
+};
+
+struct Encoder {
+  lc_encoder_config cfg{};
+  std::vector<Layer> layers;
+  LcTensor* tok = nullptr;
+  LcTensor* emb_norm = nullptr;
+  LcTensor* final_norm = nullptr;
+  std::vector<LcTensor*> owned;  // references released by lc_encoder_free
+  // workspace (grow-only)
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  LcTensor* deq = nullptr;  // dequant scratch for quantized weights
+  // host staging (pinned) for cu_seqlens + tiles
+  void* stage = nullptr;
+  size_t stage_bytes = 0;
+  cudaEvent_t stage_ev = nullptr;
+  void* ids_stage = nullptr;
+  size_t ids_stage_bytes = 0;
+  void* probs_stage = nullptr;
+  size_t probs_stage_bytes = 0;
+  // tracing: CUDA events around each kernel class (0 GEMM, 1 attention, 2 LN/embedding, 3 head/other)
+  bool prof = false;
+  std::vector<cudaEvent_t> ev_pool;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pending;
+  double prof_ms[4] = {0, 0, 0, 0};
+  int64_t prof_n[4] = {0, 0, 0, 0};
+};
+
+cudaEvent_t pooled_event(Encoder* e) {
+  if (!e->ev_pool.empty()) {
+    cudaEvent_t ev = e->ev_pool.back();
+    e->ev_pool.pop_back();
+    return ev;
+  }
+  cudaEvent_t ev;
+  CUDA_OK(cudaEventCreate(&ev));
+  return ev;
+}
+
+// Records an event pair around the kernels issued in its lifetime when profiling is on.
+struct Prof {
+  Encoder* e;
+  int cls;
+  cudaEvent_t a = nullptr;
+  Prof(Encoder* e_, int c) : e(e_), cls(c) {
+    if (e->prof) {
+      a = pooled_event(e);
+      CUDA_OK(cudaEventRecord(a, stream()));
+    }
+  }
+  ~Prof() {
+    if (a) {
+      cudaEvent_t b = pooled_event(e);
+      cudaEventRecord(b, stream());
+      e->pending.push_back({cls, {a, b}});
+    }
+  }
+};
+
+std::unordered_set<Encoder*>& encoders() {
+  static std::unordered_set<Encoder*> s;
+  return s;
+}
+
+Encoder* check_enc(uint64_t h) {
+  Encoder* e = reinterpret_cast<Encoder*>(h);
+  LC_CHECK(h && encoders().count(e), "encoder: invalid or freed encoder handle");
+  return e;
+}
+
+LcTensor* keep(Encoder* e, LcTensor* t) {
+  LcTensor* v = view_of(t, t->dims(), std::vector<int64_t>(t->strides, t->strides + t->ndim), t->offset);
+  e->owned.push_back(v);
+  return v;
+}
+
+// A LayerNorm weight as an owned f32 copy (the norm kernels read f32 vectors).
+LcTensor* keep_f32(Encoder* e, LcTensor* t) {
+  LcTensor* f = alloc(LC_F32, {t->numel()});
+  copy_into(t, f);
+  e->owned.push_back(f);
+  return f;
+}
+
+void need_shape(const LcTensor* t, std::vector<int64_t> want, const std::string& what) {
+  LC_CHECK(t->dims() == want, "encoder: " + what + " has shape " + shape_str(t->dims()) + ", want " + shape_str(want));
+  LC_CHECK(t->contiguous(), "encoder: " + what + " must be dense");
+}
+
+// GeGLU interleave: output rows [v 32 | g 32] per 32-row block of the two halves.
+std::vector<int32_t> geglu_perm(int64_t I) {
+  std::vector<int32_t> p;
+  for (int64_t b = 0; b < I / 32; b++) {
+    for (int j = 0; j < 32; j++) p.push_back((int32_t)(b * 32 + j));
+    for (int j = 0; j < 32; j++) p.push_back((int32_t)(I + b * 32 + j));
+  }
+  return p;
+}
+
+LcTensor* permuted_rows(Encoder* e, const LcTensor* src, const std::vector<int32_t>& perm) {
+  LcTensor* dst = alloc(src->dtype, src->dims());
+  int32_t* d = (int32_t*)dmalloc(perm.size() * 4);
+  CUDA_OK(cudaMemcpyAsync(d, perm.data(), perm.size() * 4, cudaMemcpyHostToDevice, stream()));
+  int64_t rowbytes = src->numel() / src->shape[0] * dtype_size(src->dtype);
+  k_permute_rows<<<blocks_for(src->shape[0] * rowbytes, 256), 256, 0, stream()>>>((const uint8_t*)src->data(), (uint8_t*)dst->data(), rowbytes,
+                                                                                  d, src->shape[0]);
+  LC_LAUNCHED(1);
+  dfree(d);
+  e->owned.push_back(dst);
+  return dst;
+}
+
+Mat take_mat(Encoder* e, const lc_tensor* w, int& i, int64_t N, int64_t K, const std::string& what, bool geglu) {
+  Mat m;
+  m.N = N;
+  m.K = K;
+  const lc_encoder_config& c = e->cfg;
+  if (c.quant_bits == 0) {
+    LcTensor* t = check(w[i++], what.c_str());
+    need_shape(t, {N, K}, what);
+    LC_CHECK(t->dtype == c.dtype, "encoder: " + what + " must be stored in the encoder dtype");
+    m.dense = geglu ? permuted_rows(e, t, geglu_perm(N / 2)) : keep(e, t);
+  } else {
+    LcTensor* q = check(w[i++], what.c_str());
+    LcTensor* s = check(w[i++], what.c_str());
+    LcTensor* b = w[i] ? check(w[i], what.c_str()) : nullptr;
+    i++;
+    int64_t G = (K + c.quant_group - 1) / c.quant_group;
+    need_shape(q, {N, K * c.quant_bits / 8}, what + " (packed)");
+    need_shape(s, {N, G}, what + " scales");
+    if (c.quant_mode == 1) {
+      LC_CHECK(b, "encoder: " + what + ": affine weights need biases");
+      need_shape(b, {N, G}, what + " biases");
+    }
+    if (geglu) {
+      auto p = geglu_perm(N / 2);
+      m.q = permuted_rows(e, q, p);
+      m.s = permuted_rows(e, s, p);
+      m.b = b ? permuted_rows(e, b, p) : nullptr;
+    } else {
+      m.q = keep(e, q);
+      m.s = keep(e, s);
+      m.b = b ? keep(e, b) : nullptr;
+    }
+  }
+  return m;
+}
+
+// y = x · Wᵀ with the given epilogue (dense weight or packed weight dequantised into the scratch)
+void run_gemm(Encoder* e, const Mat& m, const void* x, int64_t M, void* y, int64_t ldy, const GemmEpilogue& ep, int64_t n_out) {
+  const void* w;
+  if (m.dense) {
+    w = m.dense->data();
+  } else {
+    if (!e->deq || e->deq->numel() < m.N * m.K) {
+      if (e->deq) release(e->deq);
+      int64_t biggest = 0;
+      for (auto& l : e->layers)
+        for (const Mat* mm : {&l.Wqkv, &l.Wo, &l.Wi, &l.WoMlp}) biggest = std::max(biggest, mm->N * mm->K);
+      e->deq = alloc(e->cfg.dtype, {biggest});
+    }
+    LcTensor* view = view_of(e->deq, {m.N, m.K}, {m.K, 1}, 0);
+    Prof pd(e, 3);
+    dequant_into(m.q, m.s, m.b, e->cfg.quant_bits, e->cfg.quant_group, e->cfg.quant_mode, view);
+    release(view);
+    w = e->deq->data();
+  }
+  Prof p(e, 0);
+  bool ok = gemm_raw(x, M, m.K, w, n_out, nullptr, 0, y, ldy, e->cfg.dtype, ep, stream());
+  LC_CHECK(ok, "encoder: the tcgen05 GEMM rejected a projection shape");
+}
+
+void grow_ws(Encoder* e, size_t bytes) {
+  if (e->ws_bytes >= bytes) return;
+  if (e->ws) dfree(e->ws);
+  e->ws = dmalloc(bytes);
+  e->ws_bytes = bytes;
+}
+
+void* grow_pinned(void*& p, size_t& have, size_t want) {
+  if (have >= want) return p;
+  if (p) CUDA_OK(cudaFreeHost(p));
+  CUDA_OK(cudaHostAlloc(&p, want, cudaHostAllocDefault));
+  have = want;
+  return p;
+}
+
+// The forward on device ids (i32 [T]) and host cu_seqlens.
+void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, LcTensor* hidden_out, const LcTensor* head_w,
+             const LcTensor* head_b, float* probs_dev) {
+  const lc_encoder_config& c = e->cfg;
+  LC_CHECK(nseq > 0 && cu[0] == 0, "encoder: cu_seqlens must start at 0");
+  int64_t T = cu[nseq];
+  int maxlen = 0;
+  for (int s = 0; s < nseq; s++) {
+    LC_CHECK(cu[s + 1] >= cu[s], "encoder: cu_seqlens must be non-decreasing");
+    maxlen = std::max(maxlen, cu[s + 1] - cu[s]);
+  }
+  LC_CHECK(T > 0, "encoder: empty batch");
+  LC_CHECK(maxlen <= 8192, "encoder: sequences longer than 8192 tokens are not supported");
+  const int H = c.hidden_size, I = c.intermediate_size;
+  const int64_t esz = 2;
+  cudaStream_t st = stream();
+  // host-built metadata: cu_seqlens + attention tiles, one pinned staging buffer
+  std::vector<int4> tiles = attention_tiles(cu, nseq);
+  size_t cu_bytes = ((size_t)(nseq + 1) * 4 + 15) & ~(size_t)15;
+  size_t meta = cu_bytes + tiles.size() * sizeof(int4);
+  if (e->stage_ev) CUDA_OK(cudaEventSynchronize(e->stage_ev));
+  grow_pinned(e->stage, e->stage_bytes, meta);
+  memcpy(e->stage, cu, (size_t)(nseq + 1) * 4);
+  memcpy((char*)e->stage + cu_bytes, tiles.data(), tiles.size() * sizeof(int4));
+  // workspace: x | h | qkv | pos | meta
+  size_t off_x = 0, off_h = off_x + T * H * esz, off_qkv = off_h + T * H * esz, off_pos = off_qkv + T * 3 * H * esz;
+  size_t off_meta = (off_pos + T * 4 + 255) & ~(size_t)255;
+  grow_ws(e, off_meta + meta);
+  char* ws = (char*)e->ws;
+  void* x = ws + off_x;
+  void* h = ws + off_h;
+  void* qkv = ws + off_qkv;
+  int32_t* pos = (int32_t*)(ws + off_pos);
+  int32_t* cu_dev = (int32_t*)(ws + off_meta);
+  int4* tiles_dev = (int4*)(ws + off_meta + cu_bytes);
+  CUDA_OK(cudaMemcpyAsync(ws + off_meta, e->stage, meta, cudaMemcpyHostToDevice, st));
+  if (!e->stage_ev) CUDA_OK(cudaEventCreateWithFlags(&e->stage_ev, cudaEventDisableTiming));
+  CUDA_OK(cudaEventRecord(e->stage_ev, st));
+  k_positions<<<std::min(nseq, 4096), 256, 0, st>>>(cu_dev, nseq, pos);
+  LC_LAUNCHED(1);
+
+  int cap_g = 0, cap_l = 0;
+  const float* rope_g = rope_table(64, c.rope_theta_global, std::max(maxlen, 1), &cap_g);
+  const float* rope_l = rope_table(64, c.rope_theta_local, std::max(maxlen, 1), &cap_l);
+
+  // embeddings
+  Prof* pe = new Prof(e, 2);
+  unsigned lnb = blocks_for(T * 32, 256);
+  const int per = (H / 8 + 31) / 32;
+#define LC_EMB(TT, MV)                                                                                                            \
+  k_embed_ln<TT, MV><<<lnb, 256, 0, st>>>((const TT*)e->tok->data(), e->tok->shape[0], ids_dev, (const float*)e->emb_norm->data(), \
+                                          (TT*)x, T, H, (float)c.norm_eps)
+  if (c.dtype == LC_F16) {
+    if (per <= 1) LC_EMB(__half, 1); else if (per <= 2) LC_EMB(__half, 2); else if (per <= 3) LC_EMB(__half, 3);
+    else if (per <= 4) LC_EMB(__half, 4); else LC_EMB(__half, 8);
+  } else {
+    if (per <= 1) LC_EMB(__nv_bfloat16, 1); else if (per <= 2) LC_EMB(__nv_bfloat16, 2); else if (per <= 3) LC_EMB(__nv_bfloat16, 3);
+    else if (per <= 4) LC_EMB(__nv_bfloat16, 4); else LC_EMB(__nv_bfloat16, 8);
+  }
+#undef LC_EMB
+  LC_LAUNCHED(1);
+  delete pe;
+
+  const float scale = 1.0f / sqrtf(64.0f);
+  for (size_t li = 0; li < e->layers.size(); li++) {
+    const Layer& L = e->layers[li];
+    const void* hin = x;
+    if (L.attn_norm) {
+      Prof p(e, 2);
+      layernorm_raw(x, (const float*)L.attn_norm->data(), h, T, H, (float)c.norm_eps, c.dtype, st);
+      hin = h;
+    }
+    GemmEpilogue eq;
+    eq.kind = EPI_ROPE_QKV;
+    eq.pos = pos;
+    eq.rope_cs = L.kind == 0 ? rope_g : rope_l;
+    eq.rope_cap = L.kind == 0 ? cap_g : cap_l;
+    eq.rope_cols = 2 * H;
+    run_gemm(e, L.Wqkv, hin, T, qkv, 3 * H, eq, 3 * H);
+    // attention -> h (h is free again once the Wqkv GEMM has read it)
+    {
+      Prof p(e, 1);
+      attention_varlen(qkv, h, tiles_dev, (int)tiles.size(), T, H, L.kind == 0 ? -1 : c.local_attention / 2, scale, c.dtype, st);
+    }
+    GemmEpilogue er;
+    er.kind = EPI_RESIDUAL;
+    er.resid = x;
+    er.ldr = H;
+    run_gemm(e, L.Wo, h, T, x, H, er, H);
+    {
+      Prof p(e, 2);
+      layernorm_raw(x, (const float*)L.mlp_norm->data(), h, T, H, (float)c.norm_eps, c.dtype, st);
+    }
+    GemmEpilogue eg;
+    eg.kind = EPI_GEGLU;
+    run_gemm(e, L.Wi, h, T, qkv, I, eg, I);
+    run_gemm(e, L.WoMlp, qkv, T, x, H, er, H);
+  }
+  void* fin = hidden_out ? hidden_out->data() : h;
+  {
+    Prof pf(e, 2);
+    layernorm_raw(x, (const float*)e->final_norm->data(), fin, T, H, (float)c.norm_eps, c.dtype, st);
+  }
+  if (head_w && probs_dev) {
+    Prof ph(e, 3);
+    int C = (int)head_w->shape[0];
+    size_t smem = C * sizeof(float);
+    unsigned blocks = (unsigned)std::min(nseq, 65535);
+    if (c.dtype == LC_F16)
+      k_cls_head<__half><<<blocks, 128, smem, st>>>((const __half*)fin, H, cu_dev, nseq, head_w->data(), head_w->dtype,
+                                                    head_b ? head_b->data() : nullptr, head_b ? head_b->dtype : 0, C, probs_dev);
+    else
+      k_cls_head<__nv_bfloat16><<<blocks, 128, smem, st>>>((const __nv_bfloat16*)fin, H, cu_dev, nseq, head_w->data(), head_w->dtype,
+                                                           head_b ? head_b->data() : nullptr, head_b ? head_b->dtype : 0, C, probs_dev);
+    LC_LAUNCHED(1);
+  }
+}
+
+void check_head(const Encoder* e, const LcTensor* w, const LcTensor* b) {
+  LC_CHECK(w->ndim == 2 && w->shape[1] == e->cfg.hidden_size && w->contiguous() && is_float(w->dtype) && w->dtype != LC_F64,
+           "encoder: head_w must be a dense float [C, H] matrix");
+  LC_CHECK(w->shape[0] >= 1 && w->shape[0] <= 4096, "encoder: 1..4096 classes");
+  if (b) LC_CHECK(b->numel() == w->shape[0] && b->contiguous() && is_float(b->dtype) && b->dtype != LC_F64, "encoder: head_b must be [C]");
+}
+
+}  // namespace
+
+extern "C" {
+
+int lc_encoder_create(uint64_t* out, const lc_encoder_config* cfg, const int32_t* kinds, const lc_tensor* w, int nweights) {
+  LC_API_BEGIN
+  const lc_encoder_config& c = *cfg;
+  LC_CHECK(c.dtype == LC_F16 || c.dtype == LC_BF16, "encoder: dtype must be f16 or bf16");
+  LC_CHECK(c.num_heads > 0 && c.hidden_size == 64 * c.num_heads, "encoder: the fused path needs head dim 64");
+  LC_CHECK(c.hidden_size % 64 == 0 && c.hidden_size <= 2048, "encoder: hidden size must be a multiple of 64, at most 2048");
+  LC_CHECK(c.intermediate_size % 32 == 0 && c.intermediate_size % 8 == 0, "encoder: intermediate size must be a multiple of 32");
+  LC_CHECK(c.num_layers >= 1 && c.vocab_size >= 1, "encoder: bad layer count / vocab");
+  LC_CHECK(c.quant_bits == 0 || c.quant_bits == 4 || c.quant_bits == 8, "encoder: quant_bits must be 0, 4 or 8");
+  int per = c.quant_bits ? 3 : 1;
+  int want = 2 + c.num_layers * (2 + 4 * per) + 1;
+  LC_CHECK(nweights == want, "encoder: expected " + std::to_string(want) + " weight handles, got " + std::to_string(nweights));
+  auto e = std::make_unique<Encoder>();
+  e->cfg = c;
+  const int64_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size;
+  int i = 0;
+  try {
+    LcTensor* tok = check(w[i++], "encoder tok_embeddings");
+    need_shape(tok, {V, H}, "tok_embeddings");
+    LC_CHECK(tok->dtype == c.dtype, "encoder: tok_embeddings must be stored in the encoder dtype");
+    e->tok = keep(e.get(), tok);
+    LcTensor* en = check(w[i++], "encoder embeddings.norm");
+    need_shape(en, {H}, "embeddings.norm");
+    e->emb_norm = keep_f32(e.get(), en);
+    for (int l = 0; l < c.num_layers; l++) {
+      Layer L;
+      L.kind = kinds[l];
+      LC_CHECK(L.kind == 0 || L.kind == 1, "encoder: layer kind must be 0 (full) or 1 (sliding)");
+      std::string p = "layers." + std::to_string(l) + ".";
+      if (w[i]) {
+        LcTensor* an = check(w[i], "encoder attn_norm");
+        need_shape(an, {H}, p + "attn_norm");
+        L.attn_norm = keep_f32(e.get(), an);
+      } else {
+        LC_CHECK(l == 0, "encoder: only layer 0 may omit attn_norm");
+      }
+      i++;
+      L.Wqkv = take_mat(e.get(), w, i, 3 * H, H, p + "attn.Wqkv", false);
+      L.Wo = take_mat(e.get(), w, i, H, H, p + "attn.Wo", false);
+      LcTensor* mn = check(w[i++], "encoder mlp_norm");
+      need_shape(mn, {H}, p + "mlp_norm");
+      L.mlp_norm = keep_f32(e.get(), mn);
+      L.Wi = take_mat(e.get(), w, i, 2 * I, H, p + "mlp.Wi", true);
+      L.WoMlp = take_mat(e.get(), w, i, H, I, p + "mlp.Wo", false);
+      e->layers.push_back(L);
+    }
+    LcTensor* fn = check(w[i++], "encoder final_norm");
+    need_shape(fn, {H}, "final_norm");
+    e->final_norm = keep_f32(e.get(), fn);
+    // RoPE tables for every position the model can see (no growth during a forward)
+    int cap;
+    rope_table(64, c.rope_theta_global, 8192, &cap);
+    rope_table(64, c.rope_theta_local, 8192, &cap);
+  } catch (...) {
+    for (auto* t : e->owned) release(t);
+    throw;
+  }
+  Encoder* raw = e.release();
+  encoders().insert(raw);
+  *out = reinterpret_cast<uint64_t>(raw);
+  LC_API_END
+}
+
+int lc_encoder_free(uint64_t h) {
+  LC_API_BEGIN
+  Encoder* e = check_enc(h);
+  encoders().erase(e);
+  CUDA_OK(cudaStreamSynchronize(stream()));
+  for (auto* t : e->owned) release(t);
+  if (e->deq) release(e->deq);
+  if (e->ws) dfree(e->ws);
+  if (e->stage) cudaFreeHost(e->stage);
+  if (e->ids_stage) cudaFreeHost(e->ids_stage);
+  if (e->probs_stage) cudaFreeHost(e->probs_stage);
+  if (e->stage_ev) cudaEventDestroy(e->stage_ev);
+  for (auto& pe : e->pending) cudaEventDestroy(pe.second.first), cudaEventDestroy(pe.second.second);
+  for (auto ev : e->ev_pool) cudaEventDestroy(ev);
+  delete e;
+  LC_API_END
+}
+
+int lc_encoder_set_profiling(uint64_t h, int on) {
+  LC_API_BEGIN
+  check_enc(h)->prof = on != 0;
+  LC_API_END
+}
+
+int lc_encoder_profile_read(uint64_t h, double* ms, int64_t* n) {
+  LC_API_BEGIN
+  Encoder* e = check_enc(h);
+  CUDA_OK(cudaStreamSynchronize(stream()));
+  for (auto& pe : e->pending) {
+    float t = 0.f;
+    CUDA_OK(cudaEventElapsedTime(&t, pe.second.first, pe.second.second));
+    e->prof_ms[pe.first] += t;
+    e->prof_n[pe.first] += 1;
+    e->ev_pool.push_back(pe.second.first);
+    e->ev_pool.push_back(pe.second.second);
+  }
+  e->pending.clear();
+  for (int i = 0; i < 4; i++) {
+    ms[i] = e->prof_ms[i];
+    n[i] = e->prof_n[i];
+    e->prof_ms[i] = 0;
+    e->prof_n[i] = 0;
+  }
+  LC_API_END
+}
+
+int lc_encoder_forward(lc_tensor* hidden, lc_tensor* probs, uint64_t h, lc_tensor idsh, const int32_t* cu, int nseq, lc_tensor hwh,
+                       lc_tensor hbh) {
+  LC_API_BEGIN
+  Encoder* e = check_enc(h);
+  LcTensor* ids = check(idsh, "encoder ids");
+  LC_CHECK(ids->dtype == LC_I32 && ids->contiguous() && ids->numel() == cu[nseq], "encoder: ids must be dense i32 [T] with T = cu_seqlens[nseq]");
+  LcTensor* hw = hwh ? check(hwh, "encoder head_w") : nullptr;
+  LcTensor* hb = hbh ? check(hbh, "encoder head_b") : nullptr;
+  if (hw) check_head(e, hw, hb);
+  LC_CHECK(!probs || hw, "encoder: probs need head_w");
+  LcTensor* hid = hidden ? alloc(e->cfg.dtype, {(int64_t)cu[nseq], (int64_t)e->cfg.hidden_size}) : nullptr;
+  LcTensor* pr = probs ? alloc(LC_F32, {(int64_t)nseq, hw->shape[0]}) : nullptr;
+  try {
+    forward(e, (const int32_t*)ids->data(), cu, nseq, hid, hw, hb, pr ? (float*)pr->data() : nullptr);
+  } catch (...) {
+    if (hid) release(hid);
+    if (pr) release(pr);
+    throw;
+  }
+  if (hidden) *hidden = handle(hid);
+  if (probs) *probs = handle(pr);
+  LC_API_END
+}
+
+int lc_encoder_forward_host(uint64_t h, const int32_t* ids_host, const int32_t* cu, int nseq, lc_tensor hwh, lc_tensor hbh, float* probs_host) {
+  LC_API_BEGIN
+  Encoder* e = check_enc(h);
+  LcTensor* hw = check(hwh, "encoder head_w");
+  LcTensor* hb = hbh ? check(hbh, "encoder head_b") : nullptr;
+  check_head(e, hw, hb);
+  LC_CHECK(nseq > 0 && cu[0] == 0, "encoder: cu_seqlens must start at 0");
+  int64_t T = cu[nseq];
+  int64_t C = hw->shape[0];
+  cudaStream_t st = stream();
+  // ids: host -> pinned staging -> device
+  grow_pinned(e->ids_stage, e->ids_stage_bytes, (size_t)T * 4);
+  if (e->stage_ev) CUDA_OK(cudaEventSynchronize(e->stage_ev));
+  memcpy(e->ids_stage, ids_host, (size_t)T * 4);
+  int32_t* ids_dev = (int32_t*)dmalloc((size_t)T * 4);
+  float* probs_dev = (float*)dmalloc((size_t)nseq * C * 4);
+  CUDA_OK(cudaMemcpyAsync(ids_dev, e->ids_stage, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+  try {
+    forward(e, ids_dev, cu, nseq, nullptr, hw, hb, probs_dev);
+  } catch (...) {
+    dfree(ids_dev);
+    dfree(probs_dev);
+    throw;
+  }
+  grow_pinned(e->probs_stage, e->probs_stage_bytes, (size_t)nseq * C * 4);
+  CUDA_OK(cudaMemcpyAsync(e->probs_stage, probs_dev, (size_t)nseq * C * 4, cudaMemcpyDeviceToHost, st));
+  dfree(ids_dev);
+  dfree(probs_dev);
+  CUDA_OK(cudaStreamSynchronize(st));
+  memcpy(probs_host, e->probs_stage, (size_t)nseq * C * 4);
+  std::string err = take_device_errors();
+  LC_CHECK(err.empty(), err);
+  LC_API_END
+}
+
+}  // extern "C"

@@ -16,7 +16,7 @@ using namespace lc;
 
 // Vectorised fast path: dense f16/bf16/f32 rows, N % 8 == 0 (f32: % 4), N <= 256 vectors.
 template <typename T, int MAXV>
-__global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, const char* w, int wdt, const char* b, int bdt,
+__global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
                                                        T* __restrict__ y, int64_t rows, int N, float eps) {
   constexpr int VN = 16 / sizeof(T);
   int lane = threadIdx.x & 31;
@@ -66,12 +66,17 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
       if (c < nv) {
         uint4 raw;
         T* e = (T*)&raw;
+        float wv[VN], bv[VN];
+#pragma unroll
+        for (int j = 0; j < VN; j += 4) {
+          float4 a4 = w ? __ldg((const float4*)(w + c * VN + j)) : make_float4(1.f, 1.f, 1.f, 1.f);
+          float4 b4 = b ? __ldg((const float4*)(b + c * VN + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          wv[j] = a4.x, wv[j + 1] = a4.y, wv[j + 2] = a4.z, wv[j + 3] = a4.w;
+          bv[j] = b4.x, bv[j + 1] = b4.y, bv[j + 2] = b4.z, bv[j + 3] = b4.w;
+        }
 #pragma unroll
         for (int j = 0; j < VN; j++) {
-          int col = c * VN + j;
-          float o = (v[t][j] - mu) * rs;
-          if (w) o *= ld_as<float>(w, wdt, col);
-          if (b) o += ld_as<float>(b, bdt, col);
+          float o = (v[t][j] - mu) * rs * wv[j] + bv[j];
           if constexpr (sizeof(T) == 4) ((float*)e)[j] = o;
           else if constexpr (std::is_same<T, __half>::value) e[j] = __float2half_rn(o);
           else e[j] = __float2bfloat16_rn(o);
@@ -81,6 +86,35 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
     }
   }
 }
+
+// The register tile is sized to the row (vectors per lane = ceil(N / VN / 32)) so
+// that short rows (H = 768 -> 3 vectors) keep full occupancy.
+template <typename T>
+void launch_layernorm_vec(const T* x, const float* w, const float* b, T* y, int64_t rows, int N, float eps, cudaStream_t st) {
+  constexpr int VN = 16 / sizeof(T);
+  int per = (N / VN + 31) / 32;
+  unsigned blocks = lc::blocks_for(rows * 32, 256);
+  switch (per) {
+    case 0: case 1: k_layernorm_vec<T, 1><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 2: k_layernorm_vec<T, 2><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 3: k_layernorm_vec<T, 3><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 4: k_layernorm_vec<T, 4><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 5: case 6: k_layernorm_vec<T, 6><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    default: k_layernorm_vec<T, 8><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+  }
+}
+
+namespace lc {
+// Dense f16/bf16 rows of N (N % 8 == 0, N <= 2048), f32 weight (or null), 16-byte aligned.
+void layernorm_raw(const void* x, const float* w, void* y, int64_t rows, int N, float eps, int dtype, cudaStream_t st) {
+  LC_CHECK(N % 8 == 0 && N <= 2048, "layernorm_raw: row length must be a multiple of 8, at most 2048");
+  if (dtype == LC_F16)
+    launch_layernorm_vec<__half>((const __half*)x, w, nullptr, (__half*)y, rows, N, eps, st);
+  else
+    launch_layernorm_vec<__nv_bfloat16>((const __nv_bfloat16*)x, w, nullptr, (__nv_bfloat16*)y, rows, N, eps, st);
+  LC_LAUNCHED(1);
+}
+}  // namespace lc
 
 template <typename CT>
 __global__ void k_layernorm_generic(const char* x, int xdt, const char* w, int wdt, const char* b, int bdt, char* y, int ydt,
@@ -458,8 +492,19 @@ int lc_layer_norm(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh, doub
   int64_t rows = N ? x0->numel() / N : 0;
   if (rows) {
     LcTensor* x = contiguous(x0);
-    LcTensor* w = w0 ? contiguous(w0) : nullptr;
-    LcTensor* b = b0 ? contiguous(b0) : nullptr;
+    // the vector kernel reads f32 weight/bias; convert others once (they are [N])
+    auto as_f32 = [](LcTensor* t) -> LcTensor* {
+      if (!t) return nullptr;
+      if (t->dtype == LC_F32 && t->contiguous()) return t;
+      LcTensor* f = alloc(LC_F32, {t->numel()});
+      LcTensor* flat = view_of(t, {t->numel()}, {t->strides[t->ndim - 1]}, t->offset);
+      copy_into(t->contiguous() ? flat : t, f);
+      release(flat);
+      return f;
+    };
+    bool f64 = x->dtype == LC_F64;
+    LcTensor* w = f64 ? w0 : as_f32(w0);
+    LcTensor* b = f64 ? b0 : as_f32(b0);
     const char* wp = w ? w->data() : nullptr;
     const char* bp = b ? b->data() : nullptr;
     int wdt = w ? w->dtype : 0, bdt = b ? b->dtype : 0;
@@ -468,10 +513,12 @@ int lc_layer_norm(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh, doub
     bool aligned = (((uintptr_t)x->data() | (uintptr_t)y->data()) & 15) == 0;
     int vn = x->dtype == LC_F32 ? 4 : 8;
     bool vec = aligned && x->dtype == odt && (odt == LC_F32 || is_half(odt)) && N % vn == 0 && N / vn <= 32 * 8;
+    const float* wf = (const float*)wp;
+    const float* bf = (const float*)bp;
     if (vec) {
-      if (odt == LC_F16) k_layernorm_vec<__half, 8><<<blocks, 256, 0, st>>>((const __half*)x->data(), wp, wdt, bp, bdt, (__half*)y->data(), rows, (int)N, (float)eps);
-      else if (odt == LC_BF16) k_layernorm_vec<__nv_bfloat16, 8><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)x->data(), wp, wdt, bp, bdt, (__nv_bfloat16*)y->data(), rows, (int)N, (float)eps);
-      else k_layernorm_vec<float, 8><<<blocks, 256, 0, st>>>((const float*)x->data(), wp, wdt, bp, bdt, (float*)y->data(), rows, (int)N, (float)eps);
+      if (odt == LC_F16) launch_layernorm_vec<__half>((const __half*)x->data(), wf, bf, (__half*)y->data(), rows, (int)N, (float)eps, st);
+      else if (odt == LC_BF16) launch_layernorm_vec<__nv_bfloat16>((const __nv_bfloat16*)x->data(), wf, bf, (__nv_bfloat16*)y->data(), rows, (int)N, (float)eps, st);
+      else launch_layernorm_vec<float>((const float*)x->data(), wf, bf, (float*)y->data(), rows, (int)N, (float)eps, st);
     } else if (x->dtype == LC_F64) {
       k_layernorm_generic<double><<<blocks, 256, 0, st>>>(x->data(), x->dtype, wp, wdt, bp, bdt, y->data(), odt, rows, N, eps);
     } else {
