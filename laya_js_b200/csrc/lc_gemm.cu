@@ -188,8 +188,29 @@ __device__ __forceinline__ void load32f(const T* p, int col, int ncols, float* v
   }
 }
 
-template <typename T, int BN, int STAGES>
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)map), "r"(smem_u32(src)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Epilogue staging: per epilogue warp two 4 KB buffers holding a 32-row x 64-column
+// block in the 128-byte-swizzled layout the TMA store/load tensor maps use
+// (16-byte chunk c of row r at chunk position c ^ (r & 7)).
+constexpr uint32_t STG_BYTES = 4 * 2 * 4096;
+
+template <int STAGES, int BN>
+constexpr size_t gemm_smem_bytes(bool tma_epi) {
+  return (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + (tma_epi ? STG_BYTES : 0) + 1024 + 256;
+}
+
+template <typename T, int BN, int STAGES, bool TMAE>
 __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                                    const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                                                     const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   constexpr uint32_t A_BYTES = BM * BK * 2;
@@ -198,11 +219,13 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = (uint64_t*)(sB + STAGES * B_BYTES);
+  uint8_t* sE = sB + STAGES * B_BYTES;  // epilogue staging (TMAE only), 1024-aligned
+  uint64_t* full = (uint64_t*)(sE + (TMAE ? STG_BYTES : 0));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
+  uint64_t* rbar = tempty + 2;  // 8 residual-load barriers (2 per epilogue warp)
+  uint32_t* tmem_slot = (uint32_t*)(rbar + 8);
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -213,6 +236,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    for (int r = 0; r < 8; r++) mbar_init(&rbar[r], 1);
     for (int a = 0; a < 2; a++) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
@@ -299,6 +323,127 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         while (!mbar_try_wait(last, last_phase) && gtimer() - t0 < kWaitNs) {}
       }
     }
+  } else if constexpr (TMAE) {
+    // ---------------- epilogue through shared memory + TMA (warps 2..5 -> TMEM lane quarter warp % 4)
+    // Each warp owns 32 rows of the tile. Per 64-column unit: tcgen05.ld the
+    // f32 accumulators, apply RoPE / bias / residual / GeGLU, write the row's
+    // 8 chunks into the swizzled staging buffer, and one lane issues a TMA
+    // store of the 32 x 64 block (rows >= M and columns >= N are clipped by
+    // the tensor map). The residual block arrives by TMA load into the same
+    // buffer. Two buffers per warp let a store drain while the next unit runs.
+    const int quarter = warp & 3;
+    const GemmEpilogue& ep = args.ep;
+    const bool geglu = ep.kind == EPI_GEGLU;
+    const bool resid = ep.kind == EPI_RESIDUAL;
+    const int ncols = geglu ? 2 * args.N : args.N;  // accumulator columns that hold data
+    uint8_t* stg0 = sE + quarter * 2 * 4096;
+    uint64_t* rb = rbar + quarter * 2;
+    uint32_t rph0 = 0, rph1 = 0;
+    int blk = 0;  // blocks stored so far by this warp (selects the buffer)
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
+      if (!mbar_wait(&tfull[acc], acc_phase, abort)) break;
+      tc_fence_after();
+      const int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
+      const int row0 = m0 + quarter * 32;
+      const int row = row0 + lane;
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int u = 0; u < BN / 64; u++) {
+        const int col = n0 + u * 64;
+        const bool first = !geglu || (u & 1) == 0;  // GeGLU: two units fill one 64-column output block
+        const bool last = !geglu || (u & 1) == 1;
+        const int bcol = geglu ? n0 + (u & ~1) * 64 : col;  // first accumulator column of the block
+        if (bcol >= ncols) break;  // the rest of this tile is past the weight rows
+        const int buf = blk & 1;
+        uint8_t* stg = stg0 + buf * 4096;
+        if (first) {
+          if (lane == 0) bulk_wait_read1();  // the store that last used this buffer has read it
+          __syncwarp();
+          if (resid && lane == 0) {
+            mbar_arrive_expect_tx(&rb[buf], 4096);
+            tma_load_2d(stg, &tmR, &rb[buf], col, row0);
+          }
+        }
+        uint32_t ra[32], rbv[32];
+        tmem_ld32(tbase + u * 64, ra);
+        tmem_ld32(tbase + u * 64 + 32, rbv);
+        tmem_wait_ld();
+        float a[32], b[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) a[j] = __uint_as_float(ra[j]), b[j] = __uint_as_float(rbv[j]);
+        if (geglu) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) a[j] = gelu_exact(a[j]) * b[j];
+        } else {
+          if (ep.kind == EPI_ROPE_QKV && col < ep.rope_cols) {
+            const int p = row < args.M ? ep.pos[row] : 0;
+            const float* cs = ep.rope_cs + (int64_t)p * 32;
+            const float* sn = ep.rope_cs + (int64_t)ep.rope_cap * 32 + (int64_t)p * 32;
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              float c = cs[j], s = sn[j];
+              float x1 = a[j], x2 = b[j];
+              a[j] = x1 * c - x2 * s;
+              b[j] = x2 * c + x1 * s;
+            }
+          }
+          if (args.bias) {
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              if (col + j < args.N) a[j] += ld_as<float>((const char*)args.bias, args.bias_dtype, col + j);
+              if (col + 32 + j < args.N) b[j] += ld_as<float>((const char*)args.bias, args.bias_dtype, col + 32 + j);
+            }
+          }
+          if (resid) {
+            const uint32_t ph = buf ? rph1 : rph0;
+            if (!mbar_wait(&rb[buf], ph, abort)) { ok = false; break; }
+            if (buf) rph1 ^= 1; else rph0 ^= 1;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+              uint4 v = *(const uint4*)(stg + lane * 128 + ((c ^ (lane & 7)) << 4));
+              const T* h = (const T*)&v;
+#pragma unroll
+              for (int j = 0; j < 8; j++) {
+                if (c < 4) a[c * 8 + j] += TcFmt<T>::back(h[j]);
+                else b[(c - 4) * 8 + j] += TcFmt<T>::back(h[j]);
+              }
+            }
+          }
+        }
+        // write this row's chunks: GeGLU writes 4 chunks (32 columns) per unit, else 8
+        const int c0 = geglu ? (u & 1) * 4 : 0;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          if (geglu && c >= 4) break;
+          const float* src = (c < 4) ? a + c * 8 : b + (c - 4) * 8;
+          uint4 v;
+          T* h = (T*)&v;
+#pragma unroll
+          for (int j = 0; j < 8; j++) h[j] = TcFmt<T>::cvt(src[j]);
+          const int cc = c0 + c;
+          *(uint4*)(stg + lane * 128 + ((cc ^ (lane & 7)) << 4)) = v;
+        }
+        if (last || bcol + 64 >= ncols) {
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmY, stg, geglu ? bcol / 2 : col, row0);
+            bulk_commit();
+          }
+          blk++;
+          if (geglu && (u & 1) == 0) break;  // the pair's second unit is past the weight rows
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..5 -> TMEM lane quarter warp % 4)
     const int quarter = warp & 3;
@@ -392,23 +537,25 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-using MapKey = std::tuple<uintptr_t, int64_t, int64_t, int, int>;
+using MapKey = std::tuple<uintptr_t, int64_t, int64_t, int64_t, int, int>;
 std::map<MapKey, CUtensorMap>& map_cache() {
   static std::map<MapKey, CUtensorMap> m;
   return m;
 }
 
 // Row-major [rows, K] matrix, boxes of box_rows x 64, 128-byte swizzle.
-const CUtensorMap& tensor_map(const void* ptr, int64_t rows, int64_t K, int box_rows, int dtype) {
-  MapKey key{(uintptr_t)ptr, rows, K, box_rows, dtype};
+// Row-major [rows, cols] matrix with row stride ld (elements), boxes of
+// box_rows x box_cols (box_cols * 2 bytes = 128: one swizzle row).
+const CUtensorMap& tensor_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype) {
+  MapKey key{(uintptr_t)ptr, rows, cols, ld, box_cols * 1024 + box_rows, dtype};
   auto& c = map_cache();
   auto it = c.find(key);
   if (it != c.end()) return it->second;
   if (c.size() > 8192) c.clear();
   CUtensorMap m;
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
   CUresult r = encode_fn()(&m, dtype == LC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr),
                            dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -417,16 +564,18 @@ const CUtensorMap& tensor_map(const void* ptr, int64_t rows, int64_t K, int box_
   return c.emplace(key, m).first->second;
 }
 
-template <typename T, int BN, int STAGES>
-void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st) {
-  constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+template <typename T, int BN, int STAGES, bool TMAE>
+void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr, const GemmArgs& a,
+                 cudaStream_t st) {
+  constexpr size_t smem = gemm_smem_bytes<STAGES, BN>(TMAE);
+  static_assert(smem <= 232448, "GEMM shared memory above the 227 KB per-CTA limit");
   static bool attr = false;
   if (!attr) {
-    CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<T, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<T, BN, STAGES, TMAE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr = true;
   }
   int grid = std::min(a.ntiles, lc::num_sms());
-  k_gemm_tc<T, BN, STAGES><<<grid, 192, smem, st>>>(ma, mb, a);
+  k_gemm_tc<T, BN, STAGES, TMAE><<<grid, 192, smem, st>>>(ma, mb, my, mr, a);
 }
 
 }  // namespace
@@ -458,14 +607,28 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
   a.bias = bias;
   a.bias_dtype = bias_dtype;
   a.ep = ep;
-  const CUtensorMap& ma = tensor_map(x, M, K, BM, dtype);
-  const CUtensorMap& mb = tensor_map(w, Nacc, K, BN, dtype);
-  if (dtype == LC_F16) {
-    if (BN == 256) launch_gemm<__half, 256, 4>(ma, mb, a, st);
-    else launch_gemm<__half, 128, 6>(ma, mb, a, st);
+  const CUtensorMap& ma = tensor_map(x, M, K, K, BK, BM, dtype);
+  const CUtensorMap& mb = tensor_map(w, Nacc, K, K, BK, BN, dtype);
+  // TMA-store epilogue when the output (and residual) rows are 16-byte strided and aligned
+  const bool tmae = a.vec_ok && (N % 8 == 0) && !(ep.kind == EPI_RESIDUAL && ep.resid == nullptr);
+  if (tmae) {
+    const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
+    const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
+    if (dtype == LC_F16) {
+      if (BN == 256) launch_gemm<__half, 256, 4, true>(ma, mb, my, mr, a, st);
+      else launch_gemm<__half, 128, 6, true>(ma, mb, my, mr, a, st);
+    } else {
+      if (BN == 256) launch_gemm<__nv_bfloat16, 256, 4, true>(ma, mb, my, mr, a, st);
+      else launch_gemm<__nv_bfloat16, 128, 6, true>(ma, mb, my, mr, a, st);
+    }
   } else {
-    if (BN == 256) launch_gemm<__nv_bfloat16, 256, 4>(ma, mb, a, st);
-    else launch_gemm<__nv_bfloat16, 128, 6>(ma, mb, a, st);
+    if (dtype == LC_F16) {
+      if (BN == 256) launch_gemm<__half, 256, 4, false>(ma, mb, ma, ma, a, st);
+      else launch_gemm<__half, 128, 6, false>(ma, mb, ma, ma, a, st);
+    } else {
+      if (BN == 256) launch_gemm<__nv_bfloat16, 256, 4, false>(ma, mb, ma, ma, a, st);
+      else launch_gemm<__nv_bfloat16, 128, 6, false>(ma, mb, ma, ma, a, st);
+    }
   }
   LC_LAUNCHED(1);
   return true;

@@ -11,7 +11,8 @@ from laya_js_b200.host import HostTensor, bf16_bits_to_f32, f32_to_bf16_bits, to
 pytestmark = pytest.mark.gpu
 
 SHAPES = [(1, 40, 64), (127, 128, 64), (128, 256, 768), (300, 768, 768), (1000, 2304, 768), (4096, 768, 1152),
-          (513, 5248, 1024), (77, 1024, 2624), (2048, 3072, 1024), (130, 24, 128), (64, 200, 200)]
+          (513, 5248, 1024), (77, 1024, 2624), (2048, 3072, 1024), (130, 24, 128), (64, 200, 200),
+          (5, 44, 64), (300, 129, 128), (1, 2304, 768)]
 
 
 def _mk(dtype, a):
