@@ -71,12 +71,14 @@ int lc_encoder_forward_host(uint64_t enc, const int32_t* ids_host, const int32_t
 /*
  * Per-kernel-class device timing of the forwards that follow (tracing):
  * when enabled, every forward records CUDA events around its kernels on the
- * library stream. lc_encoder_profile_read returns, per class
- * (0 GEMM, 1 attention, 2 LayerNorm/embedding, 3 head/other), the summed
+ * library stream. lc_encoder_profile_read returns, per class, the summed
  * milliseconds and launch counts since the last read, then resets them.
+ * Classes: 0 Wqkv GEMM (+RoPE), 1 attention, 2 LayerNorm/embedding,
+ * 3 head/dequant/other, 4 Wo GEMM (+residual), 5 Wi GEMM (+GeGLU),
+ * 6 mlp.Wo GEMM (+residual), 7 unused.
  */
 int lc_encoder_set_profiling(uint64_t enc, int on);
-int lc_encoder_profile_read(uint64_t enc, double* ms /* [4] */, int64_t* launches /* [4] */);
+int lc_encoder_profile_read(uint64_t enc, double* ms /* [8] */, int64_t* launches /* [8] */);
 
 /*
  * Attention of one encoder layer on its own: qkv [T, 3H] (RoPE applied),

@@ -171,8 +171,8 @@ struct Encoder {
   bool prof = false;
   std::vector<cudaEvent_t> ev_pool;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pending;
-  double prof_ms[4] = {0, 0, 0, 0};
-  int64_t prof_n[4] = {0, 0, 0, 0};
+  double prof_ms[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int64_t prof_n[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 };
 
 cudaEvent_t pooled_event(Encoder* e) {
@@ -296,7 +296,7 @@ Mat take_mat(Encoder* e, const lc_tensor* w, int& i, int64_t N, int64_t K, const
 }
 
 // y = x · Wᵀ with the given epilogue (dense weight or packed weight dequantised into the scratch)
-void run_gemm(Encoder* e, const Mat& m, const void* x, int64_t M, void* y, int64_t ldy, const GemmEpilogue& ep, int64_t n_out) {
+void run_gemm(Encoder* e, const Mat& m, const void* x, int64_t M, void* y, int64_t ldy, const GemmEpilogue& ep, int64_t n_out, int cls) {
   const void* w;
   if (m.dense) {
     w = m.dense->data();
@@ -314,7 +314,7 @@ void run_gemm(Encoder* e, const Mat& m, const void* x, int64_t M, void* y, int64
     release(view);
     w = e->deq->data();
   }
-  Prof p(e, 0);
+  Prof p(e, cls);
   bool ok = gemm_raw(x, M, m.K, w, n_out, nullptr, 0, y, ldy, e->cfg.dtype, ep, stream());
   LC_CHECK(ok, "encoder: the tcgen05 GEMM rejected a projection shape");
 }
@@ -376,8 +376,8 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
   LC_LAUNCHED(1);
 
   int cap_g = 0, cap_l = 0;
-  const float* rope_g = rope_table(64, c.rope_theta_global, std::max(maxlen, 1), &cap_g);
-  const float* rope_l = rope_table(64, c.rope_theta_local, std::max(maxlen, 1), &cap_l);
+  const float* rope_g = rope_table(64, c.rope_theta_global, std::max(maxlen, 1), &cap_g, true);
+  const float* rope_l = rope_table(64, c.rope_theta_local, std::max(maxlen, 1), &cap_l, true);
 
   // embeddings
   Prof* pe = new Prof(e, 2);
@@ -412,7 +412,7 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
     eq.rope_cs = L.kind == 0 ? rope_g : rope_l;
     eq.rope_cap = L.kind == 0 ? cap_g : cap_l;
     eq.rope_cols = 2 * H;
-    run_gemm(e, L.Wqkv, hin, T, qkv, 3 * H, eq, 3 * H);
+    run_gemm(e, L.Wqkv, hin, T, qkv, 3 * H, eq, 3 * H, 0);
     // attention -> h (h is free again once the Wqkv GEMM has read it)
     {
       Prof p(e, 1);
@@ -422,15 +422,15 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
     er.kind = EPI_RESIDUAL;
     er.resid = x;
     er.ldr = H;
-    run_gemm(e, L.Wo, h, T, x, H, er, H);
+    run_gemm(e, L.Wo, h, T, x, H, er, H, 4);
     {
       Prof p(e, 2);
       layernorm_raw(x, (const float*)L.mlp_norm->data(), h, T, H, (float)c.norm_eps, c.dtype, st);
     }
     GemmEpilogue eg;
     eg.kind = EPI_GEGLU;
-    run_gemm(e, L.Wi, h, T, qkv, I, eg, I);
-    run_gemm(e, L.WoMlp, qkv, T, x, H, er, H);
+    run_gemm(e, L.Wi, h, T, qkv, I, eg, I, 5);
+    run_gemm(e, L.WoMlp, qkv, T, x, H, er, H, 6);
   }
   void* fin = hidden_out ? hidden_out->data() : h;
   {
@@ -514,8 +514,8 @@ int lc_encoder_create(uint64_t* out, const lc_encoder_config* cfg, const int32_t
     e->final_norm = keep_f32(e.get(), fn);
     // RoPE tables for every position the model can see (no growth during a forward)
     int cap;
-    rope_table(64, c.rope_theta_global, 8192, &cap);
-    rope_table(64, c.rope_theta_local, 8192, &cap);
+    rope_table(64, c.rope_theta_global, 8192, &cap, true);
+    rope_table(64, c.rope_theta_local, 8192, &cap, true);
   } catch (...) {
     for (auto* t : e->owned) release(t);
     throw;
@@ -563,7 +563,7 @@ int lc_encoder_profile_read(uint64_t h, double* ms, int64_t* n) {
     e->ev_pool.push_back(pe.second.second);
   }
   e->pending.clear();
-  for (int i = 0; i < 4; i++) {
+  for (int i = 0; i < 8; i++) {
     ms[i] = e->prof_ms[i];
     n[i] = e->prof_n[i];
     e->prof_ms[i] = 0;

@@ -380,11 +380,11 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         } else {
           if (ep.kind == EPI_ROPE_QKV && col < ep.rope_cols) {
             const int p = row < args.M ? ep.pos[row] : 0;
-            const float* cs = ep.rope_cs + (int64_t)p * 32;
-            const float* sn = ep.rope_cs + (int64_t)ep.rope_cap * 32 + (int64_t)p * 32;
+            const float* cs = ep.rope_cs + p;
+            const float* sn = ep.rope_cs + (int64_t)ep.rope_cap * 32 + p;
 #pragma unroll
             for (int j = 0; j < 32; j++) {
-              float c = cs[j], s = sn[j];
+              float c = __ldg(cs + (int64_t)j * ep.rope_cap), s = __ldg(sn + (int64_t)j * ep.rope_cap);
               float x1 = a[j], x2 = b[j];
               a[j] = x1 * c - x2 * s;
               b[j] = x2 * c + x1 * s;
@@ -479,11 +479,11 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         }
         if (ep.kind == EPI_ROPE_QKV && col < ep.rope_cols) {
           const int p = ep.pos[row];
-          const float* cs = ep.rope_cs + (int64_t)p * 32;
-          const float* sn = ep.rope_cs + (int64_t)ep.rope_cap * 32 + (int64_t)p * 32;
+          const float* cs = ep.rope_cs + p;
+          const float* sn = ep.rope_cs + (int64_t)ep.rope_cap * 32 + p;
 #pragma unroll
           for (int j = 0; j < 32; j++) {
-            float c = cs[j], s = sn[j];
+            float c = __ldg(cs + (int64_t)j * ep.rope_cap), s = __ldg(sn + (int64_t)j * ep.rope_cap);
             float x1 = a[j], x2 = b[j];
             a[j] = x1 * c - x2 * s;
             b[j] = x2 * c + x1 * s;

@@ -15,7 +15,7 @@ struct GemmEpilogue {
   const void* resid = nullptr;      // EPI_RESIDUAL: [M, N] in the output dtype, row stride ldr
   int64_t ldr = 0;
   const int32_t* pos = nullptr;     // EPI_ROPE_QKV: position of each row
-  const float* rope_cs = nullptr;   // EPI_ROPE_QKV: cos/sin table [cap][32] ++ [cap][32]
+  const float* rope_cs = nullptr;   // EPI_ROPE_QKV: cos/sin table [32][cap] ++ [32][cap] (position-minor)
   int rope_cap = 0;
   int rope_cols = 0;                // EPI_ROPE_QKV: columns [0, rope_cols) are rotated (q and k), head dim 64
 };
@@ -28,7 +28,7 @@ bool gemm_linear(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, Lc
 bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, const void* bias, int bias_dtype, void* y, int64_t ldy,
               int dtype, const GemmEpilogue& ep, cudaStream_t st);
 void linear_simt(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y);
-const float* rope_table(int D, double base, int L, int* cap_out);
+const float* rope_table(int D, double base, int L, int* cap_out, bool position_minor = false);
 bool attention_try_fast(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor* y);
 // Reads and clears the device-side error words of the pipelined kernels.
 std::string take_device_errors();

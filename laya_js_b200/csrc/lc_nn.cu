@@ -202,16 +202,18 @@ struct RopeTable {
   float* d = nullptr;
   int cap = 0;
 };
-std::map<std::pair<int, double>, RopeTable>& rope_cache() {
-  static std::map<std::pair<int, double>, RopeTable> m;
+std::map<std::tuple<int, double, bool>, RopeTable>& rope_cache() {
+  static std::map<std::tuple<int, double, bool>, RopeTable> m;
   return m;
 }
 }  // namespace
 
 namespace lc {
-// cos/sin table [cap][half] ++ [cap][half] (f32) for head dim D and `base`, cap >= L.
-const float* rope_table(int D, double base, int L, int* cap_out) {
-  auto& t = rope_cache()[{D, base}];
+// cos/sin table (f32) for head dim D and `base`, cap >= L positions:
+// [cap][half] cos ++ [cap][half] sin, or with position_minor [half][cap] ++ [half][cap]
+// (what the GEMM epilogue reads: a warp's 32 rows are consecutive positions).
+const float* rope_table(int D, double base, int L, int* cap_out, bool position_minor) {
+  auto& t = rope_cache()[{D, base, position_minor}];
   if (t.cap < L) {
     int cap = 64;
     while (cap < L) cap <<= 1;
@@ -223,8 +225,9 @@ const float* rope_table(int D, double base, int L, int* cap_out) {
       float inv = (float)std::pow(2.0, (double)e);
       for (int l = 0; l < cap; l++) {
         float th = (float)((double)l * (double)inv);
-        h[(size_t)l * half + i] = (float)std::cos((double)th);
-        h[(size_t)cap * half + (size_t)l * half + i] = (float)std::sin((double)th);
+        size_t ci = position_minor ? (size_t)i * cap + l : (size_t)l * half + i;
+        h[ci] = (float)std::cos((double)th);
+        h[(size_t)cap * half + ci] = (float)std::sin((double)th);
       }
     }
     if (t.d) CUDA_OK(cudaFree(t.d));

@@ -112,8 +112,11 @@ def set_profiling(fused: FusedEncoder, on: bool) -> None:
 
 def profile_read(fused: FusedEncoder) -> dict:
     """Summed device ms and launch counts per kernel class since the last read."""
-    ms = (C.c_double * 4)()
-    n = (C.c_int64 * 4)()
+    ms = (C.c_double * 8)()
+    n = (C.c_int64 * 8)()
     _lib.call("lc_encoder_profile_read", C.c_uint64(fused.handle), ms, n)
-    names = ("gemm", "attention", "layernorm", "other")
-    return {k: {"ms": ms[i], "launches": n[i]} for i, k in enumerate(names)}
+    names = ("gemm_qkv", "attention", "layernorm", "other", "gemm_o", "gemm_i", "gemm_mlp_o")
+    out = {k: {"ms": ms[i], "launches": n[i]} for i, k in enumerate(names)}
+    out["gemm"] = {"ms": sum(out[k]["ms"] for k in names if k.startswith("gemm")),
+                   "launches": sum(out[k]["launches"] for k in names if k.startswith("gemm"))}
+    return out
