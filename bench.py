@@ -176,7 +176,7 @@ def main() -> None:
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(f"cuda:{local}"))
     else:
         torch.cuda.set_device(local)
 

@@ -1,0 +1,87 @@
+"""Small, self-contained cases of the hot kernels for profiling (ncu) and
+quick timing. Each case fits in a few GB and ends in seconds.
+
+    python -m laya_js_b200.profile_cases encoder   # 2-layer ModernBERT-base, 64 prompts L~U[32,512]
+    python -m laya_js_b200.profile_cases gemm      # one 32768x2304x768 linear (f16)
+    python -m laya_js_b200.profile_cases attention # varlen attention, 256 prompts, global + sliding
+
+Every case prints one line with its shape and the device time per launch
+(CUDA events on the library stream, after warm-up).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import sys
+import time
+
+import numpy as np
+
+from . import _lib, workloads as WL
+from .backend import createCudaBackend
+from .encoder import FusedEncoder, attention_varlen
+from .host import HostTensor
+from .modernbert import loadModernBert, parseModernBertConfig
+
+
+def _sync_time(b, fn, reps: int) -> float:
+    b.flush()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    b.flush()
+    return (time.perf_counter() - t0) / reps * 1e3
+
+
+def case_encoder(b) -> str:
+    cfg_json = {**WL.BASE, "num_hidden_layers": 2}
+    W = WL.random_weights(cfg_json, seed=1)
+    enc = loadModernBert(b, parseModernBertConfig(cfg_json), WL.host_getter(W), "f16")
+    fused = FusedEncoder(enc)
+    lens = WL.lengths(64, 32, 512, seed=2)
+    ids, cu = WL.token_batch(cfg_json, lens, seed=3)
+    tids = b.fromHost(HostTensor("i32", ids.shape, ids))
+
+    def run():
+        h, _ = fused.forward(tids, cu, want_hidden=True)
+        b.dispose(h)
+    run()
+    ms = _sync_time(b, run, 3)
+    fused.free()
+    enc.dispose()
+    return f"encoder 2 layers, T={int(cu[-1])} tokens: {ms:.3f} ms/forward"
+
+
+def case_gemm(b) -> str:
+    rng = np.random.default_rng(0)
+    M, N, K = 32768, 2304, 768
+    x = b.fromHost(HostTensor("f16", (M, K), rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)))
+    w = b.fromHost(HostTensor("f16", (N, K), (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float16)))
+    run = lambda: b.dispose(b.linear(x, w))
+    run()
+    ms = _sync_time(b, run, 5)
+    return f"gemm {M}x{N}x{K} f16: {ms * 1e3:.1f} us/launch, {2 * M * N * K / ms / 1e9:.0f} TFLOP/s (host-timed)"
+
+
+def case_attention(b) -> str:
+    rng = np.random.default_rng(0)
+    lens = WL.lengths(256, 32, 512, seed=1)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = b.fromHost(HostTensor("f16", (T, 2304), rng.standard_normal((T, 2304), dtype=np.float32).astype(np.float16)))
+    out = []
+    for hw in (-1, 64):
+        run = lambda: b.dispose(attention_varlen(b, qkv, cu, hw, 0.125))
+        run()
+        out.append(f"{'global' if hw < 0 else 'sliding'} {_sync_time(b, run, 3):.3f} ms")
+    return f"attention T={T}, 12 heads: " + ", ".join(out)
+
+
+def main(argv) -> None:
+    b = createCudaBackend(0)
+    cases = {"encoder": case_encoder, "gemm": case_gemm, "attention": case_attention}
+    for name in argv[1:] or list(cases):
+        print(cases[name](b), flush=True)
+
+
+if __name__ == "__main__":
+    main(sys.argv)
