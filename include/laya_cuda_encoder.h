@@ -83,8 +83,10 @@ int lc_encoder_profile_read(uint64_t enc, double* ms /* [8] */, int64_t* launche
 /*
  * Attention of one encoder layer on its own: qkv [T, 3H] (RoPE applied),
  * heads of 64; half_window < 0 = global attention. Returns att [T, H].
+ * kernel 0 = tcgen05/TMEM kernel (the one the encoder runs), 1 = the
+ * mma.sync kernel (kept as an independent cross-check).
  */
-int lc_attention_varlen(lc_tensor* out, lc_tensor qkv, const int32_t* cu_seqlens, int nseq, int half_window, double scale);
+int lc_attention_varlen(lc_tensor* out, lc_tensor qkv, const int32_t* cu_seqlens, int nseq, int half_window, double scale, int kernel);
 
 #ifdef __cplusplus
 }

@@ -284,8 +284,10 @@ bool attention_try_fast(const LcTensor*, const LcTensor*, const LcTensor*, const
 
 using namespace lc;
 
-extern "C" int lc_attention_varlen(lc_tensor* out, lc_tensor qkvh, const int32_t* cu_seqlens, int nseq, int half_window, double scale) {
+extern "C" int lc_attention_varlen(lc_tensor* out, lc_tensor qkvh, const int32_t* cu_seqlens, int nseq, int half_window, double scale,
+                                   int kernel) {
   LC_API_BEGIN
+  LC_CHECK(kernel == 0 || kernel == 1, "attentionVarlen: kernel must be 0 (tcgen05) or 1 (mma.sync)");
   LcTensor* qkv = check(qkvh, "attentionVarlen qkv");
   LC_CHECK(qkv->ndim == 2 && qkv->contiguous() && is_half(qkv->dtype), "attentionVarlen: qkv must be a dense f16/bf16 [T, 3H] matrix");
   LC_CHECK(qkv->shape[1] % (3 * HD) == 0, "attentionVarlen: qkv columns must be 3 x heads x 64");
@@ -294,11 +296,14 @@ extern "C" int lc_attention_varlen(lc_tensor* out, lc_tensor qkvh, const int32_t
   LC_CHECK(nseq >= 0 && cu_seqlens[0] == 0 && cu_seqlens[nseq] == T, "attentionVarlen: cu_seqlens must run from 0 to T");
   for (int s = 0; s < nseq; s++) LC_CHECK(cu_seqlens[s + 1] >= cu_seqlens[s], "attentionVarlen: cu_seqlens must be non-decreasing");
   LcTensor* y = alloc(qkv->dtype, {T, (int64_t)H});
-  std::vector<int4> tiles = attention_tiles(cu_seqlens, nseq);
+  std::vector<int4> tiles = kernel == 0 ? attention_tiles_tc(cu_seqlens, nseq) : attention_tiles(cu_seqlens, nseq);
   if (!tiles.empty()) {
     int4* d = (int4*)dmalloc(tiles.size() * sizeof(int4));
     CUDA_OK(cudaMemcpyAsync(d, tiles.data(), tiles.size() * sizeof(int4), cudaMemcpyHostToDevice, stream()));
-    attention_varlen(qkv->data(), y->data(), d, (int)tiles.size(), T, H, half_window, (float)scale, qkv->dtype, stream());
+    if (kernel == 0)
+      attention_varlen_tc(qkv->data(), y->data(), d, (int)tiles.size(), T, H, half_window, (float)scale, qkv->dtype, stream());
+    else
+      attention_varlen(qkv->data(), y->data(), d, (int)tiles.size(), T, H, half_window, (float)scale, qkv->dtype, stream());
     dfree(d);
   }
   *out = handle(y);

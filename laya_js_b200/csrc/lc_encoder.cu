@@ -351,7 +351,7 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
   const int64_t esz = 2;
   cudaStream_t st = stream();
   // host-built metadata: cu_seqlens + attention tiles, one pinned staging buffer
-  std::vector<int4> tiles = attention_tiles(cu, nseq);
+  std::vector<int4> tiles = attention_tiles_tc(cu, nseq);
   size_t cu_bytes = ((size_t)(nseq + 1) * 4 + 15) & ~(size_t)15;
   size_t meta = cu_bytes + tiles.size() * sizeof(int4);
   if (e->stage_ev) CUDA_OK(cudaEventSynchronize(e->stage_ev));
@@ -416,7 +416,7 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
     // attention -> h (h is free again once the Wqkv GEMM has read it)
     {
       Prof p(e, 1);
-      attention_varlen(qkv, h, tiles_dev, (int)tiles.size(), T, H, L.kind == 0 ? -1 : c.local_attention / 2, scale, c.dtype, st);
+      attention_varlen_tc(qkv, h, tiles_dev, (int)tiles.size(), T, H, L.kind == 0 ? -1 : c.local_attention / 2, scale, c.dtype, st);
     }
     GemmEpilogue er;
     er.kind = EPI_RESIDUAL;

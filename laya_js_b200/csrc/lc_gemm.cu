@@ -21,6 +21,7 @@
 // No cluster launch and no multicast: each CTA loads its own tiles.
 #include "lc_api.h"
 #include "lc_gemm.h"
+#include "lc_sm100.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -34,111 +35,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr uint64_t kWaitNs = 2000000000ull;
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait for phase `parity` of `bar`; false on timeout or when another
-// role has aborted (then the caller unwinds).
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = gtimer();
-  for (uint32_t it = 0;; it++) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63) == 63) {
-      if (*abort) return false;
-      if (gtimer() - t0 > kWaitNs) {
-        *abort = 1;
-        atomicOr(&g_gemm_err, 1u);
-        return false;
-      }
-    }
-  }
-}
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
-        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row
-// groups 1024 bytes apart (tcgen05 "matrix descriptor", version 1).
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: 8 rows x 128 B
-  d |= (uint64_t)1 << 46;                   // descriptor version for sm_100
-  d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
-  return d;
-}
-
-template <typename T> struct TcFmt;
-template <> struct TcFmt<__half> {
-  static constexpr uint32_t ab = 0;
-  __device__ static __half cvt(float v) { return __float2half_rn(v); }
-  __device__ static float back(__half v) { return __half2float(v); }
-};
-template <> struct TcFmt<__nv_bfloat16> {
-  static constexpr uint32_t ab = 1;
-  __device__ static __nv_bfloat16 cvt(float v) { return __float2bfloat16_rn(v); }
-  __device__ static float back(__nv_bfloat16 v) { return __bfloat162float(v); }
-};
-
-// Instruction descriptor for kind::f16: D=f32, A=B=T, both K-major, M=128, N=BN.
-template <typename T, int BN>
-__device__ __forceinline__ uint32_t idesc_f16() {
-  return (1u << 4) | (TcFmt<T>::ab << 7) | (TcFmt<T>::ab << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
+using namespace sm100;
 
 struct GemmArgs {
   int M, N, K;
@@ -268,7 +165,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
         int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
         for (int kb = 0; kb < KB; kb++) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort)) { ok = false; break; }
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
           tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, m0);
           tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, n0);
@@ -297,11 +194,11 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       uint64_t* last = nullptr;
       uint32_t last_phase = 0;
       for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) { ok = false; break; }
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * BN);
         for (int kb = 0; kb < KB; kb++) {
-          if (!mbar_wait(&full[stage], phase, abort)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, abort, &g_gemm_err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * A_BYTES), b0 = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
@@ -344,7 +241,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     uint32_t acc_phase = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
-      if (!mbar_wait(&tfull[acc], acc_phase, abort)) break;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort, &g_gemm_err)) break;
       tc_fence_after();
       const int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
       const int row0 = m0 + quarter * 32;
@@ -399,7 +296,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
           }
           if (resid) {
             const uint32_t ph = buf ? rph1 : rph0;
-            if (!mbar_wait(&rb[buf], ph, abort)) { ok = false; break; }
+            if (!mbar_wait(&rb[buf], ph, abort, &g_gemm_err)) { ok = false; break; }
             if (buf) rph1 ^= 1; else rph0 ^= 1;
 #pragma unroll
             for (int c = 0; c < 8; c++) {
@@ -452,7 +349,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < args.ntiles; t += gridDim.x) {
-      if (!mbar_wait(&tfull[acc], acc_phase, abort)) break;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort, &g_gemm_err)) break;
       tc_fence_after();
       const int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
       const int row = m0 + quarter * 32 + lane;
@@ -644,9 +541,14 @@ bool gemm_linear(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, Lc
 std::string take_device_errors() {
   unsigned int e = 0, z = 0;
   CUDA_OK(cudaMemcpyFromSymbol(&e, g_gemm_err, sizeof(e)));
-  if (!e) return "";
+  std::string msg = take_attention_errors();
+  if (!e) return msg;
   CUDA_OK(cudaMemcpyToSymbol(g_gemm_err, &z, sizeof(z)));
-  return "tcgen05 GEMM: a pipeline wait timed out (kernel aborted its tile loop)";
+  return "tcgen05 GEMM: a pipeline wait timed out (kernel aborted its tile loop)" + (msg.empty() ? std::string() : "; " + msg);
+}
+
+const CUtensorMap& tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype) {
+  return tensor_map(ptr, rows, cols, ld, box_cols, box_rows, dtype);
 }
 
 }  // namespace lc

@@ -1,5 +1,7 @@
 // Tensor-core GEMM (tcgen05 + TMA, sm_100a) and related internal entry points.
 #pragma once
+#include <cuda.h>
+
 #include "lc_common.cuh"
 
 // What the GEMM epilogue does with the f32 accumulator tile before the store.
@@ -32,5 +34,12 @@ const float* rope_table(int D, double base, int L, int* cap_out, bool position_m
 bool attention_try_fast(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor* y);
 // Reads and clears the device-side error words of the pipelined kernels.
 std::string take_device_errors();
+std::string take_attention_errors();
+// Cached 2-D tiled tensor map (128-byte swizzle) over a row-major [rows, cols] matrix with row stride ld.
+const CUtensorMap& tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype);
+// tcgen05 varlen attention (lc_attention_tc.cu) and its 128-row tile list.
+std::vector<int4> attention_tiles_tc(const int32_t* cu, int nseq);
+void attention_varlen_tc(const void* qkv, void* out, const int4* tiles_dev, int ntiles, int64_t T, int H, int half_window, float scale,
+                         int dtype, cudaStream_t st);
 }  // namespace lc
 void lc_gemm_destroy_caches();

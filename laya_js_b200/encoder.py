@@ -97,12 +97,12 @@ class FusedEncoder:
             self.handle = 0
 
 
-def attention_varlen(backend, qkv, cu_seqlens: np.ndarray, half_window: int, scale: float):
-    """lc_attention_varlen: qkv [T, 3H] (RoPE applied) -> att [T, H]."""
+def attention_varlen(backend, qkv, cu_seqlens: np.ndarray, half_window: int, scale: float, kernel: int = 0):
+    """lc_attention_varlen: qkv [T, 3H] (RoPE applied) -> att [T, H]; kernel 0 tcgen05, 1 mma.sync."""
     cu = np.ascontiguousarray(cu_seqlens, np.int32)
     out = C.c_uint64()
     _lib.call("lc_attention_varlen", C.byref(out), C.c_uint64(backend._h(qkv)), cu.ctypes.data_as(C.POINTER(C.c_int32)),
-              len(cu) - 1, int(half_window), C.c_double(scale))
+              len(cu) - 1, int(half_window), C.c_double(scale), int(kernel))
     return backend._wrap(out.value)
 
 

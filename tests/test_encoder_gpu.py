@@ -23,16 +23,17 @@ def small_base(layers=3):
     return {**WL.BASE, "num_hidden_layers": layers}
 
 
+@pytest.mark.parametrize("kernel", [0, 1])
 @pytest.mark.parametrize("half_window", [-1, 64, 8])
-def test_attention_varlen_matches_oracle(half_window):
+def test_attention_varlen_matches_oracle(half_window, kernel):
     b = backend()
     rng = np.random.default_rng(5)
     H, nh = 256, 4
-    lens = np.array([1, 3, 63, 64, 65, 129, 257])
+    lens = np.array([1, 3, 63, 64, 65, 127, 128, 129, 257, 300])
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     T = int(cu[-1])
     qkv = rng.standard_normal((T, 3 * H)).astype(np.float16)
-    att = to_f32(b.read(attention_varlen(b, b.fromHost(HostTensor("f16", qkv.shape, qkv)), cu, half_window, 0.125)))
+    att = to_f32(b.read(attention_varlen(b, b.fromHost(HostTensor("f16", qkv.shape, qkv)), cu, half_window, 0.125, kernel)))
     for s, L in enumerate(lens):
         seg = qkv[cu[s]:cu[s + 1]].astype(np.float32).reshape(L, 3, nh, 64).transpose(1, 2, 0, 3)
         mask = None
