@@ -128,6 +128,22 @@ int lc_quantized_embedding(lc_tensor* out, lc_tensor w, lc_tensor scales, lc_ten
 /* Dequantized matrix [N, K] in the scales' dtype (each value fl(q·s + b) rounded once). */
 int lc_dequantize(lc_tensor* out, lc_tensor w, lc_tensor scales, lc_tensor biases,
                   int bits, int group_size, int mode);
+/*
+ * No counterpart in the reference. quantizedLinear for callers that cannot
+ * allocate device memory (a host whose device memory belongs to another
+ * framework's allocator, or a hot path that must not call cudaMalloc/cudaFree,
+ * which can synchronise the device): y[m, n] = x[m, k] · dequant(w)ᵀ (+ bias)
+ * on raw device pointers, with the dequantised weight in a fixed 8 MiB scratch
+ * array that every GPU loading the library reserves (n·k <= 4,194,304).
+ * x/y f16 or bf16 (dtype 1/2), k >= 64 and k % 8 == 0, 16-byte aligned
+ * pointers; w/scales/biases as lc_from_host_quantized stores them (sb_dtype);
+ * bias optional ([n], bias_dtype). Allocates nothing. The first call on each
+ * device resolves the scratch address; make it before any stream capture.
+ * Calls share the scratch: calls that overlap on the GPU race.
+ */
+int lc_quantized_linear_noalloc(void* y, const void* x, int64_t m, int64_t k, int dtype, const uint8_t* w, const void* scales,
+                                const void* biases, int64_t n, int bits, int group_size, int mode, int sb_dtype,
+                                const void* bias, int bias_dtype, uint64_t stream);
 
 /* ---- optional general numerics (index.ts:265-316) ---- */
 int lc_equal(lc_tensor* out, lc_tensor a, lc_tensor b);

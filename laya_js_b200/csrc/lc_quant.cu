@@ -243,3 +243,67 @@ int lc_quantized_linear(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor sh
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------- allocation-free quantized linear
+//
+// lc_quantized_linear_noalloc is for callers that cannot allocate device memory
+// themselves: for example a host whose device memory is all handed to another
+// framework's caching allocator, or a serving loop that must not call
+// cudaMalloc / cudaFree (they can synchronise the whole device) on its hot
+// path. It computes the same y = x · dequant(w)ᵀ (+ bias) as
+// lc_quantized_linear's large-M path (dequantise once, then the tcgen05 GEMM),
+// but the dequantised weight goes into the fixed scratch array below instead of
+// an allocation; the caller passes device pointers for every input and output.
+//
+// The scratch is a file-scope __device__ array of kNoAllocScratchBytes: every
+// GPU that loads this library reserves it until the process exits. Host code
+// cannot use the array's name as a device address, so the first call on each
+// device looks the address up with cudaGetSymbolAddress (with that device
+// current) and keeps it; make that first call before any stream capture. All
+// calls share the one array and it keeps the last call's contents: each call
+// overwrites exactly the N·K values it reads, so nothing needs clearing, but
+// calls that overlap on the GPU (different streams, no ordering between them)
+// race on it.
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[(size_t)8 << 20];
+static constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // room for an 4M-element f16/bf16 weight
+
+namespace {
+void* noalloc_scratch_for_current_device() {
+  static void* ptrs[128] = {};
+  int dev = -1;
+  CUDA_OK(cudaGetDevice(&dev));
+  LC_CHECK(dev >= 0 && dev < 128, "quantizedLinearNoalloc: device ordinal out of range");
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    CUDA_OK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    LC_CHECK(p != nullptr, "quantizedLinearNoalloc: cudaGetSymbolAddress returned no address for the scratch array");
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+}  // namespace
+
+extern "C" int lc_quantized_linear_noalloc(void* y, const void* x, int64_t m, int64_t k, int dtype, const uint8_t* w, const void* scales,
+                                           const void* biases, int64_t n, int bits, int group_size, int mode, int sb_dtype,
+                                           const void* bias, int bias_dtype, uint64_t stream) {
+  LC_API_BEGIN
+  validate(n, k, bits, group_size, mode);
+  LC_CHECK(dtype == LC_F16 || dtype == LC_BF16, "quantizedLinearNoalloc: x and y must be f16 or bf16");
+  LC_CHECK(sb_dtype == LC_F32 || sb_dtype == LC_F16 || sb_dtype == LC_BF16, "quantizedLinearNoalloc: scales/biases must be f32, f16 or bf16");
+  LC_CHECK(mode == 1 ? biases != nullptr : biases == nullptr, "quantizedLinearNoalloc: biases are required for affine and not allowed for symmetric");
+  LC_CHECK(x && y && w && scales && m > 0, "quantizedLinearNoalloc: null pointer or empty input");
+  LC_CHECK(k >= 64 && k % 8 == 0, "quantizedLinearNoalloc: in features must be a multiple of 8, at least 64");
+  const size_t need = (size_t)n * (size_t)k * 2;
+  LC_CHECK(need <= kNoAllocScratchBytes,
+           "quantizedLinearNoalloc: the dequantised weight needs " + std::to_string(need) + " bytes, above the " +
+               std::to_string(kNoAllocScratchBytes) + "-byte scratch (out x in <= " + std::to_string(kNoAllocScratchBytes / 2) + ")");
+  void* scratch = noalloc_scratch_for_current_device();
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  k_dequant<<<blocks_for(n * k, 256), 256, 0, st>>>(w, (const char*)scales, (const char*)biases, sb_dtype, bits, group_size, mode, n, k,
+                                                    (char*)scratch, dtype);
+  LC_LAUNCHED(1);
+  bool ok = gemm_raw(x, m, k, scratch, n, bias, bias_dtype, y, n, dtype, GemmEpilogue{}, st);
+  LC_CHECK(ok, "quantizedLinearNoalloc: shape or alignment not supported by the tensor-core GEMM (16-byte aligned pointers needed)");
+  LC_API_END
+}
