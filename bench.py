@@ -19,7 +19,9 @@ Keys beyond the driver's contract:
   cpu_baseline  the numpy oracle (float64) on a bounded sample, all cores;
   int4       configs[3]-style 4-bit affine g64 weights (batch 512, lengths
              U[64, 1024]) tokens/s on the same GPU;
-  p50_latency_ms  configs[0] (batch 1, seq 128) end-to-end latency.
+  p50_latency_ms  configs[0] (batch 1, seq 128) end-to-end latency;
+  p50_latency_graph_ms  the same through a captured CUDA graph
+             (lc_encoder_graph_run).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -238,7 +240,6 @@ def main() -> None:
     prof = E.profile_read(fused)
     E.set_profiling(fused, False)
     ms = max_over_ranks(ms_local)
-    tokens_all = max_over_ranks(0) if False else None
     tok_total = T * world  # every rank's batch has its own lengths; sum them exactly
     if dist is not None:
         t = torch.tensor([T], device=f"cuda:{local}", dtype=torch.float64)
@@ -288,6 +289,7 @@ def main() -> None:
     if rank == 0 and not args.no_extras:
         try:
             line["p50_latency_ms"] = latency_cfg0(b, fused, thw, thb, cfg_json)
+            line["p50_latency_graph_ms"] = latency_cfg0(b, fused, thw, thb, cfg_json, graph=True)
         except Exception as ex:  # noqa: BLE001
             line["p50_latency_ms"] = f"failed: {ex}"
         try:
@@ -316,18 +318,23 @@ def b_stream(b) -> int:
     return s.value
 
 
-def latency_cfg0(b, fused, thw, thb, cfg_json) -> float:
-    """batch 1, seq 128 (CLS ... SEP), p50 over 50 end-to-end calls."""
+def latency_cfg0(b, fused, thw, thb, cfg_json, graph: bool = False) -> float:
+    """batch 1, seq 128 (CLS ... SEP), p50 over 50 end-to-end calls
+    (host ids in, host probabilities out), eager or as a captured CUDA graph."""
     from laya_js_b200 import workloads as WL
     ids, cu = WL.token_batch(cfg_json, np.array([128]), seed=SEED + 5)
     out = np.empty((1, thw.shape[0]), np.float32)
+    g = fused.graph(cu, thw, thb) if graph else None
+    call = (lambda: g.run(ids, out=out)) if graph else (lambda: fused.forward_host(ids, cu, thw, thb, out=out))
     for _ in range(5):
-        fused.forward_host(ids, cu, thw, thb, out=out)
+        call()
     ts = []
     for _ in range(50):
         t0 = time.perf_counter()
-        fused.forward_host(ids, cu, thw, thb, out=out)
+        call()
         ts.append((time.perf_counter() - t0) * 1e3)
+    if g is not None:
+        g.free()
     return statistics.median(ts)
 
 

@@ -69,6 +69,21 @@ int lc_encoder_forward_host(uint64_t enc, const int32_t* ids_host, const int32_t
                             float* probs_host);
 
 /*
+ * Replay of lc_encoder_forward_host for one fixed batch shape as a CUDA
+ * graph (no counterpart in the reference, whose TypeScript host issues every
+ * op itself). create captures, for the given cu_seqlens and head, the copy of
+ * the ids into the device, the whole forward and the copy of the
+ * probabilities out, with workspace, metadata and I/O buffers owned by the
+ * graph. run takes ids (host, T = cu_seqlens[nseq] values), replays the graph
+ * and writes probs (host, nseq x C floats); it returns after the result is on
+ * the host. Freeing the encoder frees its graphs. Per-kernel tracing does not
+ * apply to replays.
+ */
+int lc_encoder_graph_create(uint64_t* graph, uint64_t enc, const int32_t* cu_seqlens, int nseq, lc_tensor head_w, lc_tensor head_b);
+int lc_encoder_graph_run(uint64_t graph, const int32_t* ids_host, float* probs_host);
+int lc_encoder_graph_free(uint64_t graph);
+
+/*
  * Per-kernel-class device timing of the forwards that follow (tracing):
  * when enabled, every forward records CUDA events around its kernels on the
  * library stream. lc_encoder_profile_read returns, per class, the summed

@@ -334,6 +334,18 @@ void* grow_pinned(void*& p, size_t& have, size_t want) {
   return p;
 }
 
+void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const int32_t* cu_dev, const int4* tiles_dev, int ntiles,
+                 const int32_t* ids_dev, void* hidden_out, const LcTensor* head_w, const LcTensor* head_b, float* probs_dev,
+                 cudaStream_t st);
+
+// Frees the CUDA graphs captured on an encoder (they reference its weights).
+void free_graphs_of(Encoder* e);
+
+// Workspace bytes of one forward over T tokens (x | h | qkv | pos).
+size_t workspace_bytes(const lc_encoder_config& c, int64_t T) {
+  return (size_t)T * c.hidden_size * 2 * 5 + (size_t)T * 4;
+}
+
 // The forward on device ids (i32 [T]) and host cu_seqlens.
 void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, LcTensor* hidden_out, const LcTensor* head_w,
              const LcTensor* head_b, float* probs_dev) {
@@ -372,6 +384,25 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
   CUDA_OK(cudaMemcpyAsync(ws + off_meta, e->stage, meta, cudaMemcpyHostToDevice, st));
   if (!e->stage_ev) CUDA_OK(cudaEventCreateWithFlags(&e->stage_ev, cudaEventDisableTiming));
   CUDA_OK(cudaEventRecord(e->stage_ev, st));
+  (void)x, (void)h, (void)qkv, (void)pos;
+  run_kernels(e, ws, T, nseq, maxlen, cu_dev, tiles_dev, (int)tiles.size(), ids_dev, hidden_out ? hidden_out->data() : nullptr, head_w,
+              head_b, probs_dev, st);
+}
+
+// The kernel sequence of one forward on prepared buffers: ws = x [T,H] | h [T,H] |
+// qkv [T,3H] | pos [T]; cu_dev / tiles_dev on the device. Enqueues work only
+// (no host synchronisation, no allocation once the encoder is warm), so a
+// stream capture of it replays the forward.
+void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const int32_t* cu_dev, const int4* tiles_dev, int ntiles,
+                 const int32_t* ids_dev, void* hidden_out, const LcTensor* head_w, const LcTensor* head_b, float* probs_dev,
+                 cudaStream_t st) {
+  const lc_encoder_config& c = e->cfg;
+  const int H = c.hidden_size, I = c.intermediate_size;
+  const size_t esz = 2;
+  void* x = ws;
+  void* h = ws + (size_t)T * H * esz;
+  void* qkv = ws + (size_t)2 * T * H * esz;
+  int32_t* pos = (int32_t*)(ws + (size_t)5 * T * H * esz);
   k_positions<<<std::min(nseq, 4096), 256, 0, st>>>(cu_dev, nseq, pos);
   LC_LAUNCHED(1);
 
@@ -416,7 +447,7 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
     // attention -> h (h is free again once the Wqkv GEMM has read it)
     {
       Prof p(e, 1);
-      attention_varlen_tc(qkv, h, tiles_dev, (int)tiles.size(), T, H, L.kind == 0 ? -1 : c.local_attention / 2, scale, c.dtype, st);
+      attention_varlen_tc(qkv, h, tiles_dev, ntiles, T, H, L.kind == 0 ? -1 : c.local_attention / 2, scale, c.dtype, st);
     }
     GemmEpilogue er;
     er.kind = EPI_RESIDUAL;
@@ -432,7 +463,7 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
     run_gemm(e, L.Wi, h, T, qkv, I, eg, I, 5);
     run_gemm(e, L.WoMlp, qkv, T, x, H, er, H, 6);
   }
-  void* fin = hidden_out ? hidden_out->data() : h;
+  void* fin = hidden_out ? hidden_out : h;
   {
     Prof pf(e, 2);
     layernorm_raw(x, (const float*)e->final_norm->data(), fin, T, H, (float)c.norm_eps, c.dtype, st);
@@ -531,6 +562,7 @@ int lc_encoder_free(uint64_t h) {
   Encoder* e = check_enc(h);
   encoders().erase(e);
   CUDA_OK(cudaStreamSynchronize(stream()));
+  free_graphs_of(e);
   for (auto* t : e->owned) release(t);
   if (e->deq) release(e->deq);
   if (e->ws) dfree(e->ws);
@@ -628,6 +660,145 @@ int lc_encoder_forward_host(uint64_t h, const int32_t* ids_host, const int32_t* 
   memcpy(probs_host, e->probs_stage, (size_t)nseq * C * 4);
   std::string err = take_device_errors();
   LC_CHECK(err.empty(), err);
+  LC_API_END
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------- CUDA-graph replay
+// One fixed batch shape (cu_seqlens) captured as a graph: H2D of the ids from
+// the graph's pinned buffer, the whole forward, D2H of the probabilities. The
+// graph owns its workspace, metadata and I/O buffers, so eager forwards of the
+// same encoder can run in between.
+
+namespace {
+struct EncGraph {
+  Encoder* e = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  char* ws = nullptr;
+  char* meta = nullptr;
+  int32_t* ids_dev = nullptr;
+  float* probs_dev = nullptr;
+  void* ids_pin = nullptr;
+  void* probs_pin = nullptr;
+  int64_t T = 0;
+  int nseq = 0, C = 0;
+};
+std::unordered_set<EncGraph*>& graphs() {
+  static std::unordered_set<EncGraph*> s;
+  return s;
+}
+void free_graph(EncGraph* g) {
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  cudaStreamSynchronize(stream());
+  for (void* p : {(void*)g->ws, (void*)g->meta, (void*)g->ids_dev, (void*)g->probs_dev}) dfree(p);
+  if (g->ids_pin) cudaFreeHost(g->ids_pin);
+  if (g->probs_pin) cudaFreeHost(g->probs_pin);
+  delete g;
+}
+
+void free_graphs_of(Encoder* e) {
+  for (auto it = graphs().begin(); it != graphs().end();) {
+    if ((*it)->e == e) {
+      free_graph(*it);
+      it = graphs().erase(it);
+    } else {
+      ++it;
+    }
+  }
+}
+}  // namespace
+
+extern "C" {
+
+int lc_encoder_graph_create(uint64_t* out, uint64_t h, const int32_t* cu, int nseq, lc_tensor hwh, lc_tensor hbh) {
+  LC_API_BEGIN
+  Encoder* e = check_enc(h);
+  LcTensor* hw = check(hwh, "encoder graph head_w");
+  LcTensor* hb = hbh ? check(hbh, "encoder graph head_b") : nullptr;
+  check_head(e, hw, hb);
+  LC_CHECK(nseq > 0 && cu[0] == 0, "encoder graph: cu_seqlens must start at 0");
+  int maxlen = 0;
+  for (int s = 0; s < nseq; s++) {
+    LC_CHECK(cu[s + 1] >= cu[s], "encoder graph: cu_seqlens must be non-decreasing");
+    maxlen = std::max(maxlen, cu[s + 1] - cu[s]);
+  }
+  LC_CHECK(cu[nseq] > 0 && maxlen <= 8192, "encoder graph: 1..8192 tokens per sequence");
+  auto g = std::make_unique<EncGraph>();
+  g->e = e;
+  g->T = cu[nseq];
+  g->nseq = nseq;
+  g->C = (int)hw->shape[0];
+  cudaStream_t st = stream();
+  std::vector<int4> tiles = attention_tiles_tc(cu, nseq);
+  size_t cu_bytes = ((size_t)(nseq + 1) * 4 + 15) & ~(size_t)15;
+  size_t meta = cu_bytes + tiles.size() * sizeof(int4);
+  try {
+    g->ws = (char*)dmalloc(workspace_bytes(e->cfg, g->T));
+    g->meta = (char*)dmalloc(meta);
+    g->ids_dev = (int32_t*)dmalloc((size_t)g->T * 4);
+    g->probs_dev = (float*)dmalloc((size_t)nseq * g->C * 4);
+    CUDA_OK(cudaHostAlloc(&g->ids_pin, (size_t)g->T * 4, cudaHostAllocDefault));
+    CUDA_OK(cudaHostAlloc(&g->probs_pin, (size_t)nseq * g->C * 4, cudaHostAllocDefault));
+    std::vector<char> hmeta(meta, 0);
+    memcpy(hmeta.data(), cu, (size_t)(nseq + 1) * 4);
+    memcpy(hmeta.data() + cu_bytes, tiles.data(), tiles.size() * sizeof(int4));
+    CUDA_OK(cudaMemcpyAsync(g->meta, hmeta.data(), meta, cudaMemcpyHostToDevice, st));
+    CUDA_OK(cudaMemsetAsync(g->ids_dev, 0, (size_t)g->T * 4, st));
+    memset(g->ids_pin, 0, (size_t)g->T * 4);
+    const int32_t* cu_dev = (const int32_t*)g->meta;
+    const int4* tiles_dev = (const int4*)(g->meta + cu_bytes);
+    // warm-up outside the capture: tensor maps, kernel attributes, dequant scratch
+    const bool prof = e->prof;
+    e->prof = false;
+    run_kernels(e, g->ws, g->T, nseq, maxlen, cu_dev, tiles_dev, (int)tiles.size(), g->ids_dev, nullptr, hw, hb, g->probs_dev, st);
+    CUDA_OK(cudaStreamSynchronize(st));
+    CUDA_OK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    try {
+      CUDA_OK(cudaMemcpyAsync(g->ids_dev, g->ids_pin, (size_t)g->T * 4, cudaMemcpyHostToDevice, st));
+      run_kernels(e, g->ws, g->T, nseq, maxlen, cu_dev, tiles_dev, (int)tiles.size(), g->ids_dev, nullptr, hw, hb, g->probs_dev, st);
+      CUDA_OK(cudaMemcpyAsync(g->probs_pin, g->probs_dev, (size_t)nseq * g->C * 4, cudaMemcpyDeviceToHost, st));
+    } catch (...) {
+      cudaGraph_t dead = nullptr;
+      cudaStreamEndCapture(st, &dead);
+      if (dead) cudaGraphDestroy(dead);
+      e->prof = prof;
+      throw;
+    }
+    CUDA_OK(cudaStreamEndCapture(st, &g->graph));
+    e->prof = prof;
+    CUDA_OK(cudaGraphInstantiate(&g->exec, g->graph, 0));
+  } catch (...) {
+    free_graph(g.release());
+    throw;
+  }
+  EncGraph* raw = g.release();
+  graphs().insert(raw);
+  *out = reinterpret_cast<uint64_t>(raw);
+  LC_API_END
+}
+
+int lc_encoder_graph_run(uint64_t gh, const int32_t* ids_host, float* probs_host) {
+  LC_API_BEGIN
+  EncGraph* g = reinterpret_cast<EncGraph*>(gh);
+  LC_CHECK(gh && graphs().count(g), "encoder graph: invalid or freed graph handle");
+  memcpy(g->ids_pin, ids_host, (size_t)g->T * 4);
+  CUDA_OK(cudaGraphLaunch(g->exec, stream()));
+  CUDA_OK(cudaStreamSynchronize(stream()));
+  memcpy(probs_host, g->probs_pin, (size_t)g->nseq * g->C * 4);
+  std::string err = take_device_errors();
+  LC_CHECK(err.empty(), err);
+  LC_API_END
+}
+
+int lc_encoder_graph_free(uint64_t gh) {
+  LC_API_BEGIN
+  EncGraph* g = reinterpret_cast<EncGraph*>(gh);
+  LC_CHECK(gh && graphs().count(g), "encoder graph: invalid or freed graph handle");
+  graphs().erase(g);
+  free_graph(g);
   LC_API_END
 }
 

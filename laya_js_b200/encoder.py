@@ -91,10 +91,43 @@ class FusedEncoder:
                   C.c_uint64(self.backend._h(head_b)), out.ctypes.data_as(C.POINTER(C.c_float)))
         return out
 
+    def graph(self, cu_seqlens: np.ndarray, head_w, head_b=None) -> "EncoderGraph":
+        """Capture forward_host for this fixed batch shape as a CUDA graph."""
+        return EncoderGraph(self, cu_seqlens, head_w, head_b)
+
     def free(self) -> None:
         if self.handle:
             _lib.call("lc_encoder_free", C.c_uint64(self.handle))
             self.handle = 0
+
+
+class EncoderGraph:
+    """lc_encoder_graph_*: forward_host replayed as one CUDA graph launch for a
+    fixed cu_seqlens and head; ``run(ids)`` -> probabilities [nseq, C] (f32)."""
+
+    def __init__(self, fused: FusedEncoder, cu_seqlens: np.ndarray, head_w, head_b=None):
+        cu = np.ascontiguousarray(cu_seqlens, np.int32)
+        self.nseq, self.tokens, self.classes = len(cu) - 1, int(cu[-1]), int(head_w.shape[0])
+        self.fused = fused
+        h = C.c_uint64()
+        _lib.call("lc_encoder_graph_create", C.byref(h), C.c_uint64(fused.handle), cu.ctypes.data_as(C.POINTER(C.c_int32)),
+                  self.nseq, C.c_uint64(fused.backend._h(head_w)), C.c_uint64(fused.backend._h(head_b)))
+        self.handle = h.value
+
+    def run(self, ids: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32)
+        if ids.shape != (self.tokens,):
+            raise ValueError(f"encoder graph: expected {self.tokens} ids, got shape {ids.shape}")
+        if out is None:
+            out = np.empty((self.nseq, self.classes), np.float32)
+        _lib.call("lc_encoder_graph_run", C.c_uint64(self.handle), ids.ctypes.data_as(C.POINTER(C.c_int32)),
+                  out.ctypes.data_as(C.POINTER(C.c_float)))
+        return out
+
+    def free(self) -> None:
+        if self.handle and self.fused.handle:
+            _lib.call("lc_encoder_graph_free", C.c_uint64(self.handle))
+        self.handle = 0
 
 
 def attention_varlen(backend, qkv, cu_seqlens: np.ndarray, half_window: int, scale: float, kernel: int = 0):

@@ -133,3 +133,34 @@ def test_fused_encoder_deterministic_and_leak_free():
     assert b.stats()["live_tensors"] == base
     fused.free()
     enc.dispose()
+
+
+@pytest.mark.parametrize("quant_bits", [0, 4])
+def test_encoder_graph_replays_forward_host(quant_bits):
+    """A captured graph gives the eager forward_host's probabilities bit for bit,
+    for new ids on every replay, with eager forwards of other shapes in between."""
+    cfg_json = small_base(2)
+    b, W, cfg, enc = _model(cfg_json, quant_bits)
+    lens = np.array([33, 500, 1, 129, 64])
+    ids, cu = WL.token_batch(cfg_json, lens, seed=9)
+    hw, hb = WL.classifier(cfg_json, 5, seed=2)
+    hw = (hw.astype(np.float32) * 3).astype(np.float16)
+    thw, thb = b.fromHost(HostTensor("f16", hw.shape, hw)), b.fromHost(HostTensor("f32", hb.shape, hb))
+    fused = FusedEncoder(enc)
+    g = fused.graph(cu, thw, thb)
+    other_ids, other_cu = WL.token_batch(cfg_json, np.array([700, 9]), seed=1)
+    rng = np.random.default_rng(5)
+    for it in range(3):
+        cur = ids if it == 0 else rng.integers(0, cfg_json["vocab_size"], ids.shape, dtype=np.int32)
+        want = fused.forward_host(cur, cu, thw, thb)
+        got = g.run(cur)
+        assert np.array_equal(got, want), f"replay {it}: max diff {np.abs(got - want).max()}"
+        fused.forward_host(other_ids, other_cu, thw, thb)  # grows the eager workspace between replays
+    with pytest.raises(ValueError):
+        g.run(ids[:-1])
+    g.free()
+    # freeing the encoder frees the graphs captured on it
+    g2 = fused.graph(cu, thw, thb)
+    fused.free()
+    g2.free()  # no-op after the encoder is gone
+    enc.dispose()
