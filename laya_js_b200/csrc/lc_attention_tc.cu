@@ -3,27 +3,39 @@
 // (packages/modernbert/src/index.ts:348-352: sdpa with the masks of
 // attentionMasks, index.ts:240-259) computed without masks or padding.
 //
-// One CTA = 128 query rows of one (sequence, head); key blocks of 64.
-//   warp 0      TMA producer: Q once, K and V blocks into a 2-stage ring
-//               (128 x 64 tiles of the fused [T, 3H] projection, 128-byte swizzle);
+// Persistent: two CTAs per SM, each walking the work list (128-query-row tile
+// of one sequence x head; tiles longest sequence first) with a stride of the
+// grid. Key blocks of 64. Roles:
+//   warp 0      TMA producer: Q of each work item into one of two Q buffers
+//               (the next item's Q loads while the current one runs), K and V
+//               blocks into an NST-stage ring that runs on across items
+//               (128 x 64 / 64 x 64 tiles of the fused [T, 3H] projection,
+//               128-byte swizzle);
 //   warp 1      TMEM owner and single-thread MMA issuer:
 //                 S_j = Q·K_jᵀ  (M=128, N=64, K=64; A, B from shared memory)
 //                 O  += P_j·V_j (M=128, N=64, K=64; A = P from TMEM, B = V
 //                                from shared memory, MN-major)
 //               S is double-buffered in TMEM (columns 0-63 / 64-127), so
-//               S_{j+1} runs while the softmax works on S_j; O lives at
-//               columns 128-191 (256 columns per CTA: two CTAs share an SM).
+//               S_{j+1} runs while the softmax works on S_j, also across work
+//               items; O lives at columns 128-191 (256 columns per CTA).
 //   warps 2-5   softmax: thread r owns query row r (= TMEM lane r), so the
 //               row max / sum need no cross-thread reduction. It loads S_j,
 //               masks (key in the sequence, |i − j| <= window/2 for sliding
-//               layers), writes P_j = exp2(S·scale·log2e − m) as f16 over the
-//               first 64 columns of S_j's buffer, and — only when the running
-//               max grew — rescales O in TMEM once P_{j−1}·V_{j−1} is done.
-//               At the end it normalises O by the row sum and stores [T, H].
-// Every mbarrier wait is bounded (2 s); a timeout sets g_attn_err and unwinds.
+//               layers), writes P_j = exp2(S·scale·log2e − m) as 16-bit values
+//               packed two per column over the first 32 columns of S_j's
+//               buffer, and — only when the running max grew by more than
+//               2^8 — rescales O in TMEM once P_{j−1}·V_{j−1} is done. At the
+//               end of an item it normalises O by the row sum and stores
+//               [T, H]; the next item's first P_0·V_0 (which overwrites O)
+//               waits for that through the P-ready barrier.
+// Every barrier counts phases with per-role counters that run across work
+// items; every mbarrier wait is bounded (2 s); a timeout sets g_attn_err and
+// all roles unwind.
 #include "lc_api.h"
 #include "lc_gemm.h"
 #include "lc_sm100.cuh"
+
+#include <algorithm>
 
 __device__ unsigned int g_attn_err;
 
@@ -35,8 +47,10 @@ constexpr int TQ = 128, TK = 64, HD = 64;
 constexpr uint32_t TILE_BYTES = TQ * HD * 2;  // the 128 x 64 Q tile
 constexpr uint32_t KV_BYTES = TK * HD * 2;    // one 64 x 64 K or V tile
 constexpr uint32_t TMEM_COLS = 256;           // S double buffer (2 x 64) + O (64): two CTAs fit an SM
-constexpr int NST = 5;                        // K/V ring depth: covers the TMA latency of several blocks
-constexpr size_t ATTN_SMEM = TILE_BYTES + 2 * NST * KV_BYTES + 1024 + 256;
+constexpr int NS = 2;                         // S buffers
+constexpr uint32_t O_COL = NS * TK;
+constexpr int NST = 4;                        // K/V ring depth
+constexpr size_t ATTN_SMEM = 2 * TILE_BYTES + 2 * NST * KV_BYTES + 1024 + 256;
 
 struct AttnTcArgs {
   const int4* tiles;  // (first token of the sequence, its length, first query row (multiple of 128), 0)
@@ -44,12 +58,84 @@ struct AttnTcArgs {
   int H;
   int half_window;  // < 0: global attention
   float scale_log2;
+  int heads;
+  int nwork;  // tiles x heads
+};
+
+struct Work {
+  int tok0, L, q0, h, kv_lo, nb;
+};
+
+template <bool LOCAL>
+__device__ __forceinline__ Work decode(const AttnTcArgs& a, int4 t, int w) {
+  Work r;
+  r.tok0 = t.x;
+  r.L = t.y;
+  r.q0 = t.z;
+  r.h = w % a.heads;
+  int lo = 0, hi = r.L;
+  if (LOCAL) {
+    lo = max(0, r.q0 - a.half_window);
+    hi = min(r.L, r.q0 + TQ + a.half_window);
+  }
+  r.kv_lo = (lo / TK) * TK;
+  r.nb = (hi - r.kv_lo + TK - 1) / TK;  // >= 1: q0 < L
+  return r;
+}
+
+// One role's walk over this CTA's work items (w = blockIdx.x + t * gridDim.x);
+// the tile entry of the following item is loaded one item ahead.
+template <bool LOCAL>
+struct Items {
+  int w, t;
+  Work cur;
+  int4 next;
+  __device__ __forceinline__ void start(const AttnTcArgs& a) {
+    w = blockIdx.x;
+    t = 0;
+    if (w < a.nwork) cur = decode<LOCAL>(a, a.tiles[w / a.heads], w);
+    const int wn = w + (int)gridDim.x;
+    if (wn < a.nwork) next = a.tiles[wn / a.heads];
+  }
+  __device__ __forceinline__ bool valid(const AttnTcArgs& a) const { return w < a.nwork; }
+  __device__ __forceinline__ void step(const AttnTcArgs& a) {
+    w += gridDim.x;
+    t++;
+    if (w < a.nwork) cur = decode<LOCAL>(a, next, w);
+    const int wn = w + (int)gridDim.x;
+    if (wn < a.nwork) next = a.tiles[wn / a.heads];
+  }
 };
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// Packed pair arithmetic (one instruction for two lanes' worth of f32 work;
+// each element rounds exactly as fmaf / __fadd_rn).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
 }
 
 template <typename T>
@@ -68,42 +154,38 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
                                                     const __grid_constant__ AttnTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + TILE_BYTES;      // NST stages
+  uint8_t* sQ = smem;                 // 2 buffers
+  uint8_t* sK = sQ + 2 * TILE_BYTES;  // NST stages
   uint8_t* sV = sK + NST * KV_BYTES;  // NST stages
   uint64_t* bars = (uint64_t*)(sV + NST * KV_BYTES);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;          // [NST]
-  uint64_t* kv_empty = kv_full + NST;    // [NST]
-  uint64_t* s_full = kv_empty + NST;     // [2]
-  uint64_t* p_ready = s_full + 2;        // [2]
-  // P_j·V_j commits to o_done[j & 1]: with two barriers a waiter is never more
-  // than one phase behind (S_j complete implies P_{j-2}·V_{j-2} complete).
-  uint64_t* o_done = p_ready + 2;  // [2]
+  uint64_t* q_full = bars;            // [2]
+  uint64_t* q_empty = q_full + 2;     // [2]
+  uint64_t* kv_full = q_empty + 2;    // [NST]
+  uint64_t* kv_empty = kv_full + NST; // [NST]
+  uint64_t* s_full = kv_empty + NST;  // [NS]
+  uint64_t* p_ready = s_full + NS;    // [NS]
+  // P_g·V_g commits to o_done[g & 1]: a softmax warp waiting for block g is
+  // never more than one phase behind (P_{g+2}·V_{g+2} needs P_{g+2}, which
+  // that warp has not produced yet).
+  uint64_t* o_done = p_ready + NS;  // [2]
   uint32_t* tmem_slot = (uint32_t*)(o_done + 2);
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int4 tile = a.tiles[blockIdx.x];
-  const int tok0 = tile.x, L = tile.y, q0 = tile.z, h = blockIdx.y;
-  int kv_lo = 0, kv_hi = L;
-  if (LOCAL) {
-    kv_lo = max(0, q0 - a.half_window);
-    kv_hi = min(L, q0 + TQ + a.half_window);
-  }
-  kv_lo = (kv_lo / TK) * TK;
-  const int nb = (kv_hi - kv_lo + TK - 1) / TK;  // >= 1: q0 < L
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&o_done[i], 1);
+    }
+    for (int i = 0; i < NS; i++) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_ready[i], 4);
+    }
     for (int i = 0; i < NST; i++) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-    }
-    for (int i = 0; i < 2; i++) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_ready[i], 4);
-      mbar_init(&o_done[i], 1);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -117,184 +199,249 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t o_col = 2 * TK;
 
   if (warp == 0) {
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmQ) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmKV) : "memory");
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_2d(sQ, &tmQ, q_full, h * HD, tok0 + q0);
-      int issued[NST];
-      uint32_t iph[NST];
+      int issued[NST], q_issued[2] = {0, 0};
+      uint32_t iph[NST], q_ph[2] = {0, 0};
       for (int s = 0; s < NST; s++) issued[s] = 0, iph[s] = 0;
-      for (int j = 0; j < nb; j++) {
-        const int st = j % NST;
-        const uint32_t ph = (j / NST) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort, &g_attn_err)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * KV_BYTES);
-        const int row = tok0 + kv_lo + j * TK;
-        tma_load_2d(sK + st * KV_BYTES, &tmKV, &kv_full[st], a.H + h * HD, row);
-        tma_load_2d(sV + st * KV_BYTES, &tmKV, &kv_full[st], 2 * a.H + h * HD, row);
-        issued[st] = 1;
-        iph[st] = ph;
+      uint32_t kv_it = 0;
+      bool ok = true;
+      Items<LOCAL> it;
+      for (it.start(a); ok && it.valid(a); it.step(a)) {
+        const Work& wk = it.cur;
+        const int t = it.t, qb = t & 1;
+        if (!mbar_wait(&q_empty[qb], ((t >> 1) & 1) ^ 1, abort, &g_attn_err)) break;
+        mbar_arrive_expect_tx(&q_full[qb], TILE_BYTES);
+        tma_load_2d(sQ + qb * TILE_BYTES, &tmQ, &q_full[qb], wk.h * HD, wk.tok0 + wk.q0);
+        q_issued[qb] = 1;
+        q_ph[qb] = (t >> 1) & 1;
+        for (int j = 0; j < wk.nb; j++, kv_it++) {
+          const int st = kv_it % NST;
+          const uint32_t ph = (kv_it / NST) & 1;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1, abort, &g_attn_err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * KV_BYTES);
+          const int row = wk.tok0 + wk.kv_lo + j * TK;
+          tma_load_2d(sK + st * KV_BYTES, &tmKV, &kv_full[st], a.H + wk.h * HD, row);
+          tma_load_2d(sV + st * KV_BYTES, &tmKV, &kv_full[st], 2 * a.H + wk.h * HD, row);
+          issued[st] = 1;
+          iph[st] = ph;
+        }
       }
       // drain: every copy issued here has landed before the CTA can exit
-      uint64_t t0 = gtimer();
-      while (!mbar_try_wait(q_full, 0) && gtimer() - t0 < kWaitNs) {}
+      for (int qb = 0; qb < 2; qb++)
+        if (q_issued[qb]) {
+          const uint64_t t0 = gtimer();
+          while (!mbar_try_wait(&q_full[qb], q_ph[qb]) && gtimer() - t0 < kWaitNs) {}
+        }
       for (int s = 0; s < NST; s++)
         if (issued[s]) {
-          t0 = gtimer();
+          const uint64_t t0 = gtimer();
           while (!mbar_try_wait(&kv_full[s], iph[s]) && gtimer() - t0 < kWaitNs) {}
         }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // Issue order over the CTA's stream of key blocks g = 0, 1, ... (across
+      // work items):  S_0 .. S_{NS-1}, then for each g: [P_g ready] P_g·V_g,
+      // S_{g+NS}. S_{g+NS} reuses the buffer of S_g, whose P the P_g·V_g
+      // issued just before reads first (tcgen05 MMAs of one thread run in
+      // issue order); the softmax has finished with S_g (P_g ready).
       const uint32_t id_s = idesc_f16<T, TK>();
       const uint32_t id_pv = idesc_f16<T, HD, 128, true>();
-      bool ok = mbar_wait(q_full, 0, abort, &g_attn_err);
-      int pv_issued = 0;
-      for (int j = 0; ok && j <= nb; j++) {
-        if (j < nb) {
-          const int st = j % NST;
-          if (!mbar_wait(&kv_full[st], (j / NST) & 1, abort, &g_attn_err)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t d = tmem + (uint32_t)((j & 1) * TK);
-          const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + st * KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; kk++) tc_mma(d, sdesc_sw128(qa + kk * 32), sdesc_sw128(ka + kk * 32), id_s, kk > 0 ? 1u : 0u);
-          tc_commit(&s_full[j & 1]);
+      const uint64_t dq0 = sdesc_sw128(smem_u32(sQ)), dk0 = sdesc_sw128(smem_u32(sK)), dv0 = sdesc_sw128_mn(smem_u32(sV));
+      uint64_t* last_bar = nullptr;  // the barrier of the most recent commit, for the drain
+      uint32_t last_ph = 0;
+      Items<LOCAL> si, pi;  // S cursor and P·V cursor
+      si.start(a);
+      pi.start(a);
+      int sj = 0, pj = 0;
+      uint32_t sg = 0, pg = 0;
+      auto issue_s = [&]() -> bool {
+        const int qb = si.t & 1;
+        if (sj == 0) {
+          if (!mbar_wait(&q_full[qb], (si.t >> 1) & 1, abort, &g_attn_err)) return false;
         }
-        if (j >= 1) {
-          const int jj = j - 1, b = jj & 1;
-          if (!mbar_wait(&p_ready[b], (jj >> 1) & 1, abort, &g_attn_err)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t va = smem_u32(sV + (jj % NST) * KV_BYTES);
+        const int st = sg % NST;
+        if (!mbar_wait(&kv_full[st], (sg / NST) & 1, abort, &g_attn_err)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + (sg % NS) * TK;
+        const uint64_t dq = dq0 + ((qb * TILE_BYTES) >> 4), dk = dk0 + ((st * KV_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < TK / 16; kk++)
-            tc_mma_ts(tmem + o_col, tmem + (uint32_t)(b * TK + kk * 8), sdesc_sw128_mn(va + kk * 2048), id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&o_done[jj & 1]);
-          tc_commit(&kv_empty[jj % NST]);
-          pv_issued++;
+        for (int kk = 0; kk < HD / 16; kk++) tc_mma(d, dq + kk * 2, dk + kk * 2, id_s, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[sg % NS]);
+        last_bar = &s_full[sg % NS];
+        last_ph = (sg / NS) & 1;
+        if (sj == si.cur.nb - 1) tc_commit(&q_empty[qb]);
+        sg++;
+        if (++sj == si.cur.nb) {
+          sj = 0;
+          si.step(a);
         }
+        return true;
+      };
+      bool ok = true;
+      for (int i = 0; i < NS && ok && si.valid(a); i++) ok = issue_s();
+      while (ok && pi.valid(a)) {
+        const uint32_t b = pg % NS;
+        if (!mbar_wait(&p_ready[b], (pg / NS) & 1, abort, &g_attn_err)) break;
+        tc_fence_after();
+        const int st = pg % NST;
+        const uint64_t dv = dv0 + ((st * KV_BYTES) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; kk++)
+          tc_mma_ts(tmem + O_COL, tmem + b * TK + kk * 8, dv + kk * (2048 >> 4), id_pv, (pj > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&o_done[pg & 1]);
+        tc_commit(&kv_empty[st]);
+        last_bar = &o_done[pg & 1];
+        last_ph = (pg >> 1) & 1;
+        pg++;
+        if (++pj == pi.cur.nb) {
+          pj = 0;
+          pi.step(a);
+        }
+        if (si.valid(a)) ok = issue_s();
       }
-      if (pv_issued) {  // the MMAs issued here finish before TMEM is freed
-        const int last = pv_issued - 1;
-        uint64_t t0 = gtimer();
-        while (!mbar_try_wait(&o_done[last & 1], (last >> 1) & 1) && gtimer() - t0 < kWaitNs) {}
+      if (last_bar) {  // MMAs complete in issue order: the last commit covers them all
+        const uint64_t t0 = gtimer();
+        while (!mbar_try_wait(last_bar, last_ph) && gtimer() - t0 < kWaitNs) {}
       }
     }
   } else {
     // softmax / correction / epilogue: thread <-> query row
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int qi = q0 + row;
-    const int qw = q0 + quarter * 32;  // first query row of this warp
-    const bool warp_live = qw < L;     // warps wholly past the sequence end skip their exps
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    float m = -INFINITY, l = 0.f;
+    const float sl = a.scale_log2;
+    uint32_t g = 0;
     bool ok = true;
-    for (int j = 0; j < nb; j++) {
-      const int b = j & 1;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort, &g_attn_err)) { ok = false; break; }
-      tc_fence_after();
-      const int kbase = kv_lo + j * TK;
-      // this row's visible keys, relative to the block: [lo, hi]
-      const int lo = (LOCAL ? max(0, qi - a.half_window) : 0) - kbase;
-      const int hi = (LOCAL ? min(L - 1, qi + a.half_window) : L - 1) - kbase;
-      // per 32-key chunk, warp-uniform: live = some row sees a key of it; full = every row sees all of it
-      bool live[TK / 32], full[TK / 32];
+    Items<LOCAL> it;
+    for (it.start(a); ok && it.valid(a); it.step(a)) {
+      const Work& wk = it.cur;
+      const int qi = wk.q0 + row;
+      const bool warp_live = wk.q0 + quarter * 32 < wk.L;  // warps wholly past the sequence end skip their exps
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < wk.nb; j++) {
+        const uint32_t gj = g + j, b = gj % NS;
+        if (!mbar_wait(&s_full[b], (gj / NS) & 1, abort, &g_attn_err)) { ok = false; break; }
+        tc_fence_after();
+        const int kbase = wk.kv_lo + j * TK;
+        // this row's visible keys, relative to the block: [lo, hi]
+        const int lo = (LOCAL ? max(0, qi - a.half_window) : 0) - kbase;
+        const int hi = (LOCAL ? min(wk.L - 1, qi + a.half_window) : wk.L - 1) - kbase;
+        // per 32-key chunk, warp-uniform: live = some row sees a key of it; full = every row sees all of it
+        bool live[TK / 32], full[TK / 32];
 #pragma unroll
-      for (int c = 0; c < TK / 32; c++) {
-        const int c0 = c * 32, c1 = c0 + 31;
-        live[c] = warp_live && __any_sync(0xffffffffu, c1 >= lo && c0 <= hi);
-        full[c] = __all_sync(0xffffffffu, c0 >= lo && c1 <= hi);
-      }
-      float s[TK];
-      {
-        uint32_t sr[TK];
+        for (int c = 0; c < TK / 32; c++) {
+          const int c0 = c * 32, c1 = c0 + 31;
+          live[c] = warp_live && __any_sync(0xffffffffu, c1 >= lo && c0 <= hi);
+          full[c] = __all_sync(0xffffffffu, c0 >= lo && c1 <= hi);
+        }
+        float s[TK];
+        {
+          uint32_t sr[TK];
 #pragma unroll
-        for (int c = 0; c < TK / 32; c++)
-          if (live[c]) tmem_ld32(tmem + lane_off + (uint32_t)(b * TK + c * 32), sr + c * 32);
-        tmem_wait_ld();  // one wait for every load issued above
+          for (int c = 0; c < TK / 32; c++)
+            if (live[c]) tmem_ld32(tmem + lane_off + b * TK + c * 32, sr + c * 32);
+          tmem_wait_ld();  // one wait for every load issued above
 #pragma unroll
-        for (int i = 0; i < TK; i++) s[i] = __uint_as_float(sr[i]);
-      }
-      // row max of the raw scores (the softmax scale is positive, so it commutes)
-      float mx = -INFINITY;
+          for (int i = 0; i < TK; i++) s[i] = __uint_as_float(sr[i]);
+        }
+        // row max of the raw scores (the softmax scale is positive, so it
+        // commutes), four independent chains of three-input maxima
+        float mc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        const uint32_t span = (uint32_t)(hi - lo);  // k visible <=> (unsigned)(k - lo) <= span (hi >= lo)
 #pragma unroll
-      for (int c = 0; c < TK / 32; c++) {
-        if (!live[c]) continue;
-        if (full[c]) {
+        for (int c = 0; c < TK / 32; c++) {
+          if (!live[c]) continue;
+          if (full[c]) {
 #pragma unroll
-          for (int i = 0; i < 32; i++) mx = fmaxf(mx, s[c * 32 + i]);
-        } else {
+            for (int i = 0; i < 16; i++) mc[i & 3] = max3(mc[i & 3], s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            const int k = c * 32 + i;
-            const float v = (k >= lo && k <= hi) ? s[k] : -INFINITY;
-            s[k] = v;
-            mx = fmaxf(mx, v);
+            for (int i = 0; i < 16; i++) {
+              const int k = c * 32 + 2 * i;
+              const float v0 = (hi >= lo && (uint32_t)(k - lo) <= span) ? s[k] : -INFINITY;
+              const float v1 = (hi >= lo && (uint32_t)(k + 1 - lo) <= span) ? s[k + 1] : -INFINITY;
+              mc[i & 3] = max3(mc[i & 3], v0, v1);
+            }
           }
         }
-      }
-      // lazy rescale: the reference max (raw units) only moves when it grew by more
-      // than 2^8 after scaling, so P stays below 256 and O needs rescaling rarely
-      const float sl = a.scale_log2;
-      const float m_new = fmaxf(m, mx);
-      const bool grow = (m_new - m) * sl > 8.f;  // m = -inf: true unless the row is still all masked
-      const float corr = grow ? ex2((m - m_new) * sl) : 1.f;
-      if (grow) m = m_new;
-      const float nbias = m == -INFINITY ? 0.f : -m * sl;
-      float rs = 0.f;
+        const float mx = max3(mc[0], mc[1], fmaxf(mc[2], mc[3]));
+        // lazy rescale: the reference max (raw units) only moves when it grew by more
+        // than 2^8 after scaling, so P stays below 256 and O needs rescaling rarely
+        const float m_new = fmaxf(m, mx);
+        const bool grow = (m_new - m) * sl > 8.f;  // m = -inf: true unless the row is still all masked
+        const float corr = grow ? ex2((m - m_new) * sl) : 1.f;
+        if (grow) m = m_new;
+        const float nbias = m == -INFINITY ? 0.f : -m * sl;
+        float2 acc[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
-      for (int c = 0; c < TK / 32; c++) {
+        for (int c = 0; c < TK / 32; c++) {
+          if (live[c]) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          float p = 0.f;
-          if (live[c]) p = ex2(fmaf(s[c * 32 + i], sl, nbias));
-          s[c * 32 + i] = p;
-          rs += p;
+            for (int i = 0; i < 16; i++) {
+              const int k = c * 32 + 2 * i;
+              float2 x = fma2(make_float2(s[k], s[k + 1]), make_float2(sl, sl), make_float2(nbias, nbias));
+              x.x = ex2(x.x);
+              x.y = ex2(x.y);
+              if (!full[c]) {  // keys outside the row's range contribute 0
+                x.x = (hi >= lo && (uint32_t)(k - lo) <= span) ? x.x : 0.f;
+                x.y = (hi >= lo && (uint32_t)(k + 1 - lo) <= span) ? x.y : 0.f;
+              }
+              s[k] = x.x;
+              s[k + 1] = x.y;
+              acc[i & 3] = add2(acc[i & 3], x);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++) s[c * 32 + i] = 0.f;
+          }
         }
-      }
-      l = l * corr + rs;
+        const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
+        const float2 at = add2(a01, a23);
+        l = fmaf(l, corr, at.x + at.y);
+        {
+          uint32_t pr[32];
 #pragma unroll
-      for (int c = 0; c < TK / 64; c++) {
-        uint32_t pr[32];
-#pragma unroll
-        for (int i = 0; i < 32; i++) pr[i] = pack2<T>(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
-        tmem_st32(tmem + lane_off + (uint32_t)(b * TK + c * 32), pr);
-      }
-      tmem_wait_st();
-      if (j >= 1 && __any_sync(0xffffffffu, grow)) {
-        // O holds blocks < j once P_{j-1}·V_{j-1} is done; rescale it before P_j·V_j
-        if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, &g_attn_err)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < HD / 32; c++) {
-          uint32_t r[32];
-          tmem_ld32(tmem + lane_off + o_col + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-          tmem_st32(tmem + lane_off + o_col + c * 32, r);
+          for (int i = 0; i < 32; i++) pr[i] = pack2<T>(s[2 * i], s[2 * i + 1]);
+          tmem_st32(tmem + lane_off + b * TK, pr);
         }
         tmem_wait_st();
+        if (j >= 1 && __any_sync(0xffffffffu, grow)) {
+          // O holds blocks < j once P_{j-1}·V_{j-1} is done; rescale it before P_j·V_j
+          const uint32_t gp = gj - 1;
+          if (!mbar_wait(&o_done[gp & 1], (gp >> 1) & 1, abort, &g_attn_err)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HD / 32; c++) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_off + O_COL + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+            tmem_st32(tmem + lane_off + O_COL + c * 32, r);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[b]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[b]);
-    }
-    if (ok && mbar_wait(&o_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, abort, &g_attn_err)) {
+      if (!ok) break;
+      const uint32_t gl = g + wk.nb - 1;
+      if (!mbar_wait(&o_done[gl & 1], (gl >> 1) & 1, abort, &g_attn_err)) break;
       tc_fence_after();
       const float inv = 1.f / l;
-      T* out = (T*)a.out + ((int64_t)tok0 + qi) * a.H + h * HD;
+      T* out = (T*)a.out + ((int64_t)wk.tok0 + qi) * a.H + wk.h * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; c++) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_off + o_col + c * 32, r);
+        tmem_ld32(tmem + lane_off + O_COL + c * 32, r);
         tmem_wait_ld();
-        if (qi < L) {
+        if (qi < wk.L) {
 #pragma unroll
           for (int q = 0; q < 4; q++) {
             uint4 v;
@@ -306,6 +453,7 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
           }
         }
       }
+      g += wk.nb;
     }
   }
   tc_fence_before();
@@ -317,26 +465,30 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
 }
 
 template <typename T, bool LOCAL>
-void launch_attn(const CUtensorMap& mq, const CUtensorMap& mkv, const AttnTcArgs& a, int ntiles, int heads, cudaStream_t st) {
+void launch_attn(const CUtensorMap& mq, const CUtensorMap& mkv, const AttnTcArgs& a, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
     CUDA_OK(cudaFuncSetAttribute(k_attn_tc<T, LOCAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTN_SMEM));
     attr = true;
   }
-  k_attn_tc<T, LOCAL><<<dim3((unsigned)ntiles, (unsigned)heads), 192, ATTN_SMEM, st>>>(mq, mkv, a);
+  const int grid = std::min(a.nwork, 2 * lc::num_sms());  // persistent: two CTAs per SM
+  k_attn_tc<T, LOCAL><<<(unsigned)grid, 192, ATTN_SMEM, st>>>(mq, mkv, a);
 }
 
 }  // namespace
 
 namespace lc {
 
-// Tile list for the tcgen05 kernel: one entry per 128-row query tile.
+// Work list of the tcgen05 kernel: one entry per 128-row query tile, longest
+// sequences first (the persistent CTAs take items in this order, so the
+// costly ones start early and the short ones fill the tail).
 std::vector<int4> attention_tiles_tc(const int32_t* cu, int nseq) {
   std::vector<int4> t;
   for (int s = 0; s < nseq; s++) {
     int L = cu[s + 1] - cu[s];
     for (int q0 = 0; q0 < L; q0 += TQ) t.push_back(make_int4(cu[s], L, q0, 0));
   }
+  std::stable_sort(t.begin(), t.end(), [](const int4& x, const int4& y) { return x.y > y.y; });
   return t;
 }
 
@@ -347,14 +499,15 @@ void attention_varlen_tc(const void* qkv, void* out, const int4* tiles_dev, int 
   LC_CHECK(ntiles < (1 << 30), "attention: too many tiles");
   const CUtensorMap& mq = tensor_map_2d(qkv, T, 3 * (int64_t)H, 3 * (int64_t)H, 64, TQ, dtype);
   const CUtensorMap& mkv = tensor_map_2d(qkv, T, 3 * (int64_t)H, 3 * (int64_t)H, 64, TK, dtype);
-  AttnTcArgs a{tiles_dev, out, H, half_window, scale * 1.4426950408889634f};
   const int heads = H / HD;
+  LC_CHECK((int64_t)ntiles * heads < INT32_MAX, "attention: too many work items");
+  AttnTcArgs a{tiles_dev, out, H, half_window, scale * 1.4426950408889634f, heads, ntiles * heads};
   if (dtype == LC_F16) {
-    if (half_window >= 0) launch_attn<__half, true>(mq, mkv, a, ntiles, heads, st);
-    else launch_attn<__half, false>(mq, mkv, a, ntiles, heads, st);
+    if (half_window >= 0) launch_attn<__half, true>(mq, mkv, a, st);
+    else launch_attn<__half, false>(mq, mkv, a, st);
   } else {
-    if (half_window >= 0) launch_attn<__nv_bfloat16, true>(mq, mkv, a, ntiles, heads, st);
-    else launch_attn<__nv_bfloat16, false>(mq, mkv, a, ntiles, heads, st);
+    if (half_window >= 0) launch_attn<__nv_bfloat16, true>(mq, mkv, a, st);
+    else launch_attn<__nv_bfloat16, false>(mq, mkv, a, st);
   }
   LC_LAUNCHED(1);
 }
