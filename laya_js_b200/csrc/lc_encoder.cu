@@ -7,14 +7,20 @@
 //   Wqkv linear + reshape/transpose/split + RoPE   -> GEMM, EPI_ROPE_QKV (q/k rotated at each token's position)
 //   masks + sdpa + transpose/reshape               -> attention_varlen (window rule in-kernel)
 //   Wo linear + residual add                       -> GEMM, EPI_RESIDUAL (in place on x)
-//   Wi linear + geglu                              -> GEMM, EPI_GEGLU (Wi rows interleaved in 32-row blocks at load)
+//   mlp_norm + Wi linear + geglu                   -> GEMM, EPI_GEGLU (Wi rows interleaved in 32-row blocks at load)
 //   mlp.Wo linear + residual add                   -> GEMM, EPI_RESIDUAL (in place on x)
+//   attn_norm (layers >= 1) + Wqkv                 -> the EPI_ROPE_QKV GEMM
+// The two LayerNorms of a layer are folded into the projection after them:
+// LayerNorm(x)·Wᵀ = r·(x·(W·diag(γ))ᵀ − μ·Σ_k W[n,k]γ[k]) per row, with μ and
+// r = 1/sqrt(var + eps) from row statistics the residual GEMM before records
+// in its epilogue; no normalised copy of the hidden states is written.
 // plus the CLS classifier head + softmax (packages/laya/src/model.ts:228 pattern).
 // Quantized Linear weights (4/8-bit, laya-js packing) stay packed in HBM and
 // are dequantised per GEMM into one reusable f16/bf16 scratch matrix.
 #include "lc_api.h"
 #include "lc_gemm.h"
 #include "lc_quant.cuh"
+#include "lc_sm100.cuh"
 #include "laya_cuda_encoder.h"
 
 #include <algorithm>
@@ -30,6 +36,7 @@ std::vector<int4> attention_tiles(const int32_t* cu, int nseq);
 void attention_varlen(const void* qkv, void* out, const int4* tiles_dev, int ntiles, int64_t T, int H, int half_window, float scale,
                       int dtype, cudaStream_t st);
 void dequant_into(const LcTensor* w, const LcTensor* s, const LcTensor* b, int bits, int g, int mode, LcTensor* out);
+void dequant_scaled_into(const LcTensor* w, const LcTensor* s, const LcTensor* b, int bits, int g, int mode, const float* gamma, LcTensor* out);
 }  // namespace lc
 
 namespace {
@@ -125,6 +132,28 @@ __global__ void k_cls_head(const T* __restrict__ hidden, int H, const int32_t* _
   }
 }
 
+// LayerNorm weight folded into the projection that reads the norm's output:
+// Wout[n, k] = round(W[n, k]·γ[k]) (Wout may be null) and wsum[n] = Σ_k of
+// those rounded values, one warp per row.
+template <typename T>
+__global__ void k_fold_norm(const T* __restrict__ W, const float* __restrict__ gamma, T* __restrict__ Wout, float* __restrict__ wsum, int64_t N,
+                            int64_t K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t n = warp; n < N; n += nwarps) {
+    double acc = 0.0;
+    for (int64_t k = lane; k < K; k += 32) {
+      const T v = sm100::TcFmt<T>::cvt(sm100::TcFmt<T>::back(W[n * K + k]) * gamma[k]);
+      if (Wout) Wout[n * K + k] = v;
+      acc += (double)sm100::TcFmt<T>::back(v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) wsum[n] = (float)acc;
+  }
+}
+
 __global__ void k_permute_rows(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t rowbytes, const int32_t* __restrict__ perm,
                                int64_t rows) {
   LC_GRID_STRIDE(i, rows * rowbytes) {
@@ -139,6 +168,10 @@ struct Mat {
   LcTensor* s = nullptr;
   LcTensor* b = nullptr;
   int64_t N = 0, K = 0;
+  // folded LayerNorm (the projection reads the norm's input): γ (f32 [K]) and
+  // wsum (f32 [N]) = row sums of W·diag(γ); dense weights are stored folded
+  const float* gamma = nullptr;
+  LcTensor* wsum = nullptr;
 };
 
 struct Layer {
@@ -295,6 +328,43 @@ Mat take_mat(Encoder* e, const lc_tensor* w, int& i, int64_t N, int64_t K, const
   return m;
 }
 
+// Folds LayerNorm weight γ into the projection that consumes the norm's output
+// (ModernBertLayer: Wqkv after attn_norm, Wi after mlp_norm): dense weights are
+// replaced by W·diag(γ); packed weights stay packed and their per-forward
+// dequantisation applies γ. wsum = row sums of the folded weight.
+void fold_norm(Encoder* e, Mat& m, const LcTensor* gamma) {
+  const lc_encoder_config& c = e->cfg;
+  m.gamma = (const float*)gamma->data();
+  m.wsum = alloc(LC_F32, {m.N});
+  e->owned.push_back(m.wsum);
+  LcTensor* src = m.dense;
+  LcTensor* tmp = nullptr;
+  if (!src) {
+    tmp = alloc(c.dtype, {m.N, m.K});
+    dequant_into(m.q, m.s, m.b, c.quant_bits, c.quant_group, c.quant_mode, tmp);
+    src = tmp;
+  }
+  LcTensor* out = m.dense ? alloc(c.dtype, {m.N, m.K}) : nullptr;
+  unsigned blocks = blocks_for(m.N * 32, 256);
+  if (c.dtype == LC_F16)
+    k_fold_norm<__half><<<blocks, 256, 0, stream()>>>((const __half*)src->data(), m.gamma, out ? (__half*)out->data() : nullptr,
+                                                      (float*)m.wsum->data(), m.N, m.K);
+  else
+    k_fold_norm<__nv_bfloat16><<<blocks, 256, 0, stream()>>>((const __nv_bfloat16*)src->data(), m.gamma,
+                                                             out ? (__nv_bfloat16*)out->data() : nullptr, (float*)m.wsum->data(), m.N, m.K);
+  LC_LAUNCHED(1);
+  if (tmp) release(tmp);
+  if (out) {
+    auto it = std::find(e->owned.begin(), e->owned.end(), m.dense);
+    if (it != e->owned.end()) {
+      e->owned.erase(it);
+      release(m.dense);
+    }
+    m.dense = out;
+    e->owned.push_back(out);
+  }
+}
+
 // y = x · Wᵀ with the given epilogue (dense weight or packed weight dequantised into the scratch)
 void run_gemm(Encoder* e, const Mat& m, const void* x, int64_t M, void* y, int64_t ldy, const GemmEpilogue& ep, int64_t n_out, int cls) {
   const void* w;
@@ -310,7 +380,8 @@ void run_gemm(Encoder* e, const Mat& m, const void* x, int64_t M, void* y, int64
     }
     LcTensor* view = view_of(e->deq, {m.N, m.K}, {m.K, 1}, 0);
     Prof pd(e, 3);
-    dequant_into(m.q, m.s, m.b, e->cfg.quant_bits, e->cfg.quant_group, e->cfg.quant_mode, view);
+    if (m.gamma) dequant_scaled_into(m.q, m.s, m.b, e->cfg.quant_bits, e->cfg.quant_group, e->cfg.quant_mode, m.gamma, view);
+    else dequant_into(m.q, m.s, m.b, e->cfg.quant_bits, e->cfg.quant_group, e->cfg.quant_mode, view);
     release(view);
     w = e->deq->data();
   }
@@ -341,9 +412,17 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
 // Frees the CUDA graphs captured on an encoder (they reference its weights).
 void free_graphs_of(Encoder* e);
 
-// Workspace bytes of one forward over T tokens (x | h | qkv | pos).
+// Workspace of one forward over T tokens: x [T,H] | h [T,H] | qkv [T,3H] |
+// pos [T] | LayerNorm row statistics [T][parts] (float2).
+int stats_parts(const lc_encoder_config& c) {
+  const int bn = gemm_tile_n(c.hidden_size, false);
+  return (c.hidden_size + bn - 1) / bn;
+}
+size_t stats_offset(const lc_encoder_config& c, int64_t T) {
+  return ((size_t)T * c.hidden_size * 2 * 5 + (size_t)T * 4 + 255) & ~(size_t)255;
+}
 size_t workspace_bytes(const lc_encoder_config& c, int64_t T) {
-  return (size_t)T * c.hidden_size * 2 * 5 + (size_t)T * 4;
+  return stats_offset(c, T) + (size_t)T * stats_parts(c) * sizeof(float2);
 }
 
 // The forward on device ids (i32 [T]) and host cu_seqlens.
@@ -370,21 +449,16 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
   grow_pinned(e->stage, e->stage_bytes, meta);
   memcpy(e->stage, cu, (size_t)(nseq + 1) * 4);
   memcpy((char*)e->stage + cu_bytes, tiles.data(), tiles.size() * sizeof(int4));
-  // workspace: x | h | qkv | pos | meta
-  size_t off_x = 0, off_h = off_x + T * H * esz, off_qkv = off_h + T * H * esz, off_pos = off_qkv + T * 3 * H * esz;
-  size_t off_meta = (off_pos + T * 4 + 255) & ~(size_t)255;
+  // workspace: the forward's buffers, then the metadata
+  size_t off_meta = (workspace_bytes(c, T) + 255) & ~(size_t)255;
   grow_ws(e, off_meta + meta);
   char* ws = (char*)e->ws;
-  void* x = ws + off_x;
-  void* h = ws + off_h;
-  void* qkv = ws + off_qkv;
-  int32_t* pos = (int32_t*)(ws + off_pos);
   int32_t* cu_dev = (int32_t*)(ws + off_meta);
   int4* tiles_dev = (int4*)(ws + off_meta + cu_bytes);
   CUDA_OK(cudaMemcpyAsync(ws + off_meta, e->stage, meta, cudaMemcpyHostToDevice, st));
   if (!e->stage_ev) CUDA_OK(cudaEventCreateWithFlags(&e->stage_ev, cudaEventDisableTiming));
   CUDA_OK(cudaEventRecord(e->stage_ev, st));
-  (void)x, (void)h, (void)qkv, (void)pos;
+  (void)H, (void)I, (void)esz;
   run_kernels(e, ws, T, nseq, maxlen, cu_dev, tiles_dev, (int)tiles.size(), ids_dev, hidden_out ? hidden_out->data() : nullptr, head_w,
               head_b, probs_dev, st);
 }
@@ -403,6 +477,8 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
   void* h = ws + (size_t)T * H * esz;
   void* qkv = ws + (size_t)2 * T * H * esz;
   int32_t* pos = (int32_t*)(ws + (size_t)5 * T * H * esz);
+  float2* stats = (float2*)(ws + stats_offset(c, T));
+  const int parts = stats_parts(c), part_cols = gemm_tile_n(H, false);
   k_positions<<<std::min(nseq, 4096), 256, 0, st>>>(cu_dev, nseq, pos);
   LC_LAUNCHED(1);
 
@@ -429,20 +505,32 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
   delete pe;
 
   const float scale = 1.0f / sqrtf(64.0f);
+  // LayerNorms folded into the projection after them: the residual GEMMs
+  // (Wo, mlp.Wo) record row statistics, the next projection normalises.
+  auto folded = [&](GemmEpilogue& ep, const Mat& m) {
+    ep.ln_stats = stats;
+    ep.ln_wsum = (const float*)m.wsum->data();
+    ep.ln_parts = parts;
+    ep.ln_part_cols = part_cols;
+    ep.ln_cols = H;
+    ep.ln_eps = (float)c.norm_eps;
+  };
   for (size_t li = 0; li < e->layers.size(); li++) {
     const Layer& L = e->layers[li];
     const void* hin = x;
-    if (L.attn_norm) {
-      Prof p(e, 2);
-      layernorm_raw(x, (const float*)L.attn_norm->data(), h, T, H, (float)c.norm_eps, c.dtype, st);
-      hin = h;
-    }
     GemmEpilogue eq;
     eq.kind = EPI_ROPE_QKV;
     eq.pos = pos;
     eq.rope_cs = L.kind == 0 ? rope_g : rope_l;
     eq.rope_cap = L.kind == 0 ? cap_g : cap_l;
     eq.rope_cols = 2 * H;
+    if (L.attn_norm && L.Wqkv.wsum) {
+      folded(eq, L.Wqkv);
+    } else if (L.attn_norm) {  // a norm before the first layer: the embedding output has no statistics
+      Prof p(e, 2);
+      layernorm_raw(x, (const float*)L.attn_norm->data(), h, T, H, (float)c.norm_eps, c.dtype, st);
+      hin = h;
+    }
     run_gemm(e, L.Wqkv, hin, T, qkv, 3 * H, eq, 3 * H, 0);
     // attention -> h (h is free again once the Wqkv GEMM has read it)
     {
@@ -453,14 +541,12 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
     er.kind = EPI_RESIDUAL;
     er.resid = x;
     er.ldr = H;
+    er.stats_out = stats;
     run_gemm(e, L.Wo, h, T, x, H, er, H, 4);
-    {
-      Prof p(e, 2);
-      layernorm_raw(x, (const float*)L.mlp_norm->data(), h, T, H, (float)c.norm_eps, c.dtype, st);
-    }
     GemmEpilogue eg;
     eg.kind = EPI_GEGLU;
-    run_gemm(e, L.Wi, h, T, qkv, I, eg, I, 5);
+    folded(eg, L.Wi);
+    run_gemm(e, L.Wi, x, T, qkv, I, eg, I, 5);
     run_gemm(e, L.WoMlp, qkv, T, x, H, er, H, 6);
   }
   void* fin = hidden_out ? hidden_out : h;
@@ -538,6 +624,8 @@ int lc_encoder_create(uint64_t* out, const lc_encoder_config* cfg, const int32_t
       L.mlp_norm = keep_f32(e.get(), mn);
       L.Wi = take_mat(e.get(), w, i, 2 * I, H, p + "mlp.Wi", true);
       L.WoMlp = take_mat(e.get(), w, i, H, I, p + "mlp.Wo", false);
+      if (l > 0) fold_norm(e.get(), L.Wqkv, L.attn_norm);
+      fold_norm(e.get(), L.Wi, L.mlp_norm);
       e->layers.push_back(L);
     }
     LcTensor* fn = check(w[i++], "encoder final_norm");

@@ -12,8 +12,9 @@
 //               fp16/bf16 in, f32 accumulate) from one elected thread; commits
 //               free the ring slot and, per tile, signal the epilogue;
 //   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator (each warp owns 32
-//               TMEM lanes = 32 rows), fused bias / residual / RoPE / GeGLU,
-//               16-byte stores.
+//               TMEM lanes = 32 rows), fused bias / residual / RoPE / GeGLU /
+//               folded-LayerNorm correction (and the row statistics a later
+//               folded LayerNorm needs), 16-byte or TMA stores.
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1. Every mbarrier wait is bounded
 // (2 s of %globaltimer); on timeout the kernel records an error word, drains
@@ -49,6 +50,70 @@ struct GemmArgs {
 };
 
 __device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
+
+// Folded LayerNorm, consumer side: mean and 1/sqrt(var + eps) of row `row`
+// from its per-part (mean, M2) statistics (Chan et al.'s pairwise combination).
+__device__ __forceinline__ void ln_row(const GemmEpilogue& ep, int row, int M, float& mu, float& r) {
+  mu = 0.f;
+  r = 1.f;
+  if (row >= M) return;
+  float n = 0.f, mean = 0.f, m2 = 0.f;
+  for (int p = 0; p < ep.ln_parts; p++) {
+    const float2 v = ep.ln_stats[(int64_t)row * ep.ln_parts + p];
+    const float c = (float)min(ep.ln_part_cols, ep.ln_cols - p * ep.ln_part_cols);
+    const float nn = n + c, d = v.x - mean;
+    mean += d * (c / nn);
+    m2 += v.y + d * d * (n * c / nn);
+    n = nn;
+  }
+  mu = mean;
+  r = rsqrtf(fmaxf(m2, 0.f) / (float)ep.ln_cols + ep.ln_eps);
+}
+// acc columns [col, col+64) -> r·(acc − μ·wsum)
+__device__ __forceinline__ void ln_apply(const GemmEpilogue& ep, int col, float mu, float r, float* a, float* b) {
+  const float4* w4 = (const float4*)(ep.ln_wsum + col);
+#pragma unroll
+  for (int q = 0; q < 8; q++) {
+    const float4 w = __ldg(w4 + q);
+    a[q * 4 + 0] = r * fmaf(-mu, w.x, a[q * 4 + 0]);
+    a[q * 4 + 1] = r * fmaf(-mu, w.y, a[q * 4 + 1]);
+    a[q * 4 + 2] = r * fmaf(-mu, w.z, a[q * 4 + 2]);
+    a[q * 4 + 3] = r * fmaf(-mu, w.w, a[q * 4 + 3]);
+  }
+#pragma unroll
+  for (int q = 0; q < 8; q++) {
+    const float4 w = __ldg(w4 + 8 + q);
+    b[q * 4 + 0] = r * fmaf(-mu, w.x, b[q * 4 + 0]);
+    b[q * 4 + 1] = r * fmaf(-mu, w.y, b[q * 4 + 1]);
+    b[q * 4 + 2] = r * fmaf(-mu, w.z, b[q * 4 + 2]);
+    b[q * 4 + 3] = r * fmaf(-mu, w.w, b[q * 4 + 3]);
+  }
+}
+// Producer side: round the 64 outputs to the stored type (so the statistics
+// describe the tensor the next layer reads) and fold their mean / M2 into
+// the tile's running (n, mean, M2).
+template <typename T>
+__device__ __forceinline__ void stats_unit(float* a, float* b, float& n, float& mean, float& m2) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    a[j] = TcFmt<T>::back(TcFmt<T>::cvt(a[j]));
+    b[j] = TcFmt<T>::back(TcFmt<T>::cvt(b[j]));
+    s += a[j] + b[j];
+  }
+  const float mu = s * (1.f / 64.f);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    const float d0 = a[j] - mu, d1 = b[j] - mu;
+    q = fmaf(d0, d0, q);
+    q = fmaf(d1, d1, q);
+  }
+  const float nn = n + 64.f, d = mu - mean;
+  mean += d * (64.f / nn);
+  m2 += q + d * d * (n * 64.f / nn);
+  n = nn;
+}
 
 // store 32 consecutive values v[0..31] at columns [col, col+32) of row `row`, valid columns < ncols
 template <typename T>
@@ -247,6 +312,9 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       const int row0 = m0 + quarter * 32;
       const int row = row0 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      float ln_mu, ln_r;
+      if (ep.ln_stats) ln_row(ep, row, args.M, ln_mu, ln_r);
+      float st_n = 0.f, st_mean = 0.f, st_m2 = 0.f;
 #pragma unroll 1
       for (int u = 0; u < BN / 64; u++) {
         const int col = n0 + u * 64;
@@ -271,6 +339,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         float a[32], b[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) a[j] = __uint_as_float(ra[j]), b[j] = __uint_as_float(rbv[j]);
+        if (ep.ln_stats) ln_apply(ep, col, ln_mu, ln_r, a, b);
         if (geglu) {
 #pragma unroll
           for (int j = 0; j < 32; j++) a[j] = gelu_exact(a[j]) * b[j];
@@ -308,6 +377,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
                 else b[(c - 4) * 8 + j] += TcFmt<T>::back(h[j]);
               }
             }
+            if (ep.stats_out) stats_unit<T>(a, b, st_n, st_mean, st_m2);
           }
         }
         // write this row's chunks: GeGLU writes 4 chunks (32 columns) per unit, else 8
@@ -334,6 +404,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
           if (geglu && (u & 1) == 0) break;  // the pair's second unit is past the weight rows
         }
       }
+      if (ep.stats_out && row < args.M) ep.stats_out[(int64_t)row * args.ntile_n + t % args.ntile_n] = make_float2(st_mean, st_m2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -356,6 +427,9 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       const bool live = row < args.M;
       T* rowp = Y + (int64_t)row * args.ldy;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      float ln_mu, ln_r;
+      if (args.ep.ln_stats) ln_row(args.ep, row, args.M, ln_mu, ln_r);
+      float st_n = 0.f, st_mean = 0.f, st_m2 = 0.f;
 #pragma unroll 1
       for (int u = 0; u < BN / 64; u++) {
         uint32_t ra[32], rb[32];
@@ -368,6 +442,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         const int col = n0 + u * 64;
         if (!live || col >= (args.ep.kind == EPI_GEGLU ? 2 * args.N : args.N)) continue;
         const GemmEpilogue& ep = args.ep;
+        if (ep.ln_stats) ln_apply(ep, col, ln_mu, ln_r, a, b);
         if (ep.kind == EPI_GEGLU) {
 #pragma unroll
           for (int j = 0; j < 32; j++) a[j] = gelu_exact(a[j]) * b[j];
@@ -402,10 +477,12 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
           load32f<T>(rp, col + 32, args.N, r, vec);
 #pragma unroll
           for (int j = 0; j < 32; j++) b[j] += r[j];
+          if (ep.stats_out) stats_unit<T>(a, b, st_n, st_mean, st_m2);
         }
         store32<T>(rowp, col, args.N, a, vec);
         store32<T>(rowp, col + 32, args.N, b, vec);
       }
+      if (args.ep.stats_out && live) args.ep.stats_out[(int64_t)row * args.ntile_n + t % args.ntile_n] = make_float2(st_mean, st_m2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -487,9 +564,11 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
   // the accumulator width covered by the weight rows: GeGLU produces N outputs from 2N rows
   int64_t Nacc = ep.kind == EPI_GEGLU ? 2 * N : N;
-  int BN = (Nacc % 256 == 0 || Nacc > 1024) ? 256 : 128;
-  if (ep.kind == EPI_GEGLU && Nacc % BN) BN = 128;
+  const int BN = gemm_tile_n(Nacc, ep.kind == EPI_GEGLU);
   if (ep.kind == EPI_ROPE_QKV && (ep.rope_cols % 64)) return false;
+  // folded-LayerNorm statistics cover whole 64-column units
+  if (ep.stats_out && (ep.kind != EPI_RESIDUAL || N % 64)) return false;
+  if (ep.ln_stats && (Nacc % 64 || ((uintptr_t)ep.ln_wsum & 15) || ep.ln_parts < 1 || ep.ln_cols != K)) return false;
   GemmArgs a{};
   a.M = (int)M;
   a.N = (int)N;
@@ -529,6 +608,12 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
   }
   LC_LAUNCHED(1);
   return true;
+}
+
+int gemm_tile_n(int64_t Nacc, bool geglu) {
+  int BN = (Nacc % 256 == 0 || Nacc > 1024) ? 256 : 128;
+  if (geglu && Nacc % BN) BN = 128;
+  return BN;
 }
 
 bool gemm_linear(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y, const GemmEpilogue& ep) {

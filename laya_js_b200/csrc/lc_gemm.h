@@ -20,6 +20,15 @@ struct GemmEpilogue {
   const float* rope_cs = nullptr;   // EPI_ROPE_QKV: cos/sin table [32][cap] ++ [32][cap] (position-minor)
   int rope_cap = 0;
   int rope_cols = 0;                // EPI_ROPE_QKV: columns [0, rope_cols) are rotated (q and k), head dim 64
+  // LayerNorm folded into the next projection (the fused encoder): a residual
+  // GEMM records row statistics of what it stores, and the projection that
+  // consumes LayerNorm(y)·diag(γ) turns x·(W·diag(γ))ᵀ into the normalised
+  // product: out = r·(acc − μ·wsum[n]) with μ, r = 1/sqrt(var + eps) of row m.
+  float2* stats_out = nullptr;       // EPI_RESIDUAL: (mean, M2) of the stored row over each N tile: [M][ntile_n]
+  const float2* ln_stats = nullptr;  // the statistics to apply: [M][ln_parts], ln_part_cols columns per part
+  const float* ln_wsum = nullptr;    // Σ_k W[n, k]·γ[k] per accumulator column n (16-byte aligned)
+  int ln_parts = 0, ln_part_cols = 0, ln_cols = 0;
+  float ln_eps = 0.f;
 };
 
 namespace lc {
@@ -29,6 +38,8 @@ bool gemm_linear(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, Lc
 // Raw-pointer form used by the fused encoder: all dense row-major, dtype f16/bf16.
 bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, const void* bias, int bias_dtype, void* y, int64_t ldy,
               int dtype, const GemmEpilogue& ep, cudaStream_t st);
+// N-tile width gemm_raw uses for an accumulator of Nacc columns.
+int gemm_tile_n(int64_t Nacc, bool geglu);
 void linear_simt(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y);
 const float* rope_table(int D, double base, int L, int* cap_out, bool position_minor = false);
 bool attention_try_fast(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor* y);

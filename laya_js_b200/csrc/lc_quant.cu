@@ -36,6 +36,21 @@ __global__ void k_dequant(const uint8_t* __restrict__ w, const char* s, const ch
   }
 }
 
+// dequantise rows [N, K] into 16-bit `out` with column k scaled by gamma[k]:
+// out = round(round(q·s + b) · γ_k) — the weight the encoder's folded
+// LayerNorm multiplies by (the dense path folds the stored weight the same way)
+__global__ void k_dequant_scaled(const uint8_t* __restrict__ w, const char* s, const char* b, int sdt, int bits, int g, int mode, int64_t N,
+                                 int64_t K, const float* __restrict__ gamma, char* out, int odt) {
+  int64_t G = (K + g - 1) / g;
+  LC_GRID_STRIDE(t, N * K) {
+    int64_t r = t / K, j = t % K;
+    int q = quant_value(w + r * (K * bits / 8), j, bits, mode);
+    float sv = ld_as<float>(s, sdt, r * G + j / g);
+    float bv = b ? ld_as<float>(b, sdt, r * G + j / g) : 0.f;
+    st_as<float>(out, odt, t, dequant_rounded(odt, q, sv, bv) * gamma[j]);
+  }
+}
+
 // row gather + dequantise: out [n, K], row i = dequant(w[ids[i]]) (zeros for an out-of-range id)
 __global__ void k_quant_gather(const uint8_t* __restrict__ w, const char* s, const char* b, int sdt, int bits, int g, int mode, int64_t V,
                                int64_t K, const char* ids, int iddt, int64_t n, char* out, int odt) {
@@ -132,6 +147,13 @@ void dequant_into(const LcTensor* w, const LcTensor* s, const LcTensor* b, int b
   int64_t N = w->shape[0], K = w->shape[1] * 8 / bits;
   k_dequant<<<blocks_for(N * K, 256), 256, 0, stream()>>>((const uint8_t*)w->data(), s->data(), b ? b->data() : nullptr, s->dtype, bits, g,
                                                            mode, N, K, out->data(), out->dtype);
+  LC_LAUNCHED(1);
+}
+// The same with column k scaled by gamma[k] (f32, K values), out f16/bf16.
+void dequant_scaled_into(const LcTensor* w, const LcTensor* s, const LcTensor* b, int bits, int g, int mode, const float* gamma, LcTensor* out) {
+  int64_t N = w->shape[0], K = w->shape[1] * 8 / bits;
+  k_dequant_scaled<<<blocks_for(N * K, 256), 256, 0, stream()>>>((const uint8_t*)w->data(), s->data(), b ? b->data() : nullptr, s->dtype,
+                                                                  bits, g, mode, N, K, gamma, out->data(), out->dtype);
   LC_LAUNCHED(1);
 }
 }  // namespace lc
