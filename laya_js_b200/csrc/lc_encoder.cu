@@ -415,8 +415,8 @@ void free_graphs_of(Encoder* e);
 // Workspace of one forward over T tokens: x [T,H] | h [T,H] | qkv [T,3H] |
 // pos [T] | LayerNorm row statistics [T][parts] (float2).
 int stats_parts(const lc_encoder_config& c) {
-  const int bn = gemm_tile_n(c.hidden_size, false);
-  return (c.hidden_size + bn - 1) / bn;
+  const int pc = gemm_stats_part_cols(c.hidden_size);
+  return (c.hidden_size + pc - 1) / pc;
 }
 size_t stats_offset(const lc_encoder_config& c, int64_t T) {
   return ((size_t)T * c.hidden_size * 2 * 5 + (size_t)T * 4 + 255) & ~(size_t)255;
@@ -478,7 +478,7 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
   void* qkv = ws + (size_t)2 * T * H * esz;
   int32_t* pos = (int32_t*)(ws + (size_t)5 * T * H * esz);
   float2* stats = (float2*)(ws + stats_offset(c, T));
-  const int parts = stats_parts(c), part_cols = gemm_tile_n(H, false);
+  const int parts = stats_parts(c), part_cols = gemm_stats_part_cols(H);
   k_positions<<<std::min(nseq, 4096), 256, 0, st>>>(cu_dev, nseq, pos);
   LC_LAUNCHED(1);
 

@@ -5,14 +5,16 @@
 // packages/backend-mlx/src/index.ts:576-587) for the contract op `linear`
 // (packages/tensor-backend/src/index.ts:211-215: f32 accumulation).
 //
-// Design (one persistent CTA per SM, 6 warps):
+// Design (one persistent CTA per SM, 10 warps):
 //   warp 0      TMA producer: 128x64 tiles of x and BNx64 tiles of w, 128-byte
 //               swizzle, into a STAGES-deep shared-memory ring (mbarrier full/empty);
 //   warp 1      allocates TMEM and issues tcgen05.mma (M=128, N=BN, K=16,
 //               fp16/bf16 in, f32 accumulate) from one elected thread; commits
 //               free the ring slot and, per tile, signal the epilogue;
-//   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator (each warp owns 32
-//               TMEM lanes = 32 rows), fused bias / residual / RoPE / GeGLU /
+//   warps 2-9   epilogue: tcgen05.ld of the f32 accumulator (a warp reaches
+//               the 32 TMEM lanes = rows of quarter warp % 4; warps w and
+//               w + 4 share those rows and take one half of the tile's
+//               columns each), fused bias / residual / RoPE / GeGLU /
 //               folded-LayerNorm correction (and the row statistics a later
 //               folded LayerNorm needs), 16-byte or TMA stores.
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
@@ -51,6 +53,32 @@ struct GemmArgs {
 
 __device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
 
+// erf(x) by the rational approximation of Abramowitz & Stegun, Handbook of
+// Mathematical Functions (1964), eq. 7.1.26 (after C. Hastings):
+// erf(x) = 1 − (a1·t + a2·t² + a3·t³ + a4·t⁴ + a5·t⁵)·exp(−x²), t = 1/(1 + p·x),
+// x >= 0, |error| <= 1.5e-7, odd extension for x < 0. Two MUFU operations
+// (reciprocal, exp2) and six FMAs per value.
+__device__ __forceinline__ float erf_as(float x) {
+  const float ax = fabsf(x);
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.f)));
+  float q = fmaf(1.061405429f, t, -1.453152027f);
+  q = fmaf(q, t, 1.421413741f);
+  q = fmaf(q, t, -0.284496736f);
+  q = fmaf(q, t, 0.254829592f);
+  q *= t;
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(ax * (ax * -1.4426950408889634f)));  // exp(−x²)
+  return copysignf(fmaf(-q, e, 1.f), x);
+}
+// GELU with the erf above: 0.5·x·(1 + erf(x/√2)), the GeGLU activation of the
+// fused encoder (packages/backend-webgpu/src/kernels.ts:102 computes the same
+// function with its own erf approximation).
+__device__ __forceinline__ float gelu_as(float x) {
+  const float h = 0.5f * x;
+  return fmaf(h, erf_as(x * 0.7071067811865476f), h);
+}
+
 // Folded LayerNorm, consumer side: mean and 1/sqrt(var + eps) of row `row`
 // from its per-part (mean, M2) statistics (Chan et al.'s pairwise combination).
 __device__ __forceinline__ void ln_row(const GemmEpilogue& ep, int row, int M, float& mu, float& r) {
@@ -60,7 +88,9 @@ __device__ __forceinline__ void ln_row(const GemmEpilogue& ep, int row, int M, f
   float n = 0.f, mean = 0.f, m2 = 0.f;
   for (int p = 0; p < ep.ln_parts; p++) {
     const float2 v = ep.ln_stats[(int64_t)row * ep.ln_parts + p];
-    const float c = (float)min(ep.ln_part_cols, ep.ln_cols - p * ep.ln_part_cols);
+    const int ci = min(ep.ln_part_cols, ep.ln_cols - p * ep.ln_part_cols);
+    if (ci <= 0) break;
+    const float c = (float)ci;
     const float nn = n + c, d = v.x - mean;
     mean += d * (c / nn);
     m2 += v.y + d * d * (n * c / nn);
@@ -156,14 +186,17 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// Epilogue staging: per epilogue warp two 4 KB buffers holding a 32-row x 64-column
-// block in the 128-byte-swizzled layout the TMA store/load tensor maps use
-// (16-byte chunk c of row r at chunk position c ^ (r & 7)).
-constexpr uint32_t STG_BYTES = 4 * 2 * 4096;
+// Epilogue warps (two per TMEM lane quarter) and their staging: one 4 KB
+// buffer per warp holding a 32-row x 64-column block in the 128-byte-swizzled
+// layout the TMA store/load tensor maps use (16-byte chunk c of row r at
+// chunk position c ^ (r & 7)).
+constexpr int EPI_WARPS = 8;
+constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
+constexpr uint32_t STG_BYTES = EPI_WARPS * 4096;
 
 template <int STAGES, int BN>
 constexpr size_t gemm_smem_bytes(bool tma_epi) {
@@ -171,7 +204,7 @@ constexpr size_t gemm_smem_bytes(bool tma_epi) {
 }
 
 template <typename T, int BN, int STAGES, bool TMAE>
-__global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+__global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                                     const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                                                     const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -186,8 +219,8 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint64_t* rbar = tempty + 2;  // 8 residual-load barriers (2 per epilogue warp)
-  uint32_t* tmem_slot = (uint32_t*)(rbar + 8);
+  uint64_t* rbar = tempty + 2;  // residual-load barriers, one per epilogue warp
+  uint32_t* tmem_slot = (uint32_t*)(rbar + EPI_WARPS);
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -198,10 +231,10 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int r = 0; r < 8; r++) mbar_init(&rbar[r], 1);
+    for (int r = 0; r < EPI_WARPS; r++) mbar_init(&rbar[r], 1);
     for (int a = 0; a < 2; a++) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], EPI_WARPS);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -286,22 +319,25 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       }
     }
   } else if constexpr (TMAE) {
-    // ---------------- epilogue through shared memory + TMA (warps 2..5 -> TMEM lane quarter warp % 4)
-    // Each warp owns 32 rows of the tile. Per 64-column unit: tcgen05.ld the
-    // f32 accumulators, apply RoPE / bias / residual / GeGLU, write the row's
-    // 8 chunks into the swizzled staging buffer, and one lane issues a TMA
-    // store of the 32 x 64 block (rows >= M and columns >= N are clipped by
-    // the tensor map). The residual block arrives by TMA load into the same
-    // buffer. Two buffers per warp let a store drain while the next unit runs.
-    const int quarter = warp & 3;
+    // ---------------- epilogue through shared memory + TMA (warps 2..9 -> TMEM lane quarter warp % 4)
+    // Each warp owns 32 rows and half of the 64-column units of the tile. Per
+    // unit: tcgen05.ld the f32 accumulators, apply folded LayerNorm / RoPE /
+    // bias / residual / GeGLU, write the row's 8 chunks into the swizzled
+    // staging buffer, and one lane issues a TMA store of the 32 x 64 block
+    // (rows >= M and columns >= N are clipped by the tensor map). The
+    // residual block arrives by TMA load into the same buffer.
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     const GemmEpilogue& ep = args.ep;
     const bool geglu = ep.kind == EPI_GEGLU;
     const bool resid = ep.kind == EPI_RESIDUAL;
     const int ncols = geglu ? 2 * args.N : args.N;  // accumulator columns that hold data
-    uint8_t* stg0 = sE + quarter * 2 * 4096;
-    uint64_t* rb = rbar + quarter * 2;
-    uint32_t rph0 = 0, rph1 = 0;
-    int blk = 0;  // blocks stored so far by this warp (selects the buffer)
+    constexpr int U = BN / 64;
+    // this warp's units: halves of the tile (a GeGLU output block = an even/odd unit pair stays in one warp)
+    const int u_lo = (geglu && U == 2) ? (half ? U : 0) : half * (U / 2);
+    const int u_hi = (geglu && U == 2) ? U : (half + 1) * (U / 2);
+    uint8_t* stg = sE + (warp - 2) * 4096;
+    uint64_t* rb = rbar + (warp - 2);
+    uint32_t rph = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
@@ -315,21 +351,27 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       float ln_mu, ln_r;
       if (ep.ln_stats) ln_row(ep, row, args.M, ln_mu, ln_r);
       float st_n = 0.f, st_mean = 0.f, st_m2 = 0.f;
+      // RoPE: every head of q and k at this row uses the same 32 (cos, sin)
+      // pairs; pull them into L1 while the accumulator is read
+      const bool rope = ep.kind == EPI_ROPE_QKV && n0 + u_lo * 64 < ep.rope_cols;
+      const float* rcs = ep.rope_cs + (rope && row < args.M ? ep.pos[row] : 0);
+      if (rope) {
+#pragma unroll
+        for (int j = 0; j < 64; j++) asm volatile("prefetch.global.L1 [%0];" ::"l"(rcs + (int64_t)j * ep.rope_cap));
+      }
 #pragma unroll 1
-      for (int u = 0; u < BN / 64; u++) {
+      for (int u = u_lo; u < u_hi; u++) {
         const int col = n0 + u * 64;
         const bool first = !geglu || (u & 1) == 0;  // GeGLU: two units fill one 64-column output block
         const bool last = !geglu || (u & 1) == 1;
         const int bcol = geglu ? n0 + (u & ~1) * 64 : col;  // first accumulator column of the block
         if (bcol >= ncols) break;  // the rest of this tile is past the weight rows
-        const int buf = blk & 1;
-        uint8_t* stg = stg0 + buf * 4096;
-        if (first) {
-          if (lane == 0) bulk_wait_read1();  // the store that last used this buffer has read it
+        if (first && resid) {  // the residual block lands in the staging buffer
+          if (lane == 0) bulk_wait_read0();  // this warp's previous store has read the buffer
           __syncwarp();
-          if (resid && lane == 0) {
-            mbar_arrive_expect_tx(&rb[buf], 4096);
-            tma_load_2d(stg, &tmR, &rb[buf], col, row0);
+          if (lane == 0) {
+            mbar_arrive_expect_tx(rb, 4096);
+            tma_load_2d(stg, &tmR, rb, col, row0);
           }
         }
         uint32_t ra[32], rbv[32];
@@ -342,18 +384,15 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         if (ep.ln_stats) ln_apply(ep, col, ln_mu, ln_r, a, b);
         if (geglu) {
 #pragma unroll
-          for (int j = 0; j < 32; j++) a[j] = gelu_exact(a[j]) * b[j];
+          for (int j = 0; j < 32; j++) a[j] = gelu_as(a[j]) * b[j];
         } else {
-          if (ep.kind == EPI_ROPE_QKV && col < ep.rope_cols) {
-            const int p = row < args.M ? ep.pos[row] : 0;
-            const float* cs = ep.rope_cs + p;
-            const float* sn = ep.rope_cs + (int64_t)ep.rope_cap * 32 + p;
+          if (rope && col < ep.rope_cols) {
 #pragma unroll
             for (int j = 0; j < 32; j++) {
-              float c = __ldg(cs + (int64_t)j * ep.rope_cap), s = __ldg(sn + (int64_t)j * ep.rope_cap);
-              float x1 = a[j], x2 = b[j];
-              a[j] = x1 * c - x2 * s;
-              b[j] = x2 * c + x1 * s;
+              const float c = __ldg(rcs + (int64_t)j * ep.rope_cap), sn = __ldg(rcs + (int64_t)(32 + j) * ep.rope_cap);
+              const float x1 = a[j], x2 = b[j];
+              a[j] = x1 * c - x2 * sn;
+              b[j] = x2 * c + x1 * sn;
             }
           }
           if (args.bias) {
@@ -364,9 +403,8 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
             }
           }
           if (resid) {
-            const uint32_t ph = buf ? rph1 : rph0;
-            if (!mbar_wait(&rb[buf], ph, abort, &g_gemm_err)) { ok = false; break; }
-            if (buf) rph1 ^= 1; else rph0 ^= 1;
+            if (!mbar_wait(rb, rph, abort, &g_gemm_err)) { ok = false; break; }
+            rph ^= 1;
 #pragma unroll
             for (int c = 0; c < 8; c++) {
               uint4 v = *(const uint4*)(stg + lane * 128 + ((c ^ (lane & 7)) << 4));
@@ -379,6 +417,10 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
             }
             if (ep.stats_out) stats_unit<T>(a, b, st_n, st_mean, st_m2);
           }
+        }
+        if (first && !resid) {  // the previous store drained while this unit computed
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
         }
         // write this row's chunks: GeGLU writes 4 chunks (32 columns) per unit, else 8
         const int c0 = geglu ? (u & 1) * 4 : 0;
@@ -400,11 +442,11 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
             tma_store_2d(&tmY, stg, geglu ? bcol / 2 : col, row0);
             bulk_commit();
           }
-          blk++;
           if (geglu && (u & 1) == 0) break;  // the pair's second unit is past the weight rows
         }
       }
-      if (ep.stats_out && row < args.M) ep.stats_out[(int64_t)row * args.ntile_n + t % args.ntile_n] = make_float2(st_mean, st_m2);
+      if (ep.stats_out && row < args.M)
+        ep.stats_out[((int64_t)row * args.ntile_n + t % args.ntile_n) * 2 + half] = make_float2(st_mean, st_m2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -413,8 +455,9 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     if (lane == 0) bulk_wait_all();
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5 -> TMEM lane quarter warp % 4)
-    const int quarter = warp & 3;
+    // ---------------- epilogue (warps 2..9 -> TMEM lane quarter warp % 4, half of the units each)
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    constexpr int U = BN / 64;
     const bool vec = args.vec_ok != 0;
     T* Y = (T*)args.y;
     int acc = 0;
@@ -431,7 +474,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       if (args.ep.ln_stats) ln_row(args.ep, row, args.M, ln_mu, ln_r);
       float st_n = 0.f, st_mean = 0.f, st_m2 = 0.f;
 #pragma unroll 1
-      for (int u = 0; u < BN / 64; u++) {
+      for (int u = half * (U / 2); u < (half + 1) * (U / 2); u++) {
         uint32_t ra[32], rb[32];
         tmem_ld32(tbase + u * 64, ra);
         tmem_ld32(tbase + u * 64 + 32, rb);
@@ -482,7 +525,8 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         store32<T>(rowp, col, args.N, a, vec);
         store32<T>(rowp, col + 32, args.N, b, vec);
       }
-      if (args.ep.stats_out && live) args.ep.stats_out[(int64_t)row * args.ntile_n + t % args.ntile_n] = make_float2(st_mean, st_m2);
+      if (args.ep.stats_out && live)
+        args.ep.stats_out[((int64_t)row * args.ntile_n + t % args.ntile_n) * 2 + half] = make_float2(st_mean, st_m2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -549,7 +593,7 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap
     attr = true;
   }
   int grid = std::min(a.ntiles, lc::num_sms());
-  k_gemm_tc<T, BN, STAGES, TMAE><<<grid, 192, smem, st>>>(ma, mb, my, mr, a);
+  k_gemm_tc<T, BN, STAGES, TMAE><<<grid, GEMM_THREADS, smem, st>>>(ma, mb, my, mr, a);
 }
 
 }  // namespace
@@ -615,6 +659,8 @@ int gemm_tile_n(int64_t Nacc, bool geglu) {
   if (geglu && Nacc % BN) BN = 128;
   return BN;
 }
+
+int gemm_stats_part_cols(int64_t N) { return gemm_tile_n(N, false) / 2; }
 
 bool gemm_linear(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y, const GemmEpilogue& ep) {
   int64_t M = x2->shape[0], K = x2->shape[1], N = w->shape[0];

@@ -24,7 +24,7 @@ struct GemmEpilogue {
   // GEMM records row statistics of what it stores, and the projection that
   // consumes LayerNorm(y)·diag(γ) turns x·(W·diag(γ))ᵀ into the normalised
   // product: out = r·(acc − μ·wsum[n]) with μ, r = 1/sqrt(var + eps) of row m.
-  float2* stats_out = nullptr;       // EPI_RESIDUAL: (mean, M2) of the stored row over each N tile: [M][ntile_n]
+  float2* stats_out = nullptr;       // EPI_RESIDUAL: (mean, M2) of the stored row per gemm_stats_part_cols(N) columns
   const float2* ln_stats = nullptr;  // the statistics to apply: [M][ln_parts], ln_part_cols columns per part
   const float* ln_wsum = nullptr;    // Σ_k W[n, k]·γ[k] per accumulator column n (16-byte aligned)
   int ln_parts = 0, ln_part_cols = 0, ln_cols = 0;
@@ -40,6 +40,9 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
               int dtype, const GemmEpilogue& ep, cudaStream_t st);
 // N-tile width gemm_raw uses for an accumulator of Nacc columns.
 int gemm_tile_n(int64_t Nacc, bool geglu);
+// Row statistics of a residual GEMM (GemmEpilogue::stats_out) come in parts of
+// this many columns: [M][ceil(N / part)].
+int gemm_stats_part_cols(int64_t N);
 void linear_simt(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y);
 const float* rope_table(int D, double base, int L, int* cap_out, bool position_minor = false);
 bool attention_try_fast(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor* y);
