@@ -71,6 +71,38 @@ __device__ __forceinline__ float erf_as(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(ax * (ax * -1.4426950408889634f)));  // exp(−x²)
   return copysignf(fmaf(-q, e, 1.f), x);
 }
+// Two values of erf_as / gelu_as: the polynomial and the final products as packed pairs.
+__device__ __forceinline__ float2 gelu_as2(float2 x) {
+  const float2 z = mul2(x, make_float2(0.7071067811865476f, 0.7071067811865476f));
+  const float2 az = make_float2(fabsf(z.x), fabsf(z.y));
+  const float2 den = fma2(make_float2(0.3275911f, 0.3275911f), az, make_float2(1.f, 1.f));
+  float2 t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.x) : "f"(den.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.y) : "f"(den.y));
+  float2 q = fma2(make_float2(1.061405429f, 1.061405429f), t, make_float2(-1.453152027f, -1.453152027f));
+  q = fma2(q, t, make_float2(1.421413741f, 1.421413741f));
+  q = fma2(q, t, make_float2(-0.284496736f, -0.284496736f));
+  q = fma2(q, t, make_float2(0.254829592f, 0.254829592f));
+  q = mul2(q, t);
+  const float2 g = mul2(az, mul2(az, make_float2(-1.4426950408889634f, -1.4426950408889634f)));
+  float2 e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(g.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(g.y));
+  const float2 r = fma2(make_float2(-q.x, -q.y), e, make_float2(1.f, 1.f));  // erf(|z|)
+  const float2 erf = make_float2(copysignf(r.x, z.x), copysignf(r.y, z.y));
+  const float2 h = mul2(x, make_float2(0.5f, 0.5f));
+  return fma2(h, erf, h);
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float2 v) {
+  if constexpr (std::is_same<T, __half>::value) {
+    __half2 h = __floats2half2_rn(v.x, v.y);
+    return *(uint32_t*)&h;
+  } else {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+    return *(uint32_t*)&h;
+  }
+}
 // GELU with the erf above: 0.5·x·(1 + erf(x/√2)), the GeGLU activation of the
 // fused encoder (packages/backend-webgpu/src/kernels.ts:102 computes the same
 // function with its own erf approximation).
@@ -203,6 +235,170 @@ constexpr size_t gemm_smem_bytes(bool tma_epi) {
   return (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + (tma_epi ? STG_BYTES : 0) + 1024 + 256;
 }
 
+// The TMA-store epilogue of both GEMM kernels (warps 2..9 of the CTA). Tiles
+// t = t_begin, t_begin + t_step, ...; this CTA's rows of tile t start at
+// (t / ntile_n) * tile_rows + row_off. In a CTA pair the accumulator-free
+// arrivals go to the barrier of CTA 0, whose thread issues the MMAs.
+template <typename T, int BN, bool PAIR>
+__device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtensorMap* tmYp, const CUtensorMap* tmRp, uint8_t* sE, uint64_t* rbar,
+                                             uint64_t* tfull, uint64_t* tempty, volatile int* abort, uint32_t tmem, int warp, int lane,
+                                             int t_begin, int t_step, int tile_rows, int row_off) {
+  // Warps 2..9 -> TMEM lane quarter warp % 4. Each warp owns 32 rows and half
+  // of the 64-column units of the tile. Per unit: tcgen05.ld the f32
+  // accumulators, apply folded LayerNorm / RoPE / bias / residual / GeGLU
+  // (packed f32 pairs), write the row's 8 chunks into the swizzled staging
+  // buffer, and one lane issues a TMA store of the 32 x 64 block (rows >= M
+  // and columns >= N are clipped by the tensor map). The residual block
+  // arrives by TMA load into the same buffer. The per-row inputs of a tile
+  // (LayerNorm statistics, position) are read before its accumulator is ready.
+  const CUtensorMap& tmY = *tmYp;
+  const CUtensorMap& tmR = *tmRp;
+  const int quarter = warp & 3, half = (warp - 2) >> 2;
+  const GemmEpilogue& ep = args.ep;
+  const bool geglu = ep.kind == EPI_GEGLU;
+  const bool resid = ep.kind == EPI_RESIDUAL;
+  const int ncols = geglu ? 2 * args.N : args.N;  // accumulator columns that hold data
+  constexpr int U = BN / 64;
+  // this warp's units: halves of the tile (a GeGLU output block = an even/odd unit pair stays in one warp)
+  const int u_lo = (geglu && U == 2) ? (half ? U : 0) : half * (U / 2);
+  const int u_hi = (geglu && U == 2) ? U : (half + 1) * (U / 2);
+  uint8_t* stg = sE + (warp - 2) * 4096;
+  uint64_t* rb = rbar + (warp - 2);
+  uint32_t rph = 0;
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  bool ok = true;
+  for (int t = t_begin; t < args.ntiles && ok; t += t_step) {
+    const int m0 = (t / args.ntile_n) * tile_rows + row_off, n0 = (t % args.ntile_n) * BN;
+    const int row0 = m0 + quarter * 32;
+    const int row = row0 + lane;
+    float ln_mu = 0.f, ln_r = 1.f;
+    if (ep.ln_stats) ln_row(ep, row, args.M, ln_mu, ln_r);
+    const bool rope = ep.kind == EPI_ROPE_QKV && n0 + u_lo * 64 < ep.rope_cols;
+    // RoPE table [16][cap] of (cos 2i, cos 2i+1, sin 2i, sin 2i+1) at this row's position
+    const float4* rq = (const float4*)ep.rope_cs + (rope && row < args.M ? ep.pos[row] : 0);
+    if (!mbar_wait(&tfull[acc], acc_phase, abort, &g_gemm_err)) break;
+    tc_fence_after();
+    const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+    float st_n = 0.f, st_mean = 0.f, st_m2 = 0.f;
+#pragma unroll 1
+    for (int u = u_lo; u < u_hi; u++) {
+      const int col = n0 + u * 64;
+      const bool first = !geglu || (u & 1) == 0;  // GeGLU: two units fill one 64-column output block
+      const bool last = !geglu || (u & 1) == 1;
+      const int bcol = geglu ? n0 + (u & ~1) * 64 : col;  // first accumulator column of the block
+      if (bcol >= ncols) break;  // the rest of this tile is past the weight rows
+      if (first && resid) {  // the residual block lands in the staging buffer
+        if (lane == 0) bulk_wait_read0();  // this warp's previous store has read the buffer
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(rb, 4096);
+          tma_load_2d(stg, &tmR, rb, col, row0);
+        }
+      }
+      uint32_t ra[32], rbv[32];
+      tmem_ld32(tbase + u * 64, ra);
+      tmem_ld32(tbase + u * 64 + 32, rbv);
+      tmem_wait_ld();
+      // a = accumulator columns col..col+31, b = col+32..col+63, as packed pairs
+      float2 a[16], b[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        a[j] = make_float2(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
+        b[j] = make_float2(__uint_as_float(rbv[2 * j]), __uint_as_float(rbv[2 * j + 1]));
+      }
+      if (ep.ln_stats) {  // r·(acc − μ·wsum)
+        const float4* w4 = (const float4*)(ep.ln_wsum + col);
+        const float2 nmu = make_float2(-ln_mu, -ln_mu), r2 = make_float2(ln_r, ln_r);
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          const float4 w = __ldg(w4 + q), v = __ldg(w4 + 8 + q);
+          a[2 * q] = mul2(r2, fma2(nmu, make_float2(w.x, w.y), a[2 * q]));
+          a[2 * q + 1] = mul2(r2, fma2(nmu, make_float2(w.z, w.w), a[2 * q + 1]));
+          b[2 * q] = mul2(r2, fma2(nmu, make_float2(v.x, v.y), b[2 * q]));
+          b[2 * q + 1] = mul2(r2, fma2(nmu, make_float2(v.z, v.w), b[2 * q + 1]));
+        }
+      }
+      if (geglu) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) a[j] = mul2(gelu_as2(a[j]), b[j]);
+      } else {
+        if (rope && col < ep.rope_cols) {  // (x1, x2) -> (x1·cos − x2·sin, x2·cos + x1·sin)
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const float4 v = __ldg(rq + (int64_t)j * ep.rope_cap);
+            const float2 c = make_float2(v.x, v.y), sn = make_float2(v.z, v.w), nsn = make_float2(-v.z, -v.w);
+            const float2 x1 = a[j], x2 = b[j];
+            a[j] = fma2(x2, nsn, mul2(x1, c));
+            b[j] = fma2(x1, sn, mul2(x2, c));
+          }
+        }
+        if (args.bias) {
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const int c0 = col + 2 * j;
+            if (c0 < args.N) a[j].x += ld_as<float>((const char*)args.bias, args.bias_dtype, c0);
+            if (c0 + 1 < args.N) a[j].y += ld_as<float>((const char*)args.bias, args.bias_dtype, c0 + 1);
+            if (c0 + 32 < args.N) b[j].x += ld_as<float>((const char*)args.bias, args.bias_dtype, c0 + 32);
+            if (c0 + 33 < args.N) b[j].y += ld_as<float>((const char*)args.bias, args.bias_dtype, c0 + 33);
+          }
+        }
+        if (resid) {
+          if (!mbar_wait(rb, rph, abort, &g_gemm_err)) { ok = false; break; }
+          rph ^= 1;
+#pragma unroll
+          for (int c = 0; c < 8; c++) {
+            uint4 v = *(const uint4*)(stg + lane * 128 + ((c ^ (lane & 7)) << 4));
+            const T* h = (const T*)&v;
+            float2* dst = c < 4 ? a + c * 4 : b + (c - 4) * 4;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+              dst[j] = add2(dst[j], make_float2(TcFmt<T>::back(h[2 * j]), TcFmt<T>::back(h[2 * j + 1])));
+          }
+          if (ep.stats_out) stats_unit<T>((float*)a, (float*)b, st_n, st_mean, st_m2);
+        }
+      }
+      if (first && !resid) {  // the previous store drained while this unit computed
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+      }
+      // write this row's chunks: GeGLU writes 4 chunks (32 columns) per unit, else 8
+      const int c0 = geglu ? (u & 1) * 4 : 0;
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        if (geglu && c >= 4) break;
+        const float2* src = (c < 4) ? a + c * 4 : b + (c - 4) * 4;
+        uint4 v;
+        uint32_t* h = (uint32_t*)&v;
+#pragma unroll
+        for (int j = 0; j < 4; j++) h[j] = pack_pair<T>(src[j]);
+        const int cc = c0 + c;
+        *(uint4*)(stg + lane * 128 + ((cc ^ (lane & 7)) << 4)) = v;
+      }
+      if (last || bcol + 64 >= ncols) {
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmY, stg, geglu ? bcol / 2 : col, row0);
+          bulk_commit();
+        }
+        if (geglu && (u & 1) == 0) break;  // the pair's second unit is past the weight rows
+      }
+    }
+    if (ep.stats_out && row < args.M)
+      ep.stats_out[((int64_t)row * args.ntile_n + t % args.ntile_n) * 2 + half] = make_float2(st_mean, st_m2);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (PAIR) mbar_arrive_cluster(mapa_rank(smem_u32(&tempty[acc]), 0));  // the pair's MMA runs in CTA 0
+      else mbar_arrive(&tempty[acc]);
+    }
+    if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+  }
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
 template <typename T, int BN, int STAGES, bool TMAE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                                     const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
@@ -319,141 +515,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       }
     }
   } else if constexpr (TMAE) {
-    // ---------------- epilogue through shared memory + TMA (warps 2..9 -> TMEM lane quarter warp % 4)
-    // Each warp owns 32 rows and half of the 64-column units of the tile. Per
-    // unit: tcgen05.ld the f32 accumulators, apply folded LayerNorm / RoPE /
-    // bias / residual / GeGLU, write the row's 8 chunks into the swizzled
-    // staging buffer, and one lane issues a TMA store of the 32 x 64 block
-    // (rows >= M and columns >= N are clipped by the tensor map). The
-    // residual block arrives by TMA load into the same buffer.
-    const int quarter = warp & 3, half = (warp - 2) >> 2;
-    const GemmEpilogue& ep = args.ep;
-    const bool geglu = ep.kind == EPI_GEGLU;
-    const bool resid = ep.kind == EPI_RESIDUAL;
-    const int ncols = geglu ? 2 * args.N : args.N;  // accumulator columns that hold data
-    constexpr int U = BN / 64;
-    // this warp's units: halves of the tile (a GeGLU output block = an even/odd unit pair stays in one warp)
-    const int u_lo = (geglu && U == 2) ? (half ? U : 0) : half * (U / 2);
-    const int u_hi = (geglu && U == 2) ? U : (half + 1) * (U / 2);
-    uint8_t* stg = sE + (warp - 2) * 4096;
-    uint64_t* rb = rbar + (warp - 2);
-    uint32_t rph = 0;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
-      if (!mbar_wait(&tfull[acc], acc_phase, abort, &g_gemm_err)) break;
-      tc_fence_after();
-      const int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
-      const int row0 = m0 + quarter * 32;
-      const int row = row0 + lane;
-      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      float ln_mu, ln_r;
-      if (ep.ln_stats) ln_row(ep, row, args.M, ln_mu, ln_r);
-      float st_n = 0.f, st_mean = 0.f, st_m2 = 0.f;
-      // RoPE: every head of q and k at this row uses the same 32 (cos, sin)
-      // pairs; pull them into L1 while the accumulator is read
-      const bool rope = ep.kind == EPI_ROPE_QKV && n0 + u_lo * 64 < ep.rope_cols;
-      const float* rcs = ep.rope_cs + (rope && row < args.M ? ep.pos[row] : 0);
-      if (rope) {
-#pragma unroll
-        for (int j = 0; j < 64; j++) asm volatile("prefetch.global.L1 [%0];" ::"l"(rcs + (int64_t)j * ep.rope_cap));
-      }
-#pragma unroll 1
-      for (int u = u_lo; u < u_hi; u++) {
-        const int col = n0 + u * 64;
-        const bool first = !geglu || (u & 1) == 0;  // GeGLU: two units fill one 64-column output block
-        const bool last = !geglu || (u & 1) == 1;
-        const int bcol = geglu ? n0 + (u & ~1) * 64 : col;  // first accumulator column of the block
-        if (bcol >= ncols) break;  // the rest of this tile is past the weight rows
-        if (first && resid) {  // the residual block lands in the staging buffer
-          if (lane == 0) bulk_wait_read0();  // this warp's previous store has read the buffer
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive_expect_tx(rb, 4096);
-            tma_load_2d(stg, &tmR, rb, col, row0);
-          }
-        }
-        uint32_t ra[32], rbv[32];
-        tmem_ld32(tbase + u * 64, ra);
-        tmem_ld32(tbase + u * 64 + 32, rbv);
-        tmem_wait_ld();
-        float a[32], b[32];
-#pragma unroll
-        for (int j = 0; j < 32; j++) a[j] = __uint_as_float(ra[j]), b[j] = __uint_as_float(rbv[j]);
-        if (ep.ln_stats) ln_apply(ep, col, ln_mu, ln_r, a, b);
-        if (geglu) {
-#pragma unroll
-          for (int j = 0; j < 32; j++) a[j] = gelu_as(a[j]) * b[j];
-        } else {
-          if (rope && col < ep.rope_cols) {
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-              const float c = __ldg(rcs + (int64_t)j * ep.rope_cap), sn = __ldg(rcs + (int64_t)(32 + j) * ep.rope_cap);
-              const float x1 = a[j], x2 = b[j];
-              a[j] = x1 * c - x2 * sn;
-              b[j] = x2 * c + x1 * sn;
-            }
-          }
-          if (args.bias) {
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-              if (col + j < args.N) a[j] += ld_as<float>((const char*)args.bias, args.bias_dtype, col + j);
-              if (col + 32 + j < args.N) b[j] += ld_as<float>((const char*)args.bias, args.bias_dtype, col + 32 + j);
-            }
-          }
-          if (resid) {
-            if (!mbar_wait(rb, rph, abort, &g_gemm_err)) { ok = false; break; }
-            rph ^= 1;
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-              uint4 v = *(const uint4*)(stg + lane * 128 + ((c ^ (lane & 7)) << 4));
-              const T* h = (const T*)&v;
-#pragma unroll
-              for (int j = 0; j < 8; j++) {
-                if (c < 4) a[c * 8 + j] += TcFmt<T>::back(h[j]);
-                else b[(c - 4) * 8 + j] += TcFmt<T>::back(h[j]);
-              }
-            }
-            if (ep.stats_out) stats_unit<T>(a, b, st_n, st_mean, st_m2);
-          }
-        }
-        if (first && !resid) {  // the previous store drained while this unit computed
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-        }
-        // write this row's chunks: GeGLU writes 4 chunks (32 columns) per unit, else 8
-        const int c0 = geglu ? (u & 1) * 4 : 0;
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          if (geglu && c >= 4) break;
-          const float* src = (c < 4) ? a + c * 8 : b + (c - 4) * 8;
-          uint4 v;
-          T* h = (T*)&v;
-#pragma unroll
-          for (int j = 0; j < 8; j++) h[j] = TcFmt<T>::cvt(src[j]);
-          const int cc = c0 + c;
-          *(uint4*)(stg + lane * 128 + ((cc ^ (lane & 7)) << 4)) = v;
-        }
-        if (last || bcol + 64 >= ncols) {
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmY, stg, geglu ? bcol / 2 : col, row0);
-            bulk_commit();
-          }
-          if (geglu && (u & 1) == 0) break;  // the pair's second unit is past the weight rows
-        }
-      }
-      if (ep.stats_out && row < args.M)
-        ep.stats_out[((int64_t)row * args.ntile_n + t % args.ntile_n) * 2 + half] = make_float2(st_mean, st_m2);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-    }
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
+    epilogue_tma<T, BN, false>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x, gridDim.x, BM, 0);
   } else {
     // ---------------- epilogue (warps 2..9 -> TMEM lane quarter warp % 4, half of the units each)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
@@ -493,15 +555,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
           continue;
         }
         if (ep.kind == EPI_ROPE_QKV && col < ep.rope_cols) {
-          const int p = ep.pos[row];
-          const float* cs = ep.rope_cs + p;
-          const float* sn = ep.rope_cs + (int64_t)ep.rope_cap * 32 + p;
+          const float4* rq = (const float4*)ep.rope_cs + ep.pos[row];
 #pragma unroll
           for (int j = 0; j < 32; j++) {
-            float c = __ldg(cs + (int64_t)j * ep.rope_cap), s = __ldg(sn + (int64_t)j * ep.rope_cap);
-            float x1 = a[j], x2 = b[j];
-            a[j] = x1 * c - x2 * s;
-            b[j] = x2 * c + x1 * s;
+            const float4 v = __ldg(rq + (int64_t)(j >> 1) * ep.rope_cap);
+            const float c = (j & 1) ? v.y : v.x, sn = (j & 1) ? v.w : v.z;
+            const float x1 = a[j], x2 = b[j];
+            a[j] = x1 * c - x2 * sn;
+            b[j] = x2 * c + x1 * sn;
           }
         }
         if (args.bias) {
@@ -538,6 +599,156 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+
+// CTA-pair GEMM (cluster of two CTAs, tcgen05 cta_group::2): a pair computes a
+// 256 x 256 output tile. Each CTA loads its 128 rows of x and its 128 of the
+// tile's 256 rows of w per 64-wide k-step (32 KB, half the weight bytes per
+// CTA of the single-CTA kernel) and keeps its 128 x 256 accumulator in its
+// own TMEM. The thread of CTA 0 issues the M = 256 MMAs for both; the loads
+// of both CTAs complete on CTA 0's full barrier, and every MMA commit arrives
+// on the empty / accumulator-full barriers of both CTAs. The epilogue is the
+// single-CTA one on each CTA's rows. No load is multicast.
+template <int STAGES>
+constexpr size_t gemm_pair_smem_bytes() {
+  return (size_t)STAGES * (BM * BK * 2 + 128 * BK * 2) + STG_BYTES + 1024 + 256;
+}
+
+template <typename T, int STAGES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                                           const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
+                                                           const __grid_constant__ GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  constexpr int BN = 256;
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = 128 * BK * 2;  // this CTA's half of the tile's w rows
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sE = sB + STAGES * B_BYTES;
+  uint64_t* full = (uint64_t*)(sE + STG_BYTES);  // used in CTA 0
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;  // used in CTA 0: both CTAs' epilogue warps arrive
+  uint64_t* rbar = tempty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(rbar + EPI_WARPS);
+  volatile int* abort = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = (args.K + BK - 1) / BK;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < EPI_WARPS; r++) mbar_init(&rbar[r], 1);
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {  // the same warp of both CTAs: one allocation at the same TMEM address in each
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival or copy
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
+      const uint32_t full0 = mapa_rank(smem_u32(full), 0);  // CTA 0's full[0]
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int issued[STAGES];
+      uint32_t iss_phase[STAGES];
+      for (int s = 0; s < STAGES; s++) issued[s] = 0, iss_phase[s] = 0;
+      for (int t = pair; t < args.ntiles && ok; t += npairs) {
+        const int m0 = (t / args.ntile_n) * (2 * BM) + rank * BM, n0 = (t % args.ntile_n) * BN + rank * 128;
+        for (int kb = 0; kb < KB; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
+          tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full0 + 8 * stage, kb * BK, m0);
+          tma_load_2d_pair(sB + stage * B_BYTES, &tmB, full0 + 8 * stage, kb * BK, n0);
+          issued[stage] = 1;
+          iss_phase[stage] = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: each stage's last fill has been consumed by the pair's MMAs (so it landed)
+      for (int s = 0; s < STAGES; s++)
+        if (issued[s]) {
+          uint64_t t0 = gtimer();
+          bool done;
+          while (!(done = mbar_try_wait(&empty[s], iss_phase[s])) && gtimer() - t0 < kWaitNs) {}
+          if (!done) *abort = 1;
+        }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (CTA 0 only)
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = idesc_f16<T, BN, 256>();
+      const uint64_t dA0 = sdesc_sw128(smem_u32(sA)), dB0 = sdesc_sw128(smem_u32(sB));
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      uint64_t* last = nullptr;
+      uint32_t last_phase = 0;
+      for (int t = pair; t < args.ntiles && ok; t += npairs) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < KB; kb++) {
+          if (!mbar_wait(&full[stage], phase, abort, &g_gemm_err)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t da = dA0 + ((stage * A_BYTES) >> 4), db = dB0 + ((stage * B_BYTES) >> 4);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++) tc_mma_pair(d, da + k * 2, db + k * 2, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair(&empty[stage]);
+          last = &empty[stage];
+          last_phase = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit_pair(&tfull[acc]);
+        last = &tfull[acc];
+        last_phase = acc_phase;
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      // drain: the MMAs issued here finish before TMEM is freed
+      if (last) {
+        uint64_t t0 = gtimer();
+        while (!mbar_try_wait(last, last_phase) && gtimer() - t0 < kWaitNs) {}
+      }
+    }
+  } else {
+    epilogue_tma<T, BN, true>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, pair, npairs, 2 * BM, (int)rank * BM);
+  }
+  if (threadIdx.x == 0 && *abort) {  // after a timeout, let copies still in flight land before the pair exits
+    const uint64_t t0 = gtimer();
+    while (gtimer() - t0 < 1000000ull) {}
+  }
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its partner may still read its shared memory or arrive on its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -596,9 +807,49 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap
   k_gemm_tc<T, BN, STAGES, TMAE><<<grid, GEMM_THREADS, smem, st>>>(ma, mb, my, mr, a);
 }
 
+template <typename T, int STAGES>
+void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr, GemmArgs a, cudaStream_t st) {
+  constexpr size_t smem = gemm_pair_smem_bytes<STAGES>();
+  static_assert(smem <= 232448, "GEMM shared memory above the 227 KB per-CTA limit");
+  static int max_pairs = 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (!max_pairs) {
+    CUDA_OK(cudaFuncSetAttribute(k_gemm_pair<T, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cfg.gridDim = dim3(2 * (lc::num_sms() / 2));
+    int n = 0;
+    CUDA_OK(cudaOccupancyMaxActiveClusters(&n, k_gemm_pair<T, STAGES>, &cfg));
+    LC_CHECK(n > 0, "tcgen05 GEMM: no CTA pair fits an SM pair");
+    max_pairs = n;
+  }
+  const int pairs = std::min(a.ntiles, max_pairs);
+  cfg.gridDim = dim3(2 * pairs);
+  CUDA_OK(cudaLaunchKernelEx(&cfg, k_gemm_pair<T, STAGES>, ma, mb, my, mr, a));
+}
+
 }  // namespace
 
 namespace lc {
+
+// CTA pairs pay off when the main loop is long against the epilogue (K >= 1024
+// on the encoder's shapes); LAYA_CUDA_GEMM_PAIR=0 / =1 forces either kernel.
+bool gemm_use_pair(int64_t K) {
+  static int force = -2;
+  if (force == -2) {
+    const char* v = getenv("LAYA_CUDA_GEMM_PAIR");
+    force = v ? (v[0] == '0' ? 0 : 1) : -1;
+  }
+  return force >= 0 ? force == 1 : K >= 1024;
+}
 
 bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, const void* bias, int bias_dtype, void* y, int64_t ldy,
               int dtype, const GemmEpilogue& ep, cudaStream_t st) {
@@ -631,7 +882,17 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
   const CUtensorMap& mb = tensor_map(w, Nacc, K, K, BK, BN, dtype);
   // TMA-store epilogue when the output (and residual) rows are 16-byte strided and aligned
   const bool tmae = a.vec_ok && (N % 8 == 0) && !(ep.kind == EPI_RESIDUAL && ep.resid == nullptr);
-  if (tmae) {
+  if (tmae && BN == 256 && gemm_use_pair(K)) {
+    // CTA pairs: 256 x 256 tiles
+    const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
+    const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
+    const CUtensorMap& mbp = tensor_map(w, Nacc, K, K, BK, 128, dtype);
+    GemmArgs ap = a;
+    const int64_t ptiles = ((M + 2 * BM - 1) / (2 * BM)) * a.ntile_n;
+    ap.ntiles = (int)ptiles;
+    if (dtype == LC_F16) launch_gemm_pair<__half, 6>(ma, mbp, my, mr, ap, st);
+    else launch_gemm_pair<__nv_bfloat16, 6>(ma, mbp, my, mr, ap, st);
+  } else if (tmae) {
     const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
     const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
     if (dtype == LC_F16) {

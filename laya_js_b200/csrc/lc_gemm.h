@@ -17,7 +17,7 @@ struct GemmEpilogue {
   const void* resid = nullptr;      // EPI_RESIDUAL: [M, N] in the output dtype, row stride ldr
   int64_t ldr = 0;
   const int32_t* pos = nullptr;     // EPI_ROPE_QKV: position of each row
-  const float* rope_cs = nullptr;   // EPI_ROPE_QKV: cos/sin table [32][cap] ++ [32][cap] (position-minor)
+  const float* rope_cs = nullptr;   // EPI_ROPE_QKV: table [16][cap] of float4 (cos 2i, cos 2i+1, sin 2i, sin 2i+1)
   int rope_cap = 0;
   int rope_cols = 0;                // EPI_ROPE_QKV: columns [0, rope_cols) are rotated (q and k), head dim 64
   // LayerNorm folded into the next projection (the fused encoder): a residual

@@ -210,8 +210,10 @@ std::map<std::tuple<int, double, bool>, RopeTable>& rope_cache() {
 
 namespace lc {
 // cos/sin table (f32) for head dim D and `base`, cap >= L positions:
-// [cap][half] cos ++ [cap][half] sin, or with position_minor [half][cap] ++ [half][cap]
-// (what the GEMM epilogue reads: a warp's 32 rows are consecutive positions).
+// [cap][half] cos ++ [cap][half] sin, or with position_minor the GEMM
+// epilogue's layout [half/2][cap] of float4 (cos 2i, cos 2i+1, sin 2i,
+// sin 2i+1): a warp's 32 rows are (mostly) consecutive positions, so each
+// 16-byte load of the warp reads one contiguous run.
 const float* rope_table(int D, double base, int L, int* cap_out, bool position_minor) {
   auto& t = rope_cache()[{D, base, position_minor}];
   if (t.cap < L) {
@@ -225,9 +227,15 @@ const float* rope_table(int D, double base, int L, int* cap_out, bool position_m
       float inv = (float)std::pow(2.0, (double)e);
       for (int l = 0; l < cap; l++) {
         float th = (float)((double)l * (double)inv);
-        size_t ci = position_minor ? (size_t)i * cap + l : (size_t)l * half + i;
-        h[ci] = (float)std::cos((double)th);
-        h[(size_t)cap * half + ci] = (float)std::sin((double)th);
+        if (position_minor) {
+          const size_t base = ((size_t)(i / 2) * cap + l) * 4 + (i & 1);
+          h[base] = (float)std::cos((double)th);
+          h[base + 2] = (float)std::sin((double)th);
+        } else {
+          const size_t ci = (size_t)l * half + i;
+          h[ci] = (float)std::cos((double)th);
+          h[(size_t)cap * half + ci] = (float)std::sin((double)th);
+        }
       }
     }
     if (t.d) CUDA_OK(cudaFree(t.d));
