@@ -53,25 +53,14 @@ struct GemmArgs {
 
 __device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
 
-// erf(x) by the rational approximation of Abramowitz & Stegun, Handbook of
-// Mathematical Functions (1964), eq. 7.1.26 (after C. Hastings):
-// erf(x) = 1 − (a1·t + a2·t² + a3·t³ + a4·t⁴ + a5·t⁵)·exp(−x²), t = 1/(1 + p·x),
-// x >= 0, |error| <= 1.5e-7, odd extension for x < 0. Two MUFU operations
-// (reciprocal, exp2) and six FMAs per value.
-__device__ __forceinline__ float erf_as(float x) {
-  const float ax = fabsf(x);
-  float t;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.f)));
-  float q = fmaf(1.061405429f, t, -1.453152027f);
-  q = fmaf(q, t, 1.421413741f);
-  q = fmaf(q, t, -0.284496736f);
-  q = fmaf(q, t, 0.254829592f);
-  q *= t;
-  float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(ax * (ax * -1.4426950408889634f)));  // exp(−x²)
-  return copysignf(fmaf(-q, e, 1.f), x);
-}
-// Two values of erf_as / gelu_as: the polynomial and the final products as packed pairs.
+// GELU, 0.5·x·(1 + erf(x/√2)), the GeGLU activation of the fused encoder
+// (packages/backend-webgpu/src/kernels.ts:102 computes the same function with
+// its own erf approximation), for two values as packed pairs. erf(z) by the
+// rational approximation of Abramowitz & Stegun, Handbook of Mathematical
+// Functions (1964), eq. 7.1.26 (after C. Hastings):
+// erf(z) = 1 − (a1·t + a2·t² + a3·t³ + a4·t⁴ + a5·t⁵)·exp(−z²), t = 1/(1 + p·z),
+// z >= 0, |error| <= 1.5e-7, odd extension for z < 0. Two MUFU operations
+// (reciprocal, exp2) per value.
 __device__ __forceinline__ float2 gelu_as2(float2 x) {
   const float2 z = mul2(x, make_float2(0.7071067811865476f, 0.7071067811865476f));
   const float2 az = make_float2(fabsf(z.x), fabsf(z.y));
@@ -103,33 +92,30 @@ __device__ __forceinline__ uint32_t pack_pair(float2 v) {
     return *(uint32_t*)&h;
   }
 }
-// GELU with the erf above: 0.5·x·(1 + erf(x/√2)), the GeGLU activation of the
-// fused encoder (packages/backend-webgpu/src/kernels.ts:102 computes the same
-// function with its own erf approximation).
-__device__ __forceinline__ float gelu_as(float x) {
-  const float h = 0.5f * x;
-  return fmaf(h, erf_as(x * 0.7071067811865476f), h);
-}
 
 // Folded LayerNorm, consumer side: mean and 1/sqrt(var + eps) of row `row`
 // from its per-part (mean, M2) statistics (Chan et al.'s pairwise combination).
+// One pass over the parts, shifted by the first part's mean K for accuracy:
+// S1 = Σ c_p·(mean_p − K), S2 = Σ (M2_p + c_p·(mean_p − K)²),
+// mean = K + S1/n, M2 = S2 − S1²/n.
+constexpr int LN_MAX_PARTS = 64;
 __device__ __forceinline__ void ln_row(const GemmEpilogue& ep, int row, int M, float& mu, float& r) {
   mu = 0.f;
   r = 1.f;
   if (row >= M) return;
-  float n = 0.f, mean = 0.f, m2 = 0.f;
+  const float2* st = ep.ln_stats + (int64_t)row * ep.ln_parts;
+  const float inv_n = 1.f / (float)ep.ln_cols;
+  const float k0 = st[0].x;
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll 8
   for (int p = 0; p < ep.ln_parts; p++) {
-    const float2 v = ep.ln_stats[(int64_t)row * ep.ln_parts + p];
-    const int ci = min(ep.ln_part_cols, ep.ln_cols - p * ep.ln_part_cols);
-    if (ci <= 0) break;
-    const float c = (float)ci;
-    const float nn = n + c, d = v.x - mean;
-    mean += d * (c / nn);
-    m2 += v.y + d * d * (n * c / nn);
-    n = nn;
+    const float2 v = st[p];
+    const float c = (float)min(ep.ln_part_cols, ep.ln_cols - p * ep.ln_part_cols), d = v.x - k0;
+    s1 = fmaf(c, d, s1);
+    s2 += fmaf(c * d, d, v.y);
   }
-  mu = mean;
-  r = rsqrtf(fmaxf(m2, 0.f) / (float)ep.ln_cols + ep.ln_eps);
+  mu = fmaf(s1, inv_n, k0);
+  r = rsqrtf(fmaxf(fmaf(-s1 * s1, inv_n, s2), 0.f) * inv_n + ep.ln_eps);
 }
 // acc columns [col, col+64) -> r·(acc − μ·wsum)
 __device__ __forceinline__ void ln_apply(const GemmEpilogue& ep, int col, float mu, float r, float* a, float* b) {
@@ -219,6 +205,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -239,18 +226,22 @@ constexpr size_t gemm_smem_bytes(bool tma_epi) {
 // t = t_begin, t_begin + t_step, ...; this CTA's rows of tile t start at
 // (t / ntile_n) * tile_rows + row_off. In a CTA pair the accumulator-free
 // arrivals go to the barrier of CTA 0, whose thread issues the MMAs.
-template <typename T, int BN, bool PAIR>
+//
+// Warps 2..9 -> TMEM lane quarter warp % 4. Each warp owns 32 rows and half
+// of the 64-column units of the tile. Per unit: tcgen05.ld the f32
+// accumulators, apply folded LayerNorm / RoPE / bias / residual / GeGLU
+// (packed f32 pairs), write the row's 8 chunks into a swizzled staging
+// buffer, and one lane issues a TMA store of the 32 x 64 block (rows >= M and
+// columns >= N are clipped by the tensor map). The residual block arrives by
+// TMA load into the buffer its result is stored from. With NBUF = 2 staging
+// buffers per warp, both of a tile's residual blocks are requested before
+// its accumulator is ready, and a store drains while the next unit computes.
+// The tile's LayerNorm statistics and the first unit's LayerNorm column sums
+// (one coalesced load per warp, shared by shuffles) are read ahead as well.
+template <typename T, int BN, bool PAIR, int NBUF>
 __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtensorMap* tmYp, const CUtensorMap* tmRp, uint8_t* sE, uint64_t* rbar,
                                              uint64_t* tfull, uint64_t* tempty, volatile int* abort, uint32_t tmem, int warp, int lane,
                                              int t_begin, int t_step, int tile_rows, int row_off) {
-  // Warps 2..9 -> TMEM lane quarter warp % 4. Each warp owns 32 rows and half
-  // of the 64-column units of the tile. Per unit: tcgen05.ld the f32
-  // accumulators, apply folded LayerNorm / RoPE / bias / residual / GeGLU
-  // (packed f32 pairs), write the row's 8 chunks into the swizzled staging
-  // buffer, and one lane issues a TMA store of the 32 x 64 block (rows >= M
-  // and columns >= N are clipped by the tensor map). The residual block
-  // arrives by TMA load into the same buffer. The per-row inputs of a tile
-  // (LayerNorm statistics, position) are read before its accumulator is ready.
   const CUtensorMap& tmY = *tmYp;
   const CUtensorMap& tmR = *tmRp;
   const int quarter = warp & 3, half = (warp - 2) >> 2;
@@ -262,21 +253,38 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
   // this warp's units: halves of the tile (a GeGLU output block = an even/odd unit pair stays in one warp)
   const int u_lo = (geglu && U == 2) ? (half ? U : 0) : half * (U / 2);
   const int u_hi = (geglu && U == 2) ? U : (half + 1) * (U / 2);
-  uint8_t* stg = sE + (warp - 2) * 4096;
-  uint64_t* rb = rbar + (warp - 2);
-  uint32_t rph = 0;
+  static_assert(NBUF == 1 || U / 2 <= 2, "two staging buffers cover at most two units per warp and tile");
+  uint8_t* stg0 = sE + (warp - 2) * NBUF * 4096;
+  uint64_t* rb0 = rbar + (warp - 2) * NBUF;
+  uint32_t rph[NBUF];
+#pragma unroll
+  for (int i = 0; i < NBUF; i++) rph[i] = 0;
   int acc = 0;
   uint32_t acc_phase = 0;
   bool ok = true;
+  uint32_t nstore = 0;  // TMA stores issued by this warp
   for (int t = t_begin; t < args.ntiles && ok; t += t_step) {
     const int m0 = (t / args.ntile_n) * tile_rows + row_off, n0 = (t % args.ntile_n) * BN;
     const int row0 = m0 + quarter * 32;
     const int row = row0 + lane;
+    const bool live = row < args.M;
     float ln_mu = 0.f, ln_r = 1.f;
     if (ep.ln_stats) ln_row(ep, row, args.M, ln_mu, ln_r);
     const bool rope = ep.kind == EPI_ROPE_QKV && n0 + u_lo * 64 < ep.rope_cols;
-    // RoPE table [16][cap] of (cos 2i, cos 2i+1, sin 2i, sin 2i+1) at this row's position
-    const float4* rq = (const float4*)ep.rope_cs + (rope && row < args.M ? ep.pos[row] : 0);
+    // this row's RoPE factors: table [16][cap] of (cos 2i, cos 2i+1, sin 2i, sin 2i+1)
+    const float4* rq = (const float4*)ep.rope_cs + (rope && live ? ep.pos[row] : 0);
+    // the first unit's LayerNorm column sums (lane l: columns 2l, 2l+1)
+    float2 wsp = make_float2(0.f, 0.f);
+    if (ep.ln_stats) wsp = __ldg((const float2*)(ep.ln_wsum + n0 + u_lo * 64) + lane);
+    if (NBUF == 2 && resid) {  // both residual blocks, in flight while the accumulator is computed
+      if (lane == 0) bulk_wait_read0();  // earlier stores have read both buffers
+      __syncwarp();
+      if (lane == 0)
+        for (int i = 0; i < 2 && u_lo + i < u_hi && n0 + (u_lo + i) * 64 < ncols; i++) {
+          mbar_arrive_expect_tx(&rb0[i], 4096);
+          tma_load_2d(stg0 + i * 4096, &tmR, &rb0[i], n0 + (u_lo + i) * 64, row0);
+        }
+    }
     if (!mbar_wait(&tfull[acc], acc_phase, abort, &g_gemm_err)) break;
     tc_fence_after();
     const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
@@ -288,12 +296,17 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
       const bool last = !geglu || (u & 1) == 1;
       const int bcol = geglu ? n0 + (u & ~1) * 64 : col;  // first accumulator column of the block
       if (bcol >= ncols) break;  // the rest of this tile is past the weight rows
-      if (first && resid) {  // the residual block lands in the staging buffer
+      const bool more = u + 1 < u_hi && (geglu ? n0 + ((u + 1) & ~1) * 64 : col + 64) < ncols;
+      // staging buffer: the one; with two, the residual's (chosen per unit at the
+      // tile start), else alternating with this warp's stores
+      const int bi = NBUF == 1 ? 0 : (resid ? u - u_lo : (nstore & 1));
+      uint8_t* stg = stg0 + bi * 4096;
+      if (NBUF == 1 && first && resid) {  // the residual block lands in the staging buffer
         if (lane == 0) bulk_wait_read0();  // this warp's previous store has read the buffer
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive_expect_tx(rb, 4096);
-          tma_load_2d(stg, &tmR, rb, col, row0);
+          mbar_arrive_expect_tx(&rb0[0], 4096);
+          tma_load_2d(stg, &tmR, &rb0[0], col, row0);
         }
       }
       uint32_t ra[32], rbv[32];
@@ -307,17 +320,16 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
         a[j] = make_float2(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
         b[j] = make_float2(__uint_as_float(rbv[2 * j]), __uint_as_float(rbv[2 * j + 1]));
       }
-      if (ep.ln_stats) {  // r·(acc − μ·wsum)
-        const float4* w4 = (const float4*)(ep.ln_wsum + col);
+      if (ep.ln_stats) {  // r·(acc − μ·wsum); wsum of columns col+2j, col+2j+1 sits in lane j
         const float2 nmu = make_float2(-ln_mu, -ln_mu), r2 = make_float2(ln_r, ln_r);
 #pragma unroll
-        for (int q = 0; q < 8; q++) {
-          const float4 w = __ldg(w4 + q), v = __ldg(w4 + 8 + q);
-          a[2 * q] = mul2(r2, fma2(nmu, make_float2(w.x, w.y), a[2 * q]));
-          a[2 * q + 1] = mul2(r2, fma2(nmu, make_float2(w.z, w.w), a[2 * q + 1]));
-          b[2 * q] = mul2(r2, fma2(nmu, make_float2(v.x, v.y), b[2 * q]));
-          b[2 * q + 1] = mul2(r2, fma2(nmu, make_float2(v.z, v.w), b[2 * q + 1]));
+        for (int j = 0; j < 16; j++) {
+          const float2 wa = make_float2(__shfl_sync(0xffffffffu, wsp.x, j), __shfl_sync(0xffffffffu, wsp.y, j));
+          const float2 wb = make_float2(__shfl_sync(0xffffffffu, wsp.x, 16 + j), __shfl_sync(0xffffffffu, wsp.y, 16 + j));
+          a[j] = mul2(r2, fma2(nmu, wa, a[j]));
+          b[j] = mul2(r2, fma2(nmu, wb, b[j]));
         }
+        if (more) wsp = __ldg((const float2*)(ep.ln_wsum + col + 64) + lane);
       }
       if (geglu) {
 #pragma unroll
@@ -344,8 +356,8 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
           }
         }
         if (resid) {
-          if (!mbar_wait(rb, rph, abort, &g_gemm_err)) { ok = false; break; }
-          rph ^= 1;
+          if (!mbar_wait(&rb0[bi], rph[bi], abort, &g_gemm_err)) { ok = false; break; }
+          rph[bi] ^= 1;
 #pragma unroll
           for (int c = 0; c < 8; c++) {
             uint4 v = *(const uint4*)(stg + lane * 128 + ((c ^ (lane & 7)) << 4));
@@ -358,8 +370,11 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
           if (ep.stats_out) stats_unit<T>((float*)a, (float*)b, st_n, st_mean, st_m2);
         }
       }
-      if (first && !resid) {  // the previous store drained while this unit computed
-        if (lane == 0) bulk_wait_read0();
+      if (first && !resid) {  // the store that last used this buffer has read it
+        if (lane == 0) {
+          if (NBUF == 1) bulk_wait_read0();
+          else bulk_wait_read1();
+        }
         __syncwarp();
       }
       // write this row's chunks: GeGLU writes 4 chunks (32 columns) per unit, else 8
@@ -382,10 +397,11 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
           tma_store_2d(&tmY, stg, geglu ? bcol / 2 : col, row0);
           bulk_commit();
         }
+        nstore++;
         if (geglu && (u & 1) == 0) break;  // the pair's second unit is past the weight rows
       }
     }
-    if (ep.stats_out && row < args.M)
+    if (ep.stats_out && live)
       ep.stats_out[((int64_t)row * args.ntile_n + t % args.ntile_n) * 2 + half] = make_float2(st_mean, st_m2);
     tc_fence_before();
     __syncwarp();
@@ -515,7 +531,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       }
     }
   } else if constexpr (TMAE) {
-    epilogue_tma<T, BN, false>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x, gridDim.x, BM, 0);
+    epilogue_tma<T, BN, false, 1>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x, gridDim.x, BM, 0);
   } else {
     // ---------------- epilogue (warps 2..9 -> TMEM lane quarter warp % 4, half of the units each)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
@@ -594,6 +610,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   }
+  if (threadIdx.x == 0 && *abort) {  // after a timeout, let copies still in flight land before the CTA exits
+    const uint64_t t0 = gtimer();
+    while (gtimer() - t0 < 1000000ull) {}
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -613,7 +633,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
 // single-CTA one on each CTA's rows. No load is multicast.
 template <int STAGES>
 constexpr size_t gemm_pair_smem_bytes() {
-  return (size_t)STAGES * (BM * BK * 2 + 128 * BK * 2) + STG_BYTES + 1024 + 256;
+  return (size_t)STAGES * (BM * BK * 2 + 128 * BK * 2) + 2 * STG_BYTES + 1024 + 512;
 }
 
 template <typename T, int STAGES>
@@ -628,13 +648,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_pair(const __grid_cons
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sE = sB + STAGES * B_BYTES;
-  uint64_t* full = (uint64_t*)(sE + STG_BYTES);  // used in CTA 0
+  uint8_t* sE = sB + STAGES * B_BYTES;            // two staging buffers per epilogue warp
+  uint64_t* full = (uint64_t*)(sE + 2 * STG_BYTES);  // used in CTA 0
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;  // used in CTA 0: both CTAs' epilogue warps arrive
-  uint64_t* rbar = tempty + 2;
-  uint32_t* tmem_slot = (uint32_t*)(rbar + EPI_WARPS);
+  uint64_t* rbar = tempty + 2;   // two per epilogue warp
+  uint32_t* tmem_slot = (uint32_t*)(rbar + 2 * EPI_WARPS);
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -647,7 +667,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_pair(const __grid_cons
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int r = 0; r < EPI_WARPS; r++) mbar_init(&rbar[r], 1);
+    for (int r = 0; r < 2 * EPI_WARPS; r++) mbar_init(&rbar[r], 1);
     for (int a = 0; a < 2; a++) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 2 * EPI_WARPS);
@@ -738,7 +758,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_pair(const __grid_cons
       }
     }
   } else {
-    epilogue_tma<T, BN, true>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, pair, npairs, 2 * BM, (int)rank * BM);
+    epilogue_tma<T, BN, true, 2>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, pair, npairs, 2 * BM, (int)rank * BM);
   }
   if (threadIdx.x == 0 && *abort) {  // after a timeout, let copies still in flight land before the pair exits
     const uint64_t t0 = gtimer();
@@ -840,15 +860,17 @@ void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtens
 
 namespace lc {
 
-// CTA pairs pay off when the main loop is long against the epilogue (K >= 1024
-// on the encoder's shapes); LAYA_CUDA_GEMM_PAIR=0 / =1 forces either kernel.
+// 256-wide tiles run on CTA pairs (half the weight bytes per CTA, two staging
+// buffers per epilogue warp); LAYA_CUDA_GEMM_PAIR=0 selects the single-CTA
+// kernel instead (both are tested).
 bool gemm_use_pair(int64_t K) {
-  static int force = -2;
-  if (force == -2) {
+  static int on = -1;
+  if (on < 0) {
     const char* v = getenv("LAYA_CUDA_GEMM_PAIR");
-    force = v ? (v[0] == '0' ? 0 : 1) : -1;
+    on = (v && v[0] == '0') ? 0 : 1;
   }
-  return force >= 0 ? force == 1 : K >= 1024;
+  (void)K;
+  return on == 1;
 }
 
 bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, const void* bias, int bias_dtype, void* y, int64_t ldy,
@@ -863,7 +885,9 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
   if (ep.kind == EPI_ROPE_QKV && (ep.rope_cols % 64)) return false;
   // folded-LayerNorm statistics cover whole 64-column units
   if (ep.stats_out && (ep.kind != EPI_RESIDUAL || N % 64)) return false;
-  if (ep.ln_stats && (Nacc % 64 || ((uintptr_t)ep.ln_wsum & 15) || ep.ln_parts < 1 || ep.ln_cols != K)) return false;
+  if (ep.ln_stats && (Nacc % 64 || ((uintptr_t)ep.ln_wsum & 15) || ep.ln_parts < 1 || ep.ln_parts > LN_MAX_PARTS ||
+                      (int64_t)ep.ln_parts * ep.ln_part_cols < K || ep.ln_cols != K))
+    return false;
   GemmArgs a{};
   a.M = (int)M;
   a.N = (int)N;
@@ -890,8 +914,8 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
     GemmArgs ap = a;
     const int64_t ptiles = ((M + 2 * BM - 1) / (2 * BM)) * a.ntile_n;
     ap.ntiles = (int)ptiles;
-    if (dtype == LC_F16) launch_gemm_pair<__half, 6>(ma, mbp, my, mr, ap, st);
-    else launch_gemm_pair<__nv_bfloat16, 6>(ma, mbp, my, mr, ap, st);
+    if (dtype == LC_F16) launch_gemm_pair<__half, 5>(ma, mbp, my, mr, ap, st);
+    else launch_gemm_pair<__nv_bfloat16, 5>(ma, mbp, my, mr, ap, st);
   } else if (tmae) {
     const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
     const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
