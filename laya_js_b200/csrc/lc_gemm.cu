@@ -137,11 +137,11 @@ __device__ __forceinline__ void ln_apply(const GemmEpilogue& ep, int col, float 
     b[q * 4 + 3] = r * fmaf(-mu, w.w, b[q * 4 + 3]);
   }
 }
-// Producer side: round the 64 outputs to the stored type (so the statistics
-// describe the tensor the next layer reads) and fold their mean / M2 into
-// the tile's running (n, mean, M2).
+// Producer side: round the 64 outputs of a unit to the stored type (so the
+// statistics describe the tensor the next layer reads) and return their
+// (mean, M2).
 template <typename T>
-__device__ __forceinline__ void stats_unit(float* a, float* b, float& n, float& mean, float& m2) {
+__device__ __forceinline__ float2 stats_unit(float* a, float* b) {
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < 32; j++) {
@@ -157,10 +157,7 @@ __device__ __forceinline__ void stats_unit(float* a, float* b, float& n, float& 
     q = fmaf(d0, d0, q);
     q = fmaf(d1, d1, q);
   }
-  const float nn = n + 64.f, d = mu - mean;
-  mean += d * (64.f / nn);
-  m2 += q + d * d * (n * 64.f / nn);
-  n = nn;
+  return make_float2(mu, q);
 }
 
 // store 32 consecutive values v[0..31] at columns [col, col+32) of row `row`, valid columns < ncols
@@ -213,9 +210,12 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 // buffer per warp holding a 32-row x 64-column block in the 128-byte-swizzled
 // layout the TMA store/load tensor maps use (16-byte chunk c of row r at
 // chunk position c ^ (r & 7)).
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 8;                    // single-CTA kernel
 constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t STG_BYTES = EPI_WARPS * 4096;
+constexpr int PAIR_EPI_WARPS = 8;               // CTA-pair kernel: two staging buffers per warp
+constexpr int PAIR_NBUF = 2;
+constexpr int PAIR_THREADS = 64 + 32 * PAIR_EPI_WARPS;
 
 template <int STAGES, int BN>
 constexpr size_t gemm_smem_bytes(bool tma_epi) {
@@ -227,33 +227,45 @@ constexpr size_t gemm_smem_bytes(bool tma_epi) {
 // (t / ntile_n) * tile_rows + row_off. In a CTA pair the accumulator-free
 // arrivals go to the barrier of CTA 0, whose thread issues the MMAs.
 //
-// Warps 2..9 -> TMEM lane quarter warp % 4. Each warp owns 32 rows and half
-// of the 64-column units of the tile. Per unit: tcgen05.ld the f32
-// accumulators, apply folded LayerNorm / RoPE / bias / residual / GeGLU
-// (packed f32 pairs), write the row's 8 chunks into a swizzled staging
-// buffer, and one lane issues a TMA store of the 32 x 64 block (rows >= M and
-// columns >= N are clipped by the tensor map). The residual block arrives by
-// TMA load into the buffer its result is stored from. With NBUF = 2 staging
-// buffers per warp, both of a tile's residual blocks are requested before
-// its accumulator is ready, and a store drains while the next unit computes.
-// The tile's LayerNorm statistics and the first unit's LayerNorm column sums
-// (one coalesced load per warp, shared by shuffles) are read ahead as well.
-template <typename T, int BN, bool PAIR, int NBUF>
+// EW epilogue warps (2 .. EW+1), EW/4 per TMEM lane quarter warp % 4. Each
+// warp owns 32 rows and a contiguous share of the tile's 64-column units (a
+// GeGLU output block, an even/odd unit pair, stays in one warp). Per unit:
+// tcgen05.ld the f32 accumulators, apply folded LayerNorm / RoPE / bias /
+// residual / GeGLU (packed f32 pairs), write the row's 8 chunks into a
+// swizzled staging buffer, and one lane issues a TMA store of the 32 x 64
+// block (rows >= M and columns >= N are clipped by the tensor map). The
+// residual block arrives by TMA load into the buffer its result is stored
+// from; when the warp has a buffer per unit (NBUF staging buffers) all its
+// residual blocks are requested before the tile's accumulator is ready, and
+// with two buffers a store drains while the next unit computes. The tile's
+// LayerNorm statistics and the first unit's LayerNorm column sums (one
+// coalesced load per warp, shared by shuffles) are read ahead as well.
+template <typename T, int BN, bool PAIR, int EW, int NBUF>
 __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtensorMap* tmYp, const CUtensorMap* tmRp, uint8_t* sE, uint64_t* rbar,
                                              uint64_t* tfull, uint64_t* tempty, volatile int* abort, uint32_t tmem, int warp, int lane,
                                              int t_begin, int t_step, int tile_rows, int row_off) {
   const CUtensorMap& tmY = *tmYp;
   const CUtensorMap& tmR = *tmRp;
-  const int quarter = warp & 3, half = (warp - 2) >> 2;
+  constexpr int NSUB = EW / 4;  // warps per lane quarter
+  const int quarter = warp & 3, sub = (warp - 2) >> 2;
   const GemmEpilogue& ep = args.ep;
   const bool geglu = ep.kind == EPI_GEGLU;
   const bool resid = ep.kind == EPI_RESIDUAL;
   const int ncols = geglu ? 2 * args.N : args.N;  // accumulator columns that hold data
   constexpr int U = BN / 64;
-  // this warp's units: halves of the tile (a GeGLU output block = an even/odd unit pair stays in one warp)
-  const int u_lo = (geglu && U == 2) ? (half ? U : 0) : half * (U / 2);
-  const int u_hi = (geglu && U == 2) ? U : (half + 1) * (U / 2);
-  static_assert(NBUF == 1 || U / 2 <= 2, "two staging buffers cover at most two units per warp and tile");
+  int u_lo, u_hi;
+  if (geglu) {
+    const int per = (U / 2) / NSUB > 0 ? (U / 2) / NSUB : 1, b0 = sub * per;
+    u_lo = min(U, 2 * b0);
+    u_hi = min(U, 2 * (b0 + per));
+  } else {
+    const int per = U / NSUB > 0 ? U / NSUB : 1;
+    u_lo = min(U, sub * per);
+    u_hi = min(U, u_lo + per);
+  }
+  // residual blocks requested ahead: one buffer per unit of this warp
+  const bool ahead = resid && u_hi - u_lo <= NBUF;
+  const int nparts = args.N / 64;  // row statistics: one (mean, M2) per 64-column unit
   uint8_t* stg0 = sE + (warp - 2) * NBUF * 4096;
   uint64_t* rb0 = rbar + (warp - 2) * NBUF;
   uint32_t rph[NBUF];
@@ -276,11 +288,11 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
     // the first unit's LayerNorm column sums (lane l: columns 2l, 2l+1)
     float2 wsp = make_float2(0.f, 0.f);
     if (ep.ln_stats) wsp = __ldg((const float2*)(ep.ln_wsum + n0 + u_lo * 64) + lane);
-    if (NBUF == 2 && resid) {  // both residual blocks, in flight while the accumulator is computed
-      if (lane == 0) bulk_wait_read0();  // earlier stores have read both buffers
+    if (ahead) {  // the residual blocks, in flight while the accumulator is computed
+      if (lane == 0) bulk_wait_read0();  // earlier stores have read the buffers
       __syncwarp();
       if (lane == 0)
-        for (int i = 0; i < 2 && u_lo + i < u_hi && n0 + (u_lo + i) * 64 < ncols; i++) {
+        for (int i = 0; i < NBUF && u_lo + i < u_hi && n0 + (u_lo + i) * 64 < ncols; i++) {
           mbar_arrive_expect_tx(&rb0[i], 4096);
           tma_load_2d(stg0 + i * 4096, &tmR, &rb0[i], n0 + (u_lo + i) * 64, row0);
         }
@@ -288,7 +300,6 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
     if (!mbar_wait(&tfull[acc], acc_phase, abort, &g_gemm_err)) break;
     tc_fence_after();
     const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-    float st_n = 0.f, st_mean = 0.f, st_m2 = 0.f;
 #pragma unroll 1
     for (int u = u_lo; u < u_hi; u++) {
       const int col = n0 + u * 64;
@@ -297,11 +308,11 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
       const int bcol = geglu ? n0 + (u & ~1) * 64 : col;  // first accumulator column of the block
       if (bcol >= ncols) break;  // the rest of this tile is past the weight rows
       const bool more = u + 1 < u_hi && (geglu ? n0 + ((u + 1) & ~1) * 64 : col + 64) < ncols;
-      // staging buffer: the one; with two, the residual's (chosen per unit at the
-      // tile start), else alternating with this warp's stores
-      const int bi = NBUF == 1 ? 0 : (resid ? u - u_lo : (nstore & 1));
+      // staging buffer: the unit's residual buffer (loaded ahead), the one, or
+      // alternating with this warp's stores
+      const int bi = ahead ? u - u_lo : (NBUF == 1 ? 0 : (int)(nstore & 1));
       uint8_t* stg = stg0 + bi * 4096;
-      if (NBUF == 1 && first && resid) {  // the residual block lands in the staging buffer
+      if (!ahead && first && resid) {  // the residual block lands in the staging buffer
         if (lane == 0) bulk_wait_read0();  // this warp's previous store has read the buffer
         __syncwarp();
         if (lane == 0) {
@@ -367,7 +378,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
             for (int j = 0; j < 4; j++)
               dst[j] = add2(dst[j], make_float2(TcFmt<T>::back(h[2 * j]), TcFmt<T>::back(h[2 * j + 1])));
           }
-          if (ep.stats_out) stats_unit<T>((float*)a, (float*)b, st_n, st_mean, st_m2);
+          if (ep.stats_out && live) ep.stats_out[(int64_t)row * nparts + col / 64] = stats_unit<T>((float*)a, (float*)b);
         }
       }
       if (first && !resid) {  // the store that last used this buffer has read it
@@ -401,8 +412,6 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
         if (geglu && (u & 1) == 0) break;  // the pair's second unit is past the weight rows
       }
     }
-    if (ep.stats_out && live)
-      ep.stats_out[((int64_t)row * args.ntile_n + t % args.ntile_n) * 2 + half] = make_float2(st_mean, st_m2);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
@@ -531,7 +540,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       }
     }
   } else if constexpr (TMAE) {
-    epilogue_tma<T, BN, false, 1>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x, gridDim.x, BM, 0);
+    epilogue_tma<T, BN, false, EPI_WARPS, 1>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x, gridDim.x, BM, 0);
   } else {
     // ---------------- epilogue (warps 2..9 -> TMEM lane quarter warp % 4, half of the units each)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
@@ -550,7 +559,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
       float ln_mu, ln_r;
       if (args.ep.ln_stats) ln_row(args.ep, row, args.M, ln_mu, ln_r);
-      float st_n = 0.f, st_mean = 0.f, st_m2 = 0.f;
 #pragma unroll 1
       for (int u = half * (U / 2); u < (half + 1) * (U / 2); u++) {
         uint32_t ra[32], rb[32];
@@ -597,13 +605,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
           load32f<T>(rp, col + 32, args.N, r, vec);
 #pragma unroll
           for (int j = 0; j < 32; j++) b[j] += r[j];
-          if (ep.stats_out) stats_unit<T>(a, b, st_n, st_mean, st_m2);
+          if (ep.stats_out) ep.stats_out[(int64_t)row * (args.N / 64) + col / 64] = stats_unit<T>(a, b);
         }
         store32<T>(rowp, col, args.N, a, vec);
         store32<T>(rowp, col + 32, args.N, b, vec);
       }
-      if (args.ep.stats_out && live)
-        args.ep.stats_out[((int64_t)row * args.ntile_n + t % args.ntile_n) * 2 + half] = make_float2(st_mean, st_m2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -633,11 +639,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
 // single-CTA one on each CTA's rows. No load is multicast.
 template <int STAGES>
 constexpr size_t gemm_pair_smem_bytes() {
-  return (size_t)STAGES * (BM * BK * 2 + 128 * BK * 2) + 2 * STG_BYTES + 1024 + 512;
+  return (size_t)STAGES * (BM * BK * 2 + 128 * BK * 2) + PAIR_EPI_WARPS * PAIR_NBUF * 4096 + 1024 + 512;
 }
 
 template <typename T, int STAGES>
-__global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+__global__ void __launch_bounds__(PAIR_THREADS, 1) k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                                            const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                                                            const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -648,13 +654,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_pair(const __grid_cons
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sE = sB + STAGES * B_BYTES;            // two staging buffers per epilogue warp
-  uint64_t* full = (uint64_t*)(sE + 2 * STG_BYTES);  // used in CTA 0
+  uint8_t* sE = sB + STAGES * B_BYTES;                                  // PAIR_NBUF staging buffers per epilogue warp
+  uint64_t* full = (uint64_t*)(sE + PAIR_EPI_WARPS * PAIR_NBUF * 4096);  // used in CTA 0
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;  // used in CTA 0: both CTAs' epilogue warps arrive
-  uint64_t* rbar = tempty + 2;   // two per epilogue warp
-  uint32_t* tmem_slot = (uint32_t*)(rbar + 2 * EPI_WARPS);
+  uint64_t* rbar = tempty + 2;   // one per staging buffer
+  uint32_t* tmem_slot = (uint32_t*)(rbar + PAIR_EPI_WARPS * PAIR_NBUF);
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -667,10 +673,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_pair(const __grid_cons
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int r = 0; r < 2 * EPI_WARPS; r++) mbar_init(&rbar[r], 1);
+    for (int r = 0; r < PAIR_EPI_WARPS * PAIR_NBUF; r++) mbar_init(&rbar[r], 1);
     for (int a = 0; a < 2; a++) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 2 * EPI_WARPS);
+      mbar_init(&tempty[a], 2 * PAIR_EPI_WARPS);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -758,7 +764,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_pair(const __grid_cons
       }
     }
   } else {
-    epilogue_tma<T, BN, true, 2>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, pair, npairs, 2 * BM, (int)rank * BM);
+    epilogue_tma<T, BN, true, PAIR_EPI_WARPS, PAIR_NBUF>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, pair, npairs, 2 * BM,
+                                                 (int)rank * BM);
   }
   if (threadIdx.x == 0 && *abort) {  // after a timeout, let copies still in flight land before the pair exits
     const uint64_t t0 = gtimer();
@@ -838,7 +845,7 @@ void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtens
   at[0].val.clusterDim.x = 2;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.blockDim = dim3(PAIR_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = at;
@@ -945,7 +952,10 @@ int gemm_tile_n(int64_t Nacc, bool geglu) {
   return BN;
 }
 
-int gemm_stats_part_cols(int64_t N) { return gemm_tile_n(N, false) / 2; }
+int gemm_stats_part_cols(int64_t N) {
+  (void)N;
+  return 64;
+}
 
 bool gemm_linear(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y, const GemmEpilogue& ep) {
   int64_t M = x2->shape[0], K = x2->shape[1], N = w->shape[0];
