@@ -15,7 +15,8 @@ Keys beyond the driver's contract:
   e2e        the same metric through lc_encoder_forward_host (host ids in,
              host probabilities out, copies inside the timed region);
   roofline   the tcgen05 GEMMs (dominant kernel class) vs the measured
-             sustained bf16 tensor peak;
+             sustained bf16 tensor peak, with their DRAM traffic per launch
+             from the committed ncu capture;
   cpu_baseline  the numpy oracle (float64) on a bounded sample, all cores;
   int4       configs[3]-style 4-bit affine g64 weights (batch 512, lengths
              U[64, 1024]) tokens/s on the same GPU;
@@ -43,6 +44,9 @@ sys.path.insert(0, str(ROOT))
 
 BATCH, LO, HI, CLASSES = 256, 32, 512, 8
 SEED = 20261201
+# DRAM bytes per GEMM launch of this workload (average over the four projections),
+# from the committed one-pass ncu capture in profiles/gemm_traffic_bench.md
+GEMM_TRAFFIC_BYTES = 307.1e6
 
 
 def parse():
@@ -283,8 +287,11 @@ def main() -> None:
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * 4 + (BATCH + 1) * 4,
                 "d2h_bytes_per_step": BATCH * CLASSES * 4},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
-                     "frac": (achieved / peaks["bf16"]) if achieved else None, "traffic": None,
-                     "kernel": "k_gemm_tc (tcgen05 GEMMs: Wqkv+RoPE, Wo+residual, Wi+GeGLU, mlp.Wo+residual)",
+                     "frac": (achieved / peaks["bf16"]) if achieved else None, "traffic": GEMM_TRAFFIC_BYTES,
+                     "traffic_src": "profiles/gemm_traffic_bench.md: ncu dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch, "
+                                    "one-pass capture of this workload",
+                     "flop_per_launch": gemm_flops / max(g["launches"], 1),
+                     "kernel": "k_gemm_pair (tcgen05 CTA-pair GEMMs: Wqkv+RoPE+folded LN, Wo+residual, Wi+GeGLU+folded LN, mlp.Wo+residual)",
                      "peak_src": f"{peaks['src']} sustained bf16 (MEASURED_PEAKS.json)",
                      "gemm_ms_per_step": g["ms"] / args.steps, "gemm_launches_per_step": g["launches"] / args.steps,
                      "timing": "CUDA events around every GEMM launch on the library stream, second timed region of K steps"},
