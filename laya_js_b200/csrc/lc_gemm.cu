@@ -107,12 +107,22 @@ __device__ __forceinline__ void ln_row(const GemmEpilogue& ep, int row, int M, f
   const float inv_n = 1.f / (float)ep.ln_cols;
   const float k0 = st[0].x;
   float s1 = 0.f, s2 = 0.f;
-#pragma unroll 8
-  for (int p = 0; p < ep.ln_parts; p++) {
-    const float2 v = st[p];
+  auto part = [&](int p, float2 v) {
     const float c = (float)min(ep.ln_part_cols, ep.ln_cols - p * ep.ln_part_cols), d = v.x - k0;
     s1 = fmaf(c, d, s1);
     s2 += fmaf(c * d, d, v.y);
+  };
+  if ((ep.ln_parts & 1) == 0) {  // two parts per 16-byte load (rows start 16-byte aligned)
+    const float4* st4 = (const float4*)st;
+#pragma unroll 8
+    for (int p = 0; p < ep.ln_parts / 2; p++) {
+      const float4 v = st4[p];
+      part(2 * p, make_float2(v.x, v.y));
+      part(2 * p + 1, make_float2(v.z, v.w));
+    }
+  } else {
+#pragma unroll 8
+    for (int p = 0; p < ep.ln_parts; p++) part(p, st[p]);
   }
   mu = fmaf(s1, inv_n, k0);
   r = rsqrtf(fmaxf(fmaf(-s1 * s1, inv_n, s2), 0.f) * inv_n + ep.ln_eps);
@@ -275,6 +285,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
   uint32_t acc_phase = 0;
   bool ok = true;
   uint32_t nstore = 0;  // TMA stores issued by this warp
+  const uint32_t tempty0 = PAIR ? mapa_rank(smem_u32(tempty), 0) : 0;  // CTA 0's accumulator-empty barriers
   for (int t = t_begin; t < args.ntiles && ok; t += t_step) {
     const int m0 = (t / args.ntile_n) * tile_rows + row_off, n0 = (t % args.ntile_n) * BN;
     const int row0 = m0 + quarter * 32;
@@ -415,7 +426,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
-      if constexpr (PAIR) mbar_arrive_cluster(mapa_rank(smem_u32(&tempty[acc]), 0));  // the pair's MMA runs in CTA 0
+      if (PAIR && row_off != 0) mbar_arrive_cluster(tempty0 + 8 * acc);  // the pair's MMA runs in CTA 0
       else mbar_arrive(&tempty[acc]);
     }
     if (++acc == 2) { acc = 0; acc_phase ^= 1; }
