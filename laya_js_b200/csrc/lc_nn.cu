@@ -364,6 +364,54 @@ __global__ void k_geglu_generic(const char* x, int xdt, char* y, int ydt, int64_
   }
 }
 
+// Dense f16 / bf16 / f32 x with D % (16 / sizeof(T)) == 0: block (b, 32*VEC-column
+// chunk); its 8 warps split the L positions, each lane sums VEC columns from
+// 16-byte loads (the masked-out rows are skipped), then the warps' partial
+// sums and counts combine in shared memory.
+template <typename T>
+__global__ void __launch_bounds__(256) k_mean_pool_vec(const T* __restrict__ x, const char* mask, int mdt, float* __restrict__ out,
+                                                       int64_t L, int64_t D) {
+  constexpr int VEC = 16 / sizeof(T);
+  __shared__ float part[8][32 * VEC];
+  __shared__ float cnt[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t b = blockIdx.y;
+  const int64_t c0 = (int64_t)blockIdx.x * 32 * VEC + lane * VEC;
+  const bool on = c0 < D;
+  float acc[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; j++) acc[j] = 0.f;
+  float n = 0.f;
+  for (int64_t l = warp; l < L; l += 8) {
+    if (ld_as<int64_t>(mask, mdt, b * L + l) == 0) continue;  // warp-uniform
+    n += 1.f;
+    if (on) {
+      const uint4 raw = *(const uint4*)(x + (b * L + l) * D + c0);
+      const T* e = (const T*)&raw;
+#pragma unroll
+      for (int j = 0; j < VEC; j++) acc[j] += ld_as<float>((const char*)e, std::is_same<T, float>::value ? LC_F32 : (std::is_same<T, __half>::value ? LC_F16 : LC_BF16), j);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VEC; j++) part[warp][lane * VEC + j] = acc[j];
+  if (lane == 0) cnt[warp] = n;
+  __syncthreads();
+  if (warp == 0) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) tot += cnt[w];
+    const float inv = 1.f / fmaxf(tot, 1.f);
+    if (on)
+#pragma unroll
+      for (int j = 0; j < VEC; j++) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) s += part[w][lane * VEC + j];
+        out[b * D + c0 + j] = s * inv;
+      }
+  }
+}
+
 __global__ void k_mean_pool(const char* x, int xdt, const char* mask, int mdt, float* out, int64_t B, int64_t L, int64_t D) {
   LC_GRID_STRIDE(t, B * D) {
     int64_t b = t / D, d = t % D;
@@ -688,7 +736,17 @@ int lc_mean_pool(lc_tensor* out, lc_tensor xh, lc_tensor mh) {
   if (B * D) {
     LcTensor* x = contiguous(x0);
     LcTensor* m = contiguous(m0);
-    k_mean_pool<<<blocks_for(B * D, 256), 256, 0, stream()>>>(x->data(), x->dtype, m->data(), m->dtype, (float*)y->data(), B, L, D);
+    const int d = x->dtype;
+    const int vec = d == LC_F32 ? 4 : 8;
+    if ((d == LC_F16 || d == LC_BF16 || d == LC_F32) && D % vec == 0 && B <= 65535) {
+      dim3 grid((unsigned)((D + 32 * vec - 1) / (32 * vec)), (unsigned)B);
+      if (d == LC_F16) k_mean_pool_vec<__half><<<grid, 256, 0, stream()>>>((const __half*)x->data(), m->data(), m->dtype, (float*)y->data(), L, D);
+      else if (d == LC_BF16)
+        k_mean_pool_vec<__nv_bfloat16><<<grid, 256, 0, stream()>>>((const __nv_bfloat16*)x->data(), m->data(), m->dtype, (float*)y->data(), L, D);
+      else k_mean_pool_vec<float><<<grid, 256, 0, stream()>>>((const float*)x->data(), m->data(), m->dtype, (float*)y->data(), L, D);
+    } else {
+      k_mean_pool<<<blocks_for(B * D, 256), 256, 0, stream()>>>(x->data(), x->dtype, m->data(), m->dtype, (float*)y->data(), B, L, D);
+    }
     LC_LAUNCHED(1);
     if (x != x0) release(x);
     if (m != m0) release(m);

@@ -115,6 +115,117 @@ __global__ void k_softmax_cols(const char* x, int dtype, char* out, int out_dtyp
   }
 }
 
+// ---- dense 16-bit / f32 rows, one warp per row held in registers
+// (16-byte loads, each element read once): the fast paths of softmax and of
+// sum / mean / max / min over the last axis. n % (16 / sizeof(T)) == 0 and
+// n <= 32 * (16 / sizeof(T)) * MAXV.
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int n) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int nv = n / VEC;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    float v[MAXV][VEC];
+    float m = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      const int c = t * 32 + lane;
+      if (c < nv) {
+        const uint4 raw = *(const uint4*)(x + r * n + (int64_t)c * VEC);
+        const T* e = (const T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VEC; j++) {
+          v[t][j] = to_f<T>(e[j]);
+          m = fmaxf(m, v[t][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++)
+      if (t * 32 + lane < nv)
+#pragma unroll
+        for (int j = 0; j < VEC; j++) {
+          v[t][j] = expf(v[t][j] - m);
+          s += v[t][j];
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float inv = 1.f / s;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      const int c = t * 32 + lane;
+      if (c < nv) {
+        uint4 raw;
+        T* e = (T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VEC; j++) e[j] = from_f<T>(v[t][j] * inv);
+        *(uint4*)(y + r * n + (int64_t)c * VEC) = raw;
+      }
+    }
+  }
+}
+
+// max / min with NaN propagation (the generic path's rule)
+__device__ __forceinline__ float pick(int op, float a, float b) {
+  if (isnan(a) || isnan(b)) return isnan(a) ? a : b;
+  return op == R_MAX ? fmaxf(a, b) : fminf(a, b);
+}
+
+// sum (f32 accumulation), mean (f64), max, min over each row
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) k_reduce_rows_vec(const T* __restrict__ x, char* out, int out_dtype, int op, int64_t rows, int n) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int nv = n / VEC;
+  const bool mm = op == R_MAX || op == R_MIN;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    float acc = 0.f, best = op == R_MAX ? -INFINITY : INFINITY;
+    double dacc = 0.0;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      const int c = t * 32 + lane;
+      if (c < nv) {
+        const uint4 raw = *(const uint4*)(x + r * n + (int64_t)c * VEC);
+        const T* e = (const T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VEC; j++) {
+          const float f = to_f<T>(e[j]);
+          if (mm) best = pick(op, best, f);
+          else if (op == R_MEAN) dacc += (double)f;
+          else acc += f;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      if (mm) best = pick(op, best, __shfl_xor_sync(0xffffffffu, best, o));
+      else if (op == R_MEAN) dacc += __shfl_xor_sync(0xffffffffu, dacc, o);
+      else acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    }
+    if (lane == 0) {
+      if (mm) st_as<float>(out, out_dtype, r, best);
+      else if (op == R_MEAN) st_as<double>(out, out_dtype, r, dacc / (double)n);
+      else st_as<float>(out, out_dtype, r, acc);
+    }
+  }
+}
+
 // inclusive prefix sum, one thread per column, wrapping in the output dtype
 template <typename CT>
 __global__ void k_cumsum(const char* x, int dtype, char* out, int out_dtype, int64_t outer, int64_t n, int64_t inner) {
@@ -200,6 +311,27 @@ std::vector<int64_t> reduced_shape(const LcTensor* x, int a, bool keep) {
   return sh;
 }
 
+// Fast-path dispatch: dense f16 / bf16 / f32 rows of at most 32 * VEC * 8
+// elements, n a multiple of the vector width. Returns false when it does not apply.
+bool row_vec_ok(int dtype, int64_t n, int64_t rows) {
+  if (!(dtype == LC_F16 || dtype == LC_BF16 || dtype == LC_F32) || rows <= 0) return false;
+  const int vec = dtype == LC_F32 ? 4 : 8;
+  return n > 0 && n % vec == 0 && n <= 32 * vec * 8 && n < INT32_MAX;
+}
+int row_vec_maxv(int dtype, int64_t n) {
+  const int vec = dtype == LC_F32 ? 4 : 8;
+  const int per = (int)((n / vec + 31) / 32);
+  return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8;
+}
+
+#define LC_ROWVEC_DISPATCH(KERNEL, T, MAXV_RT, BLOCKS, ...)                     \
+  switch (MAXV_RT) {                                                           \
+    case 1: KERNEL<T, 1><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    case 2: KERNEL<T, 2><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    case 4: KERNEL<T, 4><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    default: KERNEL<T, 8><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;   \
+  }
+
 template <typename CT, typename AT>
 void launch_reduce(LcTensor* c, LcTensor* y, int op, Axis3 s) {
   cudaStream_t st = stream();
@@ -230,6 +362,17 @@ LcTensor* reduce(int op, uint64_t xh, int axis, bool keep, const char* name) {
   if (y->numel() == 0) return y;
   LcTensor* c = contiguous(x);
   int d = x->dtype;
+  if (s.inner == 1 && op != R_ARGMAX && op != R_ARGMIN && row_vec_ok(d, s.n, s.outer)) {
+    const unsigned blocks = blocks_for(s.outer * 32, 256);
+    const int mv = row_vec_maxv(d, s.n);
+    const int n = (int)s.n;
+    if (d == LC_F16) { LC_ROWVEC_DISPATCH(k_reduce_rows_vec, __half, mv, blocks, (const __half*)c->data(), y->data(), y->dtype, op, s.outer, n) }
+    else if (d == LC_BF16) { LC_ROWVEC_DISPATCH(k_reduce_rows_vec, __nv_bfloat16, mv, blocks, (const __nv_bfloat16*)c->data(), y->data(), y->dtype, op, s.outer, n) }
+    else { LC_ROWVEC_DISPATCH(k_reduce_rows_vec, float, mv, blocks, (const float*)c->data(), y->data(), y->dtype, op, s.outer, n) }
+    LC_LAUNCHED(1);
+    if (c != x) release(c);
+    return y;
+  }
   if (op == R_MEAN) {
     if (d == LC_U64) launch_reduce<uint64_t, double>(c, y, op, s);
     else if (is_float(d)) launch_reduce<double, double>(c, y, op, s);
@@ -269,7 +412,14 @@ int lc_softmax(lc_tensor* out, lc_tensor xh, int axis) {
     LcTensor* c = contiguous(x);
     cudaStream_t st = stream();
     bool dbl = x->dtype == LC_F64;
-    if (s.inner == 1) {
+    if (s.inner == 1 && odt == x->dtype && row_vec_ok(x->dtype, s.n, s.outer)) {
+      const unsigned blocks = blocks_for(s.outer * 32, 256);
+      const int mv = row_vec_maxv(x->dtype, s.n);
+      const int n = (int)s.n;
+      if (x->dtype == LC_F16) { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, __half, mv, blocks, (const __half*)c->data(), (__half*)y->data(), s.outer, n) }
+      else if (x->dtype == LC_BF16) { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, __nv_bfloat16, mv, blocks, (const __nv_bfloat16*)c->data(), (__nv_bfloat16*)y->data(), s.outer, n) }
+      else { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, float, mv, blocks, (const float*)c->data(), (float*)y->data(), s.outer, n) }
+    } else if (s.inner == 1) {
       unsigned blocks = blocks_for(s.outer * 32, 256);
       if (dbl) k_softmax_rows<double><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), odt, s.outer, s.n);
       else k_softmax_rows<float><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), odt, s.outer, s.n);

@@ -4,6 +4,7 @@ quick timing. Each case fits in a few GB and ends in seconds.
     python -m laya_js_b200.profile_cases encoder   # 2-layer ModernBERT-base, 64 prompts L~U[32,512]
     python -m laya_js_b200.profile_cases gemm      # one 32768x2304x768 linear (f16)
     python -m laya_js_b200.profile_cases attention # varlen attention, 256 prompts, global + sliding
+    python -m laya_js_b200.profile_cases hbm       # the HBM-bound contract ops on ~100-400 MB tensors
 
 Every case prints one line with its shape and the device time per launch
 (CUDA events on the library stream, after warm-up).
@@ -76,9 +77,62 @@ def case_attention(b) -> str:
     return f"attention T={T}, 12 heads: " + ", ".join(out)
 
 
+def case_hbm(b) -> str:
+    """The HBM-bound contract ops on tensors larger than L2, each launch timed
+    with its algorithmic bytes (read + write once) -> GB/s."""
+    rng = np.random.default_rng(0)
+    R, H = 65536, 768
+    x = b.fromHost(HostTensor("f16", (R, H), rng.standard_normal((R, H), dtype=np.float32).astype(np.float16)))
+    y = b.fromHost(HostTensor("f16", (R, H), rng.standard_normal((R, H), dtype=np.float32).astype(np.float16)))
+    g = b.fromHost(HostTensor("f16", (H,), np.ones(H, np.float16)))
+    z = b.fromHost(HostTensor("f16", (R, 2 * H), rng.standard_normal((R, 2 * H), dtype=np.float32).astype(np.float16)))
+    V = 50368
+    table = b.fromHost(HostTensor("f16", (V, H), (rng.standard_normal((V, H), dtype=np.float32) * 0.02).astype(np.float16)))
+    ids = b.fromHost(HostTensor("i32", (R,), rng.integers(0, V, R, dtype=np.int32)))
+    B, L = 128, 512
+    mask = b.fromHost(HostTensor("i32", (B, L), np.ones((B, L), np.int32)))
+    xb = b.reshape(x, [B, L, H])
+    e = 2
+    cases = [
+        ("add [65536,768] f16", lambda: b.add(x, y), 3 * R * H * e),
+        ("gelu [65536,768] f16", lambda: b.gelu(x), 2 * R * H * e),
+        ("layerNorm [65536,768] f16", lambda: b.layerNorm(x, g, None, 1e-5), 2 * R * H * e),
+        ("softmax rows [65536,768] f16", lambda: b.softmax(x, -1), 2 * R * H * e),
+        ("geglu [65536,1536]->[65536,768] f16", lambda: b.geglu(z), (2 * R * H + R * H) * e),
+        ("sum rows [65536,768] f16", lambda: b.sum(x, -1), R * H * e),
+        ("embedding 65536 ids of [50368,768] f16", lambda: b.embedding(table, ids), 2 * R * H * e),
+        ("meanPool [128,512,768] f16", lambda: b.meanPool(xb, mask), R * H * e),
+    ]
+    out = []
+    for name, fn, nbytes in cases:
+        run = lambda: b.dispose(fn())
+        run()
+        ms = _event_time(b, run, 10)
+        out.append(f"{name}: {ms * 1e3:.1f} us, {nbytes / ms / 1e6:.0f} GB/s")
+    return "hbm kernels (algorithmic bytes / CUDA-event time):\n  " + "\n  ".join(out)
+
+
+def _event_time(b, fn, reps: int) -> float:
+    """Device ms per call: CUDA events on the library stream around `reps` calls."""
+    import torch
+    s = C.c_uint64()
+    _lib.call("lc_get_stream", C.byref(s))
+    stream = torch.cuda.ExternalStream(s.value)
+    b.flush()
+    with torch.cuda.stream(stream):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    b.flush()
+    return e0.elapsed_time(e1) / reps
+
+
 def main(argv) -> None:
     b = createCudaBackend(0)
-    cases = {"encoder": case_encoder, "gemm": case_gemm, "attention": case_attention}
+    cases = {"encoder": case_encoder, "gemm": case_gemm, "attention": case_attention, "hbm": case_hbm}
     for name in argv[1:] or list(cases):
         print(cases[name](b), flush=True)
 
