@@ -1,0 +1,73 @@
+"""The row fast paths (softmax, sum / mean / max / min over the last axis,
+meanPool) against float64 numpy, across the widths that select them (a
+multiple of the 16-byte vector, at most 32 lanes x 8 vectors) and the widths
+that fall back to the generic kernels, in f32 / f16 / bf16; NaN propagation
+of max / min; meanPool with masked-out and fully masked rows."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from gpu_util import backend
+from laya_js_b200.host import HostTensor, f32_to_bf16_bits, to_f32
+
+pytestmark = pytest.mark.gpu
+
+WIDTHS = {"f32": [4, 256, 1024, 1028, 770], "f16": [8, 768, 2048, 2056, 770], "bf16": [8, 512, 2048, 2056, 770]}
+EPS = {"f32": 1e-5, "f16": 2e-3, "bf16": 1.6e-2}
+
+
+def _host(dt, a):
+    if dt == "f32":
+        return HostTensor("f32", a.shape, a.astype(np.float32))
+    if dt == "f16":
+        return HostTensor("f16", a.shape, a.astype(np.float16))
+    return HostTensor("bf16", a.shape, f32_to_bf16_bits(a.astype(np.float32)))
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_softmax_and_reductions_over_rows(dt):
+    b = backend()
+    rng = np.random.default_rng(7)
+    for n in WIDTHS[dt]:
+        a = (rng.standard_normal((37, n)) * 3).astype(np.float32)
+        h = _host(dt, a)
+        x = to_f32(h).astype(np.float64)  # the values the device sees
+        t = b.fromHost(h)
+        sm = to_f32(b.read(b.softmax(t, -1))).astype(np.float64)
+        e = np.exp(x - x.max(-1, keepdims=True))
+        ref = e / e.sum(-1, keepdims=True)
+        assert np.abs(sm - ref).max() <= EPS[dt], f"softmax n={n}"
+        for name, fn, want, tol in [("sum", b.sum, x.sum(-1), EPS[dt] * np.sqrt(n) * 8 + EPS[dt] * np.abs(x).sum(-1)),
+                                    ("mean", b.mean, x.mean(-1), 1e-6 + 1e-6 * np.abs(x).mean(-1)),
+                                    ("max", b.max, x.max(-1), 0.0), ("min", b.min, x.min(-1), 0.0)]:
+            got = to_f32(b.read(fn(t, -1))).astype(np.float64)
+            assert np.all(np.abs(got - want) <= tol + (EPS[dt] * np.abs(want) if name == "sum" else 0)), f"{name} n={n}"
+        b.dispose(t)
+
+
+def test_max_min_propagate_nan():
+    b = backend()
+    a = np.arange(2 * 768, dtype=np.float32).reshape(2, 768)
+    a[1, 500] = np.nan
+    t = b.fromHost(HostTensor("f16", a.shape, a.astype(np.float16)))
+    mx, mn = to_f32(b.read(b.max(t, -1))), to_f32(b.read(b.min(t, -1)))
+    assert not np.isnan(mx[0]) and np.isnan(mx[1]) and np.isnan(mn[1])
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_mean_pool_masks(dt):
+    b = backend()
+    rng = np.random.default_rng(3)
+    B, L, D = 5, 77, 768
+    a = rng.standard_normal((B, L, D)).astype(np.float32)
+    h = _host(dt, a)
+    x = to_f32(h).astype(np.float64)
+    mask = (rng.random((B, L)) < 0.6).astype(np.int32)
+    mask[2] = 0  # a fully masked row pools to zeros
+    got = to_f32(b.read(b.meanPool(b.fromHost(h), b.fromHost(HostTensor("i32", mask.shape, mask))))).astype(np.float64)
+    cnt = np.maximum(mask.sum(1, keepdims=True), 1)
+    ref = (x * mask[:, :, None]).sum(1) / cnt
+    assert got.shape == (B, D)
+    assert np.abs(got - ref).max() < 1e-5
+    assert np.all(got[2] == 0)
