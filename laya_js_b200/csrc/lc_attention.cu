@@ -278,8 +278,6 @@ void attention_varlen(const void* qkv, void* out, const int4* tiles_dev, int nti
   LC_LAUNCHED(1);
 }
 
-bool attention_try_fast(const LcTensor*, const LcTensor*, const LcTensor*, const LcTensor*, float, LcTensor*) { return false; }
-
 }  // namespace lc
 
 using namespace lc;
