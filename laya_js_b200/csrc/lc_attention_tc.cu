@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; i++) {
@@ -174,15 +175,18 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmQ) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmKV) : "memory");
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the projection that wrote q, k, v has completed
 
   if (warp == 0) {
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmQ) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmKV) : "memory");
       int issued[NST], q_issued[2] = {0, 0};
       uint32_t iph[NST], q_ph[2] = {0, 0};
       for (int s = 0; s < NST; s++) issued[s] = 0, iph[s] = 0;
@@ -451,7 +455,7 @@ void launch_attn(const CUtensorMap& mq, const CUtensorMap& mkv, const AttnTcArgs
     attr = true;
   }
   const int grid = std::min(a.nwork, 2 * lc::num_sms());  // persistent: two CTAs per SM
-  k_attn_tc<T, LOCAL><<<(unsigned)grid, 192, ATTN_SMEM, st>>>(mq, mkv, a);
+  lc::launch_chain(k_attn_tc<T, LOCAL>, dim3((unsigned)grid), dim3(192), ATTN_SMEM, st, mq, mkv, a);
 }
 
 }  // namespace

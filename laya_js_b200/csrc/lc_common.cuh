@@ -118,7 +118,51 @@ inline unsigned blocks_for(int64_t n, int threads) {
   return (unsigned)(b < 1 ? 1 : (b > cap ? cap : b));
 }
 
+// Programmatic dependent launch for a chain of kernels on one stream (the
+// fused encoder's forward): while a PdlScope lives on the calling thread,
+// launch_chain() lets each kernel launch before its predecessor has finished.
+// Only kernels that call pdl_wait() in every CTA before touching memory an
+// earlier kernel wrote (and before exiting) may be launched this way.
+bool& pdl_flag();
+struct PdlScope {
+  bool prev;
+  PdlScope() : prev(pdl_flag()) { pdl_flag() = true; }
+  ~PdlScope() { pdl_flag() = prev; }
+  PdlScope(const PdlScope&) = delete;
+  PdlScope& operator=(const PdlScope&) = delete;
+};
+// Launch attributes for a kernel of the chain: the caller's (e.g. a cluster
+// size) plus programmatic stream serialisation when a PdlScope is active.
+inline void chain_attrs(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* at, int n_given) {
+  int n = n_given;
+  if (pdl_flag()) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
+  cfg.attrs = n ? at : nullptr;
+  cfg.numAttrs = (unsigned)n;
+}
+template <typename... KArgs, typename... Args>
+void launch_chain(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  chain_attrs(cfg, at, 0);
+  CUDA_OK(cudaLaunchKernelEx(&cfg, kernel, args...));
+}
+
 }  // namespace lc
+
+// The device side of programmatic dependent launch. pdl_trigger(): this CTA
+// no longer holds back the launch of the next kernel of the chain.
+// pdl_wait(): returns once the kernels this one depends on have completed
+// and their memory is visible (at once when launched without the attribute).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ------------------------------------------------------------- device helpers
 

@@ -57,6 +57,10 @@ cudaStream_t stream() { return S().cur; }
 int device() { return S().device; }
 int num_sms() { return S().sms; }
 void count_launch(int n) { S().launches += n; }
+bool& pdl_flag() {
+  static thread_local bool on = false;
+  return on;
+}
 
 void* dmalloc(size_t bytes) {
   ensure_init();

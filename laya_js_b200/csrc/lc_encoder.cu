@@ -42,6 +42,8 @@ void dequant_scaled_into(const LcTensor* w, const LcTensor* s, const LcTensor* b
 namespace {
 
 __global__ void k_positions(const int32_t* __restrict__ cu, int nseq, int32_t* __restrict__ pos) {
+  pdl_trigger();
+  pdl_wait();
   for (int s = blockIdx.x; s < nseq; s += gridDim.x) {
     int a = cu[s], b = cu[s + 1];
     for (int t = a + threadIdx.x; t < b; t += blockDim.x) pos[t] = t - a;
@@ -52,6 +54,8 @@ __global__ void k_positions(const int32_t* __restrict__ cu, int nseq, int32_t* _
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) k_embed_ln(const T* __restrict__ table, int64_t V, const int32_t* __restrict__ ids,
                                                   const float* __restrict__ w, T* __restrict__ y, int64_t rows, int H, float eps) {
+  pdl_trigger();
+  pdl_wait();
   int lane = threadIdx.x & 31;
   int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -110,6 +114,8 @@ template <typename T>
 __global__ void k_cls_head(const T* __restrict__ hidden, int H, const int32_t* __restrict__ cu, int nseq, const char* w, int wdt,
                            const char* b, int bdt, int C, float* __restrict__ probs) {
   extern __shared__ float logits[];
+  pdl_trigger();
+  pdl_wait();
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int s = blockIdx.x; s < nseq; s += gridDim.x) {
     const T* row = hidden + (int64_t)cu[s] * H;
@@ -479,7 +485,10 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
   int32_t* pos = (int32_t*)(ws + (size_t)5 * T * H * esz);
   float2* stats = (float2*)(ws + stats_offset(c, T));
   const int parts = stats_parts(c), part_cols = gemm_stats_part_cols(H);
-  k_positions<<<std::min(nseq, 4096), 256, 0, st>>>(cu_dev, nseq, pos);
+  // every kernel below waits for its predecessor on the device (pdl_wait)
+  // and may be launched while that one still runs
+  PdlScope pdl;
+  launch_chain(k_positions, dim3(std::min(nseq, 4096)), dim3(256), 0, st, cu_dev, nseq, pos);
   LC_LAUNCHED(1);
 
   int cap_g = 0, cap_l = 0;
@@ -490,9 +499,9 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
   Prof* pe = new Prof(e, 2);
   unsigned lnb = blocks_for(T * 32, 256);
   const int per = (H / 8 + 31) / 32;
-#define LC_EMB(TT, MV)                                                                                                            \
-  k_embed_ln<TT, MV><<<lnb, 256, 0, st>>>((const TT*)e->tok->data(), e->tok->shape[0], ids_dev, (const float*)e->emb_norm->data(), \
-                                          (TT*)x, T, H, (float)c.norm_eps)
+#define LC_EMB(TT, MV)                                                                                                    \
+  launch_chain(k_embed_ln<TT, MV>, dim3(lnb), dim3(256), 0, st, (const TT*)e->tok->data(), e->tok->shape[0], ids_dev,        \
+               (const float*)e->emb_norm->data(), (TT*)x, T, H, (float)c.norm_eps)
   if (c.dtype == LC_F16) {
     if (per <= 1) LC_EMB(__half, 1); else if (per <= 2) LC_EMB(__half, 2); else if (per <= 3) LC_EMB(__half, 3);
     else if (per <= 4) LC_EMB(__half, 4); else LC_EMB(__half, 8);
@@ -559,12 +568,14 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
     int C = (int)head_w->shape[0];
     size_t smem = C * sizeof(float);
     unsigned blocks = (unsigned)std::min(nseq, 65535);
+    const char* hb = head_b ? (const char*)head_b->data() : nullptr;
+    const int hbt = head_b ? head_b->dtype : 0;
     if (c.dtype == LC_F16)
-      k_cls_head<__half><<<blocks, 128, smem, st>>>((const __half*)fin, H, cu_dev, nseq, head_w->data(), head_w->dtype,
-                                                    head_b ? head_b->data() : nullptr, head_b ? head_b->dtype : 0, C, probs_dev);
+      launch_chain(k_cls_head<__half>, dim3(blocks), dim3(128), smem, st, (const __half*)fin, H, cu_dev, nseq, (const char*)head_w->data(),
+                   head_w->dtype, hb, hbt, C, probs_dev);
     else
-      k_cls_head<__nv_bfloat16><<<blocks, 128, smem, st>>>((const __nv_bfloat16*)fin, H, cu_dev, nseq, head_w->data(), head_w->dtype,
-                                                           head_b ? head_b->data() : nullptr, head_b ? head_b->dtype : 0, C, probs_dev);
+      launch_chain(k_cls_head<__nv_bfloat16>, dim3(blocks), dim3(128), smem, st, (const __nv_bfloat16*)fin, H, cu_dev, nseq,
+                   (const char*)head_w->data(), head_w->dtype, hb, hbt, C, probs_dev);
     LC_LAUNCHED(1);
   }
 }

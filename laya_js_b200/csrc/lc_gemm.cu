@@ -49,6 +49,7 @@ struct GemmArgs {
   const void* bias;
   int bias_dtype;
   GemmEpilogue ep;
+  int ksplit;  // split-K factor: the CTAs of a cluster of ksplit share a tile (k_gemm_tc with KS)
 };
 
 __device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
@@ -227,9 +228,14 @@ constexpr int PAIR_EPI_WARPS = 8;               // CTA-pair kernel: two staging 
 constexpr int PAIR_NBUF = 2;
 constexpr int PAIR_THREADS = 64 + 32 * PAIR_EPI_WARPS;
 
+// split-K partial tile: BM rows of BN f32 accumulators, rows padded by 16 bytes
+template <int BN>
+constexpr uint32_t part_bytes() {
+  return BM * (BN + 4) * 4;
+}
 template <int STAGES, int BN>
-constexpr size_t gemm_smem_bytes(bool tma_epi) {
-  return (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + (tma_epi ? STG_BYTES : 0) + 1024 + 256;
+constexpr size_t gemm_smem_bytes(bool tma_epi, bool ksplit = false) {
+  return (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + (tma_epi ? STG_BYTES : 0) + (ksplit ? part_bytes<BN>() : 0) + 1024 + 256;
 }
 
 // The TMA-store epilogue of both GEMM kernels (warps 2..9 of the CTA). Tiles
@@ -250,10 +256,22 @@ constexpr size_t gemm_smem_bytes(bool tma_epi) {
 // with two buffers a store drains while the next unit computes. The tile's
 // LayerNorm statistics and the first unit's LayerNorm column sums (one
 // coalesced load per warp, shared by shuffles) are read ahead as well.
-template <typename T, int BN, bool PAIR, int EW, int NBUF>
+//
+// Split K (KS, args.ksplit = S > 1, one tile per cluster): the S CTAs of a
+// cluster computed partial accumulators of the same tile over S slices of K.
+// CTA r owns the lane quarters q with q·S/4 == r. For each quarter, the warp
+// holding whole rows of the tile copies its partial rows from TMEM into this
+// CTA's shared memory (sSend, the idle pipeline stages) and one bulk copy
+// moves them into the owner's receive buffer (sP: one slot of 128/S rows per
+// CTA of the cluster), completing on the owner's pbar[0], which expects
+// 128 rows' worth of bytes. The owner's warps then add the S slots of their
+// rows in the fixed order 0..S-1 (the same bits whichever CTA is slower), put
+// the sums back into TMEM and run the ordinary epilogue on the sums.
+template <typename T, int BN, bool PAIR, int EW, int NBUF, bool KS = false>
 __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtensorMap* tmYp, const CUtensorMap* tmRp, uint8_t* sE, uint64_t* rbar,
                                              uint64_t* tfull, uint64_t* tempty, volatile int* abort, uint32_t tmem, int warp, int lane,
-                                             int t_begin, int t_step, int tile_rows, int row_off) {
+                                             int t_begin, int t_step, int tile_rows, int row_off, float* sP = nullptr,
+                                             float* sSend = nullptr, uint64_t* pbar = nullptr) {
   const CUtensorMap& tmY = *tmYp;
   const CUtensorMap& tmR = *tmRp;
   constexpr int NSUB = EW / 4;  // warps per lane quarter
@@ -286,20 +304,23 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
   bool ok = true;
   uint32_t nstore = 0;  // TMA stores issued by this warp
   const uint32_t tempty0 = PAIR ? mapa_rank(smem_u32(tempty), 0) : 0;  // CTA 0's accumulator-empty barriers
+  const int S = KS ? args.ksplit : 1;
+  const bool split = KS && S > 1;
+  const bool mine = !split || (quarter * S) / 4 == (int)cluster_rank();  // this warp's rows are reduced here
   for (int t = t_begin; t < args.ntiles && ok; t += t_step) {
     const int m0 = (t / args.ntile_n) * tile_rows + row_off, n0 = (t % args.ntile_n) * BN;
     const int row0 = m0 + quarter * 32;
     const int row = row0 + lane;
     const bool live = row < args.M;
     float ln_mu = 0.f, ln_r = 1.f;
-    if (ep.ln_stats) ln_row(ep, row, args.M, ln_mu, ln_r);
+    if (ep.ln_stats && mine) ln_row(ep, row, args.M, ln_mu, ln_r);
     const bool rope = ep.kind == EPI_ROPE_QKV && n0 + u_lo * 64 < ep.rope_cols;
     // this row's RoPE factors: table [16][cap] of (cos 2i, cos 2i+1, sin 2i, sin 2i+1)
     const float4* rq = (const float4*)ep.rope_cs + (rope && live ? ep.pos[row] : 0);
     // the first unit's LayerNorm column sums (lane l: columns 2l, 2l+1)
     float2 wsp = make_float2(0.f, 0.f);
-    if (ep.ln_stats) wsp = __ldg((const float2*)(ep.ln_wsum + n0 + u_lo * 64) + lane);
-    if (ahead) {  // the residual blocks, in flight while the accumulator is computed
+    if (ep.ln_stats && mine) wsp = __ldg((const float2*)(ep.ln_wsum + n0 + u_lo * 64) + lane);
+    if (ahead && mine) {  // the residual blocks, in flight while the accumulator is computed
       if (lane == 0) bulk_wait_read0();  // earlier stores have read the buffers
       __syncwarp();
       if (lane == 0)
@@ -311,6 +332,79 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
     if (!mbar_wait(&tfull[acc], acc_phase, abort, &g_gemm_err)) break;
     tc_fence_after();
     const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+    if constexpr (KS) {
+      if (split) {
+        // rows of lane quarter q are reduced by CTA q·S/4, which holds one
+        // slot of 128/S rows per CTA of the cluster
+        const int owner = (quarter * S) / 4, orows = BM / S;
+        const int lrow0 = (quarter - owner * (4 / S)) * 32;
+        if (u_lo == 0 && u_hi == U) {  // this warp holds whole rows of the tile: it sends the quarter
+          float* srow = sSend + (quarter * 32 + lane) * (BN + 4);
+#pragma unroll 1
+          for (int u = 0; u < U; u++) {
+            uint32_t ra[32], rbv[32];
+            tmem_ld32(tbase + u * 64, ra);
+            tmem_ld32(tbase + u * 64 + 32, rbv);
+            tmem_wait_ld();
+            float4* p4 = (float4*)(srow + u * 64);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              p4[j] = make_float4(__uint_as_float(ra[4 * j]), __uint_as_float(ra[4 * j + 1]), __uint_as_float(ra[4 * j + 2]),
+                                  __uint_as_float(ra[4 * j + 3]));
+              p4[8 + j] = make_float4(__uint_as_float(rbv[4 * j]), __uint_as_float(rbv[4 * j + 1]), __uint_as_float(rbv[4 * j + 2]),
+                                      __uint_as_float(rbv[4 * j + 3]));
+            }
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0)
+            bulk_copy_to_cluster(mapa_rank(smem_u32(sP + ((int)cluster_rank() * orows + lrow0) * (BN + 4)), (uint32_t)owner),
+                                 smem_u32(sSend + quarter * 32 * (BN + 4)), 32u * (BN + 4) * 4u,
+                                 mapa_rank(smem_u32(&pbar[0]), (uint32_t)owner));
+        }
+        if (!mine) {  // another CTA reduces these rows
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+          if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+          continue;
+        }
+        if (!mbar_wait(&pbar[0], 0, abort, &g_gemm_err)) break;
+        // sum the S slots of this row in the order 0, 1, ..., S-1
+        const float* p0 = sP + (lrow0 + lane) * (BN + 4);
+#pragma unroll 1
+        for (int u = u_lo; u < u_hi; u++) {
+#pragma unroll
+          for (int h = 0; h < 2; h++) {  // columns [32h, 32h+32) of the unit
+            const float4* src = (const float4*)(p0 + u * 64 + 32 * h);
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = src[j];
+            for (int c = 1; c < S; c++) {
+              const float4* sc = src + c * orows * (BN + 4) / 4;
+#pragma unroll
+              for (int j = 0; j < 8; j++) {
+                const float4 w = sc[j];
+                v[j].x += w.x;
+                v[j].y += w.y;
+                v[j].z += w.z;
+                v[j].w += w.w;
+              }
+            }
+            uint32_t r[32];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              r[4 * j] = __float_as_uint(v[j].x);
+              r[4 * j + 1] = __float_as_uint(v[j].y);
+              r[4 * j + 2] = __float_as_uint(v[j].z);
+              r[4 * j + 3] = __float_as_uint(v[j].w);
+            }
+            tmem_st32(tbase + u * 64 + 32 * h, r);
+          }
+        }
+        tmem_wait_st();
+      }
+    }
 #pragma unroll 1
     for (int u = u_lo; u < u_hi; u++) {
       const int col = n0 + u * 64;
@@ -435,10 +529,15 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
   __syncwarp();
 }
 
-template <typename T, int BN, int STAGES, bool TMAE>
+// KS: split K over the CTAs of a cluster of args.ksplit (launched with that
+// cluster size, one K slice per CTA rank): the unit of work is (tile, slice),
+// CTA rank r takes K blocks [r·KB/S, (r+1)·KB/S) of its cluster's tiles and
+// the epilogue reduces the partial tiles through distributed shared memory.
+template <typename T, int BN, int STAGES, bool TMAE, bool KS = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                                     const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                                                     const __grid_constant__ GemmArgs args) {
+  static_assert(!KS || TMAE, "split K runs with the TMA-store epilogue");
   extern __shared__ uint8_t smem_raw[];
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
@@ -447,16 +546,26 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sE = sB + STAGES * B_BYTES;  // epilogue staging (TMAE only), 1024-aligned
-  uint64_t* full = (uint64_t*)(sE + (TMAE ? STG_BYTES : 0));
+  float* sP = (float*)(sE + (TMAE ? STG_BYTES : 0));  // split-K partial tile (KS only)
+  uint64_t* full = (uint64_t*)((uint8_t*)sP + (KS ? part_bytes<BN>() : 0));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* rbar = tempty + 2;  // residual-load barriers, one per epilogue warp
-  uint32_t* tmem_slot = (uint32_t*)(rbar + EPI_WARPS);
+  uint64_t* pbar = rbar + EPI_WARPS;  // KS: the partial slots of this CTA's rows have landed
+  uint32_t* tmem_slot = (uint32_t*)(pbar + 1);
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = (args.K + BK - 1) / BK;
+  const int S = KS ? args.ksplit : 1;
+  static_assert(!KS || part_bytes<BN>() <= STAGES * (A_BYTES + B_BYTES), "split-K send buffer larger than the pipeline stages");
+  pdl_trigger();
+  if (KS && S > 1 && (int)(gridDim.x / S) < args.ntiles) {  // split K takes one tile per cluster
+    pdl_wait();
+    if (threadIdx.x == 0) atomicOr(&g_gemm_err, 2u);
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -468,6 +577,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], EPI_WARPS);
     }
+    mbar_init(&pbar[0], 1);
+    if (KS && S > 1) mbar_arrive_expect_tx(&pbar[0], part_bytes<BN>());  // S slots of 128/S rows
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -477,24 +588,29 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
+  }
+  if constexpr (KS) cluster_sync();  // every CTA's barriers exist before a remote arrival
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the kernel that wrote the activations has completed
 
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       int issued[STAGES];
       uint32_t iss_phase[STAGES];
       for (int s = 0; s < STAGES; s++) issued[s] = 0, iss_phase[s] = 0;
-      for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
+      for (int w = blockIdx.x; w < args.ntiles * S && ok; w += gridDim.x) {
+        const int t = w / S, kb0 = (w % S) * KB / S, kb1 = (w % S + 1) * KB / S;
         int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
-        for (int kb = 0; kb < KB; kb++) {
+        for (int kb = kb0; kb < kb1; kb++) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
           tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, m0);
@@ -523,17 +639,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       bool committed = false;
       uint64_t* last = nullptr;
       uint32_t last_phase = 0;
-      for (int t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
+      for (int w = blockIdx.x; w < args.ntiles * S && ok; w += gridDim.x) {
+        const int kb0 = (w % S) * KB / S, kb1 = (w % S + 1) * KB / S;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < KB; kb++) {
+        for (int kb = kb0; kb < kb1; kb++) {
           if (!mbar_wait(&full[stage], phase, abort, &g_gemm_err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * A_BYTES), b0 = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; k++)
-            tc_mma(d, sdesc_sw128(a0 + k * 32), sdesc_sw128(b0 + k * 32), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_mma(d, sdesc_sw128(a0 + k * 32), sdesc_sw128(b0 + k * 32), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           tc_commit(&empty[stage]);
           committed = true;
           last = &empty[stage];
@@ -551,7 +668,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       }
     }
   } else if constexpr (TMAE) {
-    epilogue_tma<T, BN, false, EPI_WARPS, 1>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x, gridDim.x, BM, 0);
+    epilogue_tma<T, BN, false, EPI_WARPS, 1, KS>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x / S,
+                                                 gridDim.x / S, BM, 0, sP, (float*)sA, pbar);
   } else {
     // ---------------- epilogue (warps 2..9 -> TMEM lane quarter warp % 4, half of the units each)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
@@ -632,7 +750,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
     while (gtimer() - t0 < 1000000ull) {}
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (KS) cluster_sync();  // no CTA leaves while another may read its partial or arrive on its barriers
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
@@ -678,6 +797,7 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) k_gemm_pair(const __grid_cons
   const int KB = (args.K + BK - 1) / BK;
   const uint32_t rank = cluster_rank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -697,16 +817,19 @@ __global__ void __launch_bounds__(PAIR_THREADS, 1) k_gemm_pair(const __grid_cons
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
+  }
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers exist before any remote arrival or copy
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the kernel that wrote the activations has completed
 
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs)
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
       const uint32_t full0 = mapa_rank(smem_u32(full), 0);  // CTA 0's full[0]
       int stage = 0;
       uint32_t phase = 0;
@@ -842,7 +965,60 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap
     attr = true;
   }
   int grid = std::min(a.ntiles, lc::num_sms());
-  k_gemm_tc<T, BN, STAGES, TMAE><<<grid, GEMM_THREADS, smem, st>>>(ma, mb, my, mr, a);
+  lc::launch_chain(k_gemm_tc<T, BN, STAGES, TMAE>, dim3(grid), dim3(GEMM_THREADS), smem, st, ma, mb, my, mr, a);
+}
+
+// Split K: clusters of a.ksplit CTAs, one cluster per tile while they fit.
+template <typename T, int BN, int STAGES>
+cudaLaunchConfig_t split_config(int S, cudaLaunchAttribute* at, cudaStream_t st) {
+  constexpr size_t smem = gemm_smem_bytes<STAGES, BN>(true, true);
+  static_assert(smem <= 232448, "GEMM shared memory above the 227 KB per-CTA limit");
+  static bool attr = false;
+  if (!attr) {
+    CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<T, BN, STAGES, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = S;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  lc::chain_attrs(cfg, at, 1);
+  return cfg;
+}
+// clusters of S of this instance that can be resident at once
+template <typename T, int BN, int STAGES>
+int split_capacity(int S) {
+  static int cap[5] = {0, 0, 0, 0, 0};
+  if (!cap[S]) {
+    cudaLaunchAttribute at[2];
+    cudaLaunchConfig_t cfg = split_config<T, BN, STAGES>(S, at, nullptr);
+    cfg.gridDim = dim3(S * (lc::num_sms() / S));
+    int n = 0;
+    CUDA_OK(cudaOccupancyMaxActiveClusters(&n, k_gemm_tc<T, BN, STAGES, true, true>, &cfg));
+    LC_CHECK(n > 0, "tcgen05 GEMM: no split-K cluster fits");
+    cap[S] = n;
+  }
+  return cap[S];
+}
+template <typename T, int BN, int STAGES>
+void launch_gemm_split(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr, const GemmArgs& a,
+                       cudaStream_t st) {
+  const int S = a.ksplit;
+  LC_CHECK(S == 1 || S == 2 || S == 4, "tcgen05 GEMM: split-K factor must be 1, 2 or 4");
+  cudaLaunchAttribute at[2];
+  cudaLaunchConfig_t cfg = split_config<T, BN, STAGES>(S, at, st);
+  const int cap = split_capacity<T, BN, STAGES>(S);
+  LC_CHECK(S == 1 || a.ntiles <= cap, "tcgen05 GEMM: split K needs one resident cluster per tile");
+  cfg.gridDim = dim3(S * std::min(a.ntiles, cap));
+  CUDA_OK(cudaLaunchKernelEx(&cfg, k_gemm_tc<T, BN, STAGES, true, true>, ma, mb, my, mr, a));
+}
+int split_capacity_for(int dtype, int BN, int S) {
+  if (dtype == LC_F16) return BN == 64 ? split_capacity<__half, 64, 4>(S) : split_capacity<__half, 128, 3>(S);
+  return BN == 64 ? split_capacity<__nv_bfloat16, 64, 4>(S) : split_capacity<__nv_bfloat16, 128, 3>(S);
 }
 
 template <typename T, int STAGES>
@@ -851,7 +1027,7 @@ void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtens
   static_assert(smem <= 232448, "GEMM shared memory above the 227 KB per-CTA limit");
   static int max_pairs = 0;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 2;
   at[0].val.clusterDim.y = 1;
@@ -859,8 +1035,7 @@ void launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtens
   cfg.blockDim = dim3(PAIR_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
+  lc::chain_attrs(cfg, at, 1);
   if (!max_pairs) {
     CUDA_OK(cudaFuncSetAttribute(k_gemm_pair<T, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cfg.gridDim = dim3(2 * (lc::num_sms() / 2));
@@ -888,6 +1063,17 @@ bool gemm_use_pair(int64_t K) {
     on = (v && v[0] == '0') ? 0 : 1;
   }
   (void)K;
+  return on == 1;
+}
+
+// Small-M launches use narrow tiles with K split over clusters;
+// LAYA_CUDA_GEMM_SPLIT=0 keeps them on the ordinary tiles (both are tested).
+bool gemm_use_split() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("LAYA_CUDA_GEMM_SPLIT");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
   return on == 1;
 }
 
@@ -920,11 +1106,41 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
   a.bias = bias;
   a.bias_dtype = bias_dtype;
   a.ep = ep;
+  a.ksplit = 1;
   const CUtensorMap& ma = tensor_map(x, M, K, K, BK, BM, dtype);
   const CUtensorMap& mb = tensor_map(w, Nacc, K, K, BK, BN, dtype);
   // TMA-store epilogue when the output (and residual) rows are 16-byte strided and aligned
   const bool tmae = a.vec_ok && (N % 8 == 0) && !(ep.kind == EPI_RESIDUAL && ep.resid == nullptr);
-  if (tmae && BN == 256 && gemm_use_pair(K)) {
+  const int sms = lc::num_sms();
+  if (tmae && gemm_use_split() && tiles * 4 <= sms) {
+    // Few rows (one prompt, a small batch): the natural tiles would occupy a
+    // few SMs, each bound by its own tensor pipe. Narrow tiles (64 columns,
+    // 128 for GeGLU's gate/up pairs) and K split over clusters of up to 4 CTAs
+    // spread the weight stream and the MMAs over most of the GPU.
+    const int BNs = ep.kind == EPI_GEGLU ? 128 : 64;
+    const int64_t mt = (M + BM - 1) / BM, nt = (Nacc + BNs - 1) / BNs;
+    const int KB = (int)((K + BK - 1) / BK);
+    int S = 1;
+    for (int c : {4, 2})
+      if (mt * nt * c <= sms && KB >= c && mt * nt <= split_capacity_for(dtype, BNs, c)) {
+        S = c;
+        break;
+      }
+    GemmArgs as = a;
+    as.ntile_n = (int)nt;
+    as.ntiles = (int)(mt * nt);
+    as.ksplit = S;
+    const CUtensorMap& mbs = tensor_map(w, Nacc, K, K, BK, BNs, dtype);
+    const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
+    const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
+    if (dtype == LC_F16) {
+      if (BNs == 64) launch_gemm_split<__half, 64, 4>(ma, mbs, my, mr, as, st);
+      else launch_gemm_split<__half, 128, 3>(ma, mbs, my, mr, as, st);
+    } else {
+      if (BNs == 64) launch_gemm_split<__nv_bfloat16, 64, 4>(ma, mbs, my, mr, as, st);
+      else launch_gemm_split<__nv_bfloat16, 128, 3>(ma, mbs, my, mr, as, st);
+    }
+  } else if (tmae && BN == 256 && gemm_use_pair(K)) {
     // CTA pairs: 256 x 256 tiles
     const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
     const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
@@ -981,7 +1197,8 @@ std::string take_device_errors() {
   std::string msg = take_attention_errors();
   if (!e) return msg;
   CUDA_OK(cudaMemcpyToSymbol(g_gemm_err, &z, sizeof(z)));
-  return "tcgen05 GEMM: a pipeline wait timed out (kernel aborted its tile loop)" + (msg.empty() ? std::string() : "; " + msg);
+  std::string what = (e & 1u) ? "a pipeline wait timed out (kernel aborted its tile loop)" : "a split-K launch had more tiles than clusters";
+  return "tcgen05 GEMM: " + what + (msg.empty() ? std::string() : "; " + msg);
 }
 
 const CUtensorMap& tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype) {

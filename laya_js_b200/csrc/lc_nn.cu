@@ -18,6 +18,8 @@ using namespace lc;
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
                                                        T* __restrict__ y, int64_t rows, int N, float eps) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int VN = 16 / sizeof(T);
   int lane = threadIdx.x & 31;
   int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -95,12 +97,12 @@ void launch_layernorm_vec(const T* x, const float* w, const float* b, T* y, int6
   int per = (N / VN + 31) / 32;
   unsigned blocks = lc::blocks_for(rows * 32, 256);
   switch (per) {
-    case 0: case 1: k_layernorm_vec<T, 1><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    case 2: k_layernorm_vec<T, 2><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    case 3: k_layernorm_vec<T, 3><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    case 4: k_layernorm_vec<T, 4><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    case 5: case 6: k_layernorm_vec<T, 6><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    default: k_layernorm_vec<T, 8><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 0: case 1: lc::launch_chain(k_layernorm_vec<T, 1>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 2: lc::launch_chain(k_layernorm_vec<T, 2>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 3: lc::launch_chain(k_layernorm_vec<T, 3>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 4: lc::launch_chain(k_layernorm_vec<T, 4>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 5: case 6: lc::launch_chain(k_layernorm_vec<T, 6>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    default: lc::launch_chain(k_layernorm_vec<T, 8>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
   }
 }
 

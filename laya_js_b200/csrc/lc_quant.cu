@@ -26,6 +26,8 @@ using namespace lc;
 // dequantise rows [N, K] -> out [N, K] in out dtype
 __global__ void k_dequant(const uint8_t* __restrict__ w, const char* s, const char* b, int sdt, int bits, int g, int mode, int64_t N,
                           int64_t K, char* out, int odt) {
+  pdl_trigger();
+  pdl_wait();
   int64_t G = (K + g - 1) / g;
   LC_GRID_STRIDE(t, N * K) {
     int64_t r = t / K, j = t % K;
@@ -41,6 +43,8 @@ __global__ void k_dequant(const uint8_t* __restrict__ w, const char* s, const ch
 // LayerNorm multiplies by (the dense path folds the stored weight the same way)
 __global__ void k_dequant_scaled(const uint8_t* __restrict__ w, const char* s, const char* b, int sdt, int bits, int g, int mode, int64_t N,
                                  int64_t K, const float* __restrict__ gamma, char* out, int odt) {
+  pdl_trigger();
+  pdl_wait();
   int64_t G = (K + g - 1) / g;
   LC_GRID_STRIDE(t, N * K) {
     int64_t r = t / K, j = t % K;
@@ -145,15 +149,15 @@ namespace lc {
 // Dequantise the whole matrix into `out` [N, K] (dense, dtype = out->dtype).
 void dequant_into(const LcTensor* w, const LcTensor* s, const LcTensor* b, int bits, int g, int mode, LcTensor* out) {
   int64_t N = w->shape[0], K = w->shape[1] * 8 / bits;
-  k_dequant<<<blocks_for(N * K, 256), 256, 0, stream()>>>((const uint8_t*)w->data(), s->data(), b ? b->data() : nullptr, s->dtype, bits, g,
-                                                           mode, N, K, out->data(), out->dtype);
+  launch_chain(k_dequant, dim3(blocks_for(N * K, 256)), dim3(256), 0, stream(), (const uint8_t*)w->data(), (const char*)s->data(),
+               b ? (const char*)b->data() : nullptr, s->dtype, bits, g, mode, N, K, (char*)out->data(), out->dtype);
   LC_LAUNCHED(1);
 }
 // The same with column k scaled by gamma[k] (f32, K values), out f16/bf16.
 void dequant_scaled_into(const LcTensor* w, const LcTensor* s, const LcTensor* b, int bits, int g, int mode, const float* gamma, LcTensor* out) {
   int64_t N = w->shape[0], K = w->shape[1] * 8 / bits;
-  k_dequant_scaled<<<blocks_for(N * K, 256), 256, 0, stream()>>>((const uint8_t*)w->data(), s->data(), b ? b->data() : nullptr, s->dtype,
-                                                                  bits, g, mode, N, K, gamma, out->data(), out->dtype);
+  launch_chain(k_dequant_scaled, dim3(blocks_for(N * K, 256)), dim3(256), 0, stream(), (const uint8_t*)w->data(), (const char*)s->data(),
+               b ? (const char*)b->data() : nullptr, s->dtype, bits, g, mode, N, K, gamma, (char*)out->data(), out->dtype);
   LC_LAUNCHED(1);
 }
 }  // namespace lc

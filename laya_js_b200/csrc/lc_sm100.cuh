@@ -196,6 +196,14 @@ static __device__ __forceinline__ uint32_t mapa_rank(uint32_t a, uint32_t rank) 
 static __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Bulk copy of `bytes` (multiple of 16, both ends 16-byte aligned) from this
+// CTA's shared memory into another CTA's (cluster address), counted as
+// complete_tx on the mbarrier at cluster address `bar` in the destination CTA.
+static __device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint32_t src, uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_cluster), "r"(src),
+               "r"(bytes), "r"(bar_cluster)
+               : "memory");
+}
 // every thread of every CTA of the cluster
 static __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");

@@ -1,8 +1,9 @@
-"""Both tcgen05 GEMM kernels — single CTA and CTA pair (cta_group::2) — on the
-shapes that select 256-wide tiles, each forced through LAYA_CUDA_GEMM_PAIR in a
-fresh process (the choice is read once per process), against an f64 reference,
-plus the fused encoder's epilogues (RoPE, GeGLU, residual + folded LayerNorm)
-compared between the two kernels."""
+"""The tcgen05 GEMM kernels — single CTA, CTA pair (cta_group::2) and the
+small-M split-K clusters — each forced through LAYA_CUDA_GEMM_PAIR /
+LAYA_CUDA_GEMM_SPLIT in a fresh process (the choice is read once per
+process), against an f64 reference, plus the fused encoder's epilogues (RoPE,
+GeGLU, residual + folded LayerNorm) compared between the kernels on a batch
+of 1023 tokens and on single short prompts (the split-K shapes)."""
 from __future__ import annotations
 
 import json
@@ -41,25 +42,35 @@ enc = loadModernBert(b, parseModernBertConfig(cfg), WL.host_getter(W), "f16")
 fused = E.FusedEncoder(enc)
 ids, cu = WL.token_batch(cfg, np.array([300, 17, 513, 129, 64]), seed=6)
 h, _ = fused.forward(b.fromHost(HostTensor("i32", ids.shape, ids)), cu)
-np.save(sys.argv[2], to_f32(b.read(h)))
+hs = [to_f32(b.read(h))]
+for lens in ([128], [33, 95], [7]):
+    ids, cu = WL.token_batch(cfg, np.array(lens), seed=7)
+    h, _ = fused.forward(b.fromHost(HostTensor("i32", ids.shape, ids)), cu)
+    hs.append(to_f32(b.read(h)))
+np.savez(sys.argv[2], *hs)
 print(json.dumps({"gemm_err_over_tol": worst}))
 '''
 
 
-def _run(mode: str, tmp_path) -> tuple[float, str]:
-    out = tmp_path / f"hidden_{mode}.npy"
-    env = dict(os.environ, LAYA_CUDA_GEMM_PAIR=mode)
+def _run(pair: str, split: str, tmp_path) -> tuple[float, str]:
+    out = tmp_path / f"hidden_{pair}{split}.npz"
+    env = dict(os.environ, LAYA_CUDA_GEMM_PAIR=pair, LAYA_CUDA_GEMM_SPLIT=split)
     r = subprocess.run([sys.executable, "-c", SCRIPT, str(ROOT), str(out)], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     return json.loads(r.stdout.strip().splitlines()[-1])["gemm_err_over_tol"], str(out)
 
 
-def test_single_and_pair_kernels_agree(tmp_path):
+def test_single_pair_and_split_kernels_agree(tmp_path):
     import numpy as np
-    e1, h1 = _run("0", tmp_path)
-    e2, h2 = _run("1", tmp_path)
-    assert e1 <= 1.0, f"single-CTA GEMM: error {e1:.2f} x tolerance"
-    assert e2 <= 1.0, f"CTA-pair GEMM: error {e2:.2f} x tolerance"
-    a, b = np.load(h1), np.load(h2)
-    assert a.shape == b.shape
-    assert np.abs(a - b).max() < 2e-2, f"encoder hidden states differ by {np.abs(a - b).max()} between the kernels"
+    runs = {name: _run(pair, split, tmp_path) for name, pair, split in
+            (("single-CTA", "0", "0"), ("CTA-pair", "1", "0"), ("split-K", "1", "1"))}
+    for name, (err, _) in runs.items():
+        assert err <= 1.0, f"{name} GEMM: error {err:.2f} x tolerance"
+    ref = np.load(runs["single-CTA"][1])
+    for name in ("CTA-pair", "split-K"):
+        got = np.load(runs[name][1])
+        for key in ref.files:
+            a, b = ref[key], got[key]
+            assert a.shape == b.shape
+            d = float(np.abs(a - b).max())
+            assert d < 2e-2, f"encoder hidden states ({key}) differ by {d} between single-CTA and {name}"
