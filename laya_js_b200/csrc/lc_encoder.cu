@@ -392,7 +392,9 @@ void run_gemm(Encoder* e, const Mat& m, const void* x, int64_t M, void* y, int64
     w = e->deq->data();
   }
   Prof p(e, cls);
-  bool ok = gemm_raw(x, M, m.K, w, n_out, nullptr, 0, y, ldy, e->cfg.dtype, ep, stream());
+  GemmEpilogue epw = ep;
+  epw.w_static = m.dense != nullptr;  // the dequantisation scratch is written inside the chain
+  bool ok = gemm_raw(x, M, m.K, w, n_out, nullptr, 0, y, ldy, e->cfg.dtype, epw, stream());
   LC_CHECK(ok, "encoder: the tcgen05 GEMM rejected a projection shape");
 }
 

@@ -596,6 +596,27 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
   else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // A weight no kernel of the chain writes is requested before the
+  // dependency wait: the first tile's first STAGES weight blocks go to their
+  // stages (whose barriers then expect the activation block as well) and the
+  // rest of its K range into L2.
+  int pre = 0;
+  int issued[STAGES];
+  uint32_t iss_phase[STAGES];
+  for (int s = 0; s < STAGES; s++) issued[s] = 0, iss_phase[s] = 0;
+  if (warp == 0 && lane == 0 && args.ep.w_static && (int)blockIdx.x < args.ntiles * S) {
+    const int w = blockIdx.x, t = w / S, kb0 = (w % S) * KB / S, kb1 = (w % S + 1) * KB / S;
+    const int n0 = (t % args.ntile_n) * BN;
+    for (int kb = kb0; kb < kb1; kb++) {
+      if (pre < STAGES) {
+        mbar_arrive_expect_tx(&full[pre], A_BYTES + B_BYTES);
+        tma_load_2d(sB + pre * B_BYTES, &tmB, &full[pre], kb * BK, n0);
+        issued[pre++] = 1;
+      } else {
+        tma_prefetch_l2(&tmB, kb * BK, n0);
+      }
+    }
+  }
   pdl_wait();  // the kernel that wrote the activations has completed
 
   if (warp == 0) {
@@ -604,17 +625,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int issued[STAGES];
-      uint32_t iss_phase[STAGES];
-      for (int s = 0; s < STAGES; s++) issued[s] = 0, iss_phase[s] = 0;
+      int it = 0;  // k blocks issued so far (the first `pre` have their weight block in flight)
       for (int w = blockIdx.x; w < args.ntiles * S && ok; w += gridDim.x) {
         const int t = w / S, kb0 = (w % S) * KB / S, kb1 = (w % S + 1) * KB / S;
         int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
-        for (int kb = kb0; kb < kb1; kb++) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
-          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, m0);
-          tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, n0);
+        for (int kb = kb0; kb < kb1; kb++, it++) {
+          if (it < pre) {
+            tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, m0);
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+            tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, m0);
+            tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, n0);
+          }
           issued[stage] = 1;
           iss_phase[stage] = phase;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }

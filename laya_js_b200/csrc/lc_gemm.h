@@ -29,6 +29,10 @@ struct GemmEpilogue {
   const float* ln_wsum = nullptr;    // Σ_k W[n, k]·γ[k] per accumulator column n (16-byte aligned)
   int ln_parts = 0, ln_part_cols = 0, ln_cols = 0;
   float ln_eps = 0.f;
+  // The weight is not written by any kernel of the current launch chain (a
+  // resident dense weight, not a dequantisation scratch): the kernel may
+  // request it before waiting for its predecessor.
+  bool w_static = false;
 };
 
 namespace lc {

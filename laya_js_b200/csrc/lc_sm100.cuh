@@ -59,6 +59,10 @@ static __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap*
       "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// Pull a tile of a tensor map into L2 (no shared-memory destination).
+static __device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"((uint64_t)map), "r"(x), "r"(y) : "memory");
+}
 static __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 static __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 static __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
