@@ -243,6 +243,11 @@ struct Prof {
       e->pending.push_back({cls, {a, b}});
     }
   }
+  // nothing was launched in this interval: drop it
+  void cancel() {
+    if (a) e->ev_pool.push_back(a);
+    a = nullptr;
+  }
 };
 
 std::unordered_set<Encoder*>& encoders() {
@@ -377,6 +382,21 @@ void run_gemm(Encoder* e, const Mat& m, const void* x, int64_t M, void* y, int64
   if (m.dense) {
     w = m.dense->data();
   } else {
+    // few rows: dequantise inside the GEMM (the weight stream dominates)
+    GemmQuantB qb;
+    qb.w = (const uint8_t*)m.q->data();
+    qb.scales = m.s->data();
+    qb.biases = m.b ? m.b->data() : nullptr;
+    qb.sdt = m.s->dtype;
+    qb.bits = e->cfg.quant_bits;
+    qb.group = e->cfg.quant_group;
+    qb.mode = e->cfg.quant_mode;
+    qb.gamma = m.gamma;
+    {
+      Prof p(e, cls);
+      if (gemm_raw_q(x, M, m.K, qb, n_out, nullptr, 0, y, ldy, e->cfg.dtype, ep, stream())) return;
+      p.cancel();
+    }
     if (!e->deq || e->deq->numel() < m.N * m.K) {
       if (e->deq) release(e->deq);
       int64_t biggest = 0;

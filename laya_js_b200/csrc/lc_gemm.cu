@@ -25,6 +25,7 @@
 #include "lc_api.h"
 #include "lc_gemm.h"
 #include "lc_sm100.cuh"
+#include "lc_quant.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -50,6 +51,7 @@ struct GemmArgs {
   int bias_dtype;
   GemmEpilogue ep;
   int ksplit;  // split-K factor: the CTAs of a cluster of ksplit share a tile (k_gemm_tc with KS)
+  GemmQuantB q;  // QB: the packed weight (tmB maps its bytes)
 };
 
 __device__ __forceinline__ float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
@@ -233,9 +235,108 @@ template <int BN>
 constexpr uint32_t part_bytes() {
   return BM * (BN + 4) * 4;
 }
+// QB: packed weight block of one stage (BN rows of BK values, at most 8 bits each)
+template <int BN>
+constexpr uint32_t packed_bytes() {
+  return BN * BK;
+}
 template <int STAGES, int BN>
-constexpr size_t gemm_smem_bytes(bool tma_epi, bool ksplit = false) {
-  return (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + (tma_epi ? STG_BYTES : 0) + (ksplit ? part_bytes<BN>() : 0) + 1024 + 256;
+constexpr size_t gemm_smem_bytes(bool tma_epi, bool ksplit = false, bool qb = false) {
+  return (size_t)STAGES * (BM * BK * 2 + BN * BK * 2 + (qb ? packed_bytes<BN>() : 0)) + (tma_epi ? STG_BYTES : 0) +
+         (ksplit ? part_bytes<BN>() : 0) + 1024 + 512;
+}
+
+// QB: the epilogue warps turn a stage's packed weight block (BN rows x BK
+// values; rows >= N and columns >= K arrive as zero bytes) into the MMA's
+// 16-bit operand in the 128-byte-swizzled K-major layout a TMA load would
+// produce: 16-byte chunk c (values 8c..8c+7) of row r at r·128 + ((c ^ (r&7))·16).
+// Thread et takes chunks (r, c) = divmod(et + 32·EPI_WARPS·i, 8).
+// Each value equals what the dense dequantisation kernels store
+// (dequant_rounded, then the optional column scale in f32 and one rounding),
+// so the product is bit-identical to dequantising first. For f16 scales,
+// biases and output the value is one fma.rn.f16x2: q (|q| <= 255), s and b
+// are exact in f16, so q·s + b is an exact multiple of 2^-24 below 2^24 — at
+// most 48 significant bits, exact in the f64 form too — and both round it
+// once to f16.
+template <int BN>
+constexpr int conv_tasks() {
+  return BN * 8 / (32 * EPI_WARPS);
+}
+// the scale and bias of each of this thread's chunks of K block kb (issued before the block lands)
+template <int BN>
+__device__ __forceinline__ void load_packed_scales(const GemmArgs& args, int n0, int kb, int et, float2* sb) {
+  const GemmQuantB& q = args.q;
+  const int64_t G = (args.K + q.group - 1) / q.group;
+  const int nrows = args.N * (args.ep.kind == EPI_GEGLU ? 2 : 1);
+#pragma unroll
+  for (int i = 0; i < conv_tasks<BN>(); i++) {
+    const int task = et + 32 * EPI_WARPS * i, r = task >> 3, c = task & 7;
+    const int n = n0 + r, k = kb * BK + 8 * c;
+    sb[i] = make_float2(0.f, 0.f);
+    if (n < nrows && k < args.K) {
+      const int64_t gi = (int64_t)n * G + k / q.group;
+      sb[i].x = ld_as<float>((const char*)q.scales, q.sdt, gi);
+      sb[i].y = q.biases ? ld_as<float>((const char*)q.biases, q.sdt, gi) : 0.f;
+    }
+  }
+}
+template <typename T, int BN>
+__device__ __forceinline__ void convert_packed_block(const GemmArgs& args, const uint8_t* pk, uint8_t* sb_out, int n0, int kb, int et,
+                                                     const float2* sb) {
+  const GemmQuantB& q = args.q;
+  const int bits = q.bits, rowb = BK * bits / 8;
+  const int nrows = args.N * (args.ep.kind == EPI_GEGLU ? 2 : 1);
+  constexpr bool HALF = std::is_same<T, __half>::value;
+  const bool fast = HALF && q.sdt == LC_F16;
+#pragma unroll
+  for (int i = 0; i < conv_tasks<BN>(); i++) {
+    const int task = et + 32 * EPI_WARPS * i, r = task >> 3, c = task & 7;
+    const int n = n0 + r, k = kb * BK + 8 * c;
+    uint4 out = make_uint4(0u, 0u, 0u, 0u);
+    if (n < nrows && k < args.K) {
+      const uint8_t* src = pk + r * rowb + c * bits;  // 8 values: 4 or 8 bytes
+      const uint64_t raw = bits == 4 ? (uint64_t)*(const uint32_t*)src : *(const uint64_t*)src;
+      int qv[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (bits == 4) {
+          const int nib = (int)((raw >> (4 * j)) & 15u);
+          qv[j] = q.mode == 0 ? ((nib ^ 8) - 8) : nib;
+        } else {
+          const int byte = (int)((raw >> (8 * j)) & 255u);
+          qv[j] = q.mode == 0 ? (int)(int8_t)byte : byte;
+        }
+      }
+      const bool full8 = k + 8 <= args.K;
+      if (fast && full8) {
+        const __half2 s2 = __float2half2_rn(sb[i].x), b2 = __float2half2_rn(sb[i].y);  // exact: f16 values
+        __half2 h[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) h[j] = __hfma2(__halves2half2(__int2half_rn(qv[2 * j]), __int2half_rn(qv[2 * j + 1])), s2, b2);
+        if (q.gamma) {
+          const float4 g0 = __ldg((const float4*)(q.gamma + k)), g1 = __ldg((const float4*)(q.gamma + k + 4));
+          const float2 gg[4] = {make_float2(g0.x, g0.y), make_float2(g0.z, g0.w), make_float2(g1.x, g1.y), make_float2(g1.z, g1.w)};
+#pragma unroll
+          for (int j = 0; j < 4; j++) h[j] = __float22half2_rn(mul2(__half22float2(h[j]), gg[j]));
+        }
+        out = *(const uint4*)h;
+      } else {
+        const int odt = HALF ? LC_F16 : LC_BF16;
+        T v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          float d = 0.f;
+          if (k + j < args.K) {
+            d = dequant_rounded(odt, qv[j], sb[i].x, sb[i].y);
+            if (q.gamma) d = d * __ldg(q.gamma + k + j);
+          }
+          v[j] = TcFmt<T>::cvt(d);
+        }
+        out = *(const uint4*)v;
+      }
+    }
+    *(uint4*)(sb_out + r * 128 + ((c ^ (r & 7)) << 4)) = out;
+  }
 }
 
 // The TMA-store epilogue of both GEMM kernels (warps 2..9 of the CTA). Tiles
@@ -533,7 +634,15 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
 // cluster size, one K slice per CTA rank): the unit of work is (tile, slice),
 // CTA rank r takes K blocks [r·KB/S, (r+1)·KB/S) of its cluster's tiles and
 // the epilogue reduces the partial tiles through distributed shared memory.
-template <typename T, int BN, int STAGES, bool TMAE, bool KS = false>
+//
+// QB: the weight is packed 4/8-bit (args.q; tmB maps its bytes). The producer
+// loads the packed blocks (pfull) beside the activation blocks (full); the
+// epilogue warps, idle until the accumulator is ready, dequantise each block
+// into the stage's 16-bit operand (convert_packed_block) and arrive on
+// conv[stage], which the MMA issuer waits for as well. The packed weight is
+// resident, so its first blocks are requested and converted before the
+// dependency wait. One unit of work per CTA.
+template <typename T, int BN, int STAGES, bool TMAE, bool KS = false, bool QB = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                                     const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                                                     const __grid_constant__ GemmArgs args) {
@@ -544,8 +653,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
   constexpr uint32_t TMEM_COLS = 2 * BN;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
+  constexpr uint32_t PK_BYTES = QB ? packed_bytes<BN>() : 0;  // packed stage buffer (QB)
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sE = sB + STAGES * B_BYTES;  // epilogue staging (TMAE only), 1024-aligned
+  uint8_t* sPk = sB + STAGES * B_BYTES;
+  uint8_t* sE = sPk + STAGES * PK_BYTES;  // epilogue staging (TMAE only), 1024-aligned
   float* sP = (float*)(sE + (TMAE ? STG_BYTES : 0));  // split-K partial tile (KS only)
   uint64_t* full = (uint64_t*)((uint8_t*)sP + (KS ? part_bytes<BN>() : 0));
   uint64_t* empty = full + STAGES;
@@ -553,15 +664,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
   uint64_t* tempty = tfull + 2;
   uint64_t* rbar = tempty + 2;  // residual-load barriers, one per epilogue warp
   uint64_t* pbar = rbar + EPI_WARPS;  // KS: the partial slots of this CTA's rows have landed
-  uint32_t* tmem_slot = (uint32_t*)(pbar + 1);
+  uint64_t* pfull = pbar + 1;                  // QB: packed block landed
+  uint64_t* conv = pfull + (QB ? STAGES : 0);  // QB: 16-bit operand written
+  uint32_t* tmem_slot = (uint32_t*)(conv + (QB ? STAGES : 0));
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = (args.K + BK - 1) / BK;
   const int S = KS ? args.ksplit : 1;
+  static_assert(!QB || (KS && TMAE), "the packed-weight GEMM runs as the split-K instance");
+  static_assert(PK_BYTES % 1024 == 0, "staging must stay 1024-byte aligned");
   static_assert(!KS || part_bytes<BN>() <= STAGES * (A_BYTES + B_BYTES), "split-K send buffer larger than the pipeline stages");
   pdl_trigger();
-  if (KS && S > 1 && (int)(gridDim.x / S) < args.ntiles) {  // split K takes one tile per cluster
+  if ((KS && S > 1 && (int)(gridDim.x / S) < args.ntiles) || (QB && (int)gridDim.x < args.ntiles * S)) {  // one unit per cluster / CTA
     pdl_wait();
     if (threadIdx.x == 0) atomicOr(&g_gemm_err, 2u);
     return;
@@ -579,6 +694,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
     }
     mbar_init(&pbar[0], 1);
     if (KS && S > 1) mbar_arrive_expect_tx(&pbar[0], part_bytes<BN>());  // S slots of 128/S rows
+    if (QB)
+      for (int s = 0; s < STAGES; s++) {
+        mbar_init(&pfull[s], 1);
+        mbar_init(&conv[s], EPI_WARPS);
+      }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -601,10 +721,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
   // stages (whose barriers then expect the activation block as well) and the
   // rest of its K range into L2.
   int pre = 0;
-  int issued[STAGES];
-  uint32_t iss_phase[STAGES];
-  for (int s = 0; s < STAGES; s++) issued[s] = 0, iss_phase[s] = 0;
-  if (warp == 0 && lane == 0 && args.ep.w_static && (int)blockIdx.x < args.ntiles * S) {
+  int issued[STAGES], pk_issued[STAGES];
+  uint32_t iss_phase[STAGES], pk_phase[STAGES];
+  for (int s = 0; s < STAGES; s++) issued[s] = 0, iss_phase[s] = 0, pk_issued[s] = 0, pk_phase[s] = 0;
+  const int pkb = QB ? BK * args.q.bits / 8 : 0;  // packed bytes per row of a block
+  if (QB && warp == 0 && lane == 0 && (int)blockIdx.x < args.ntiles * S) {
+    const int w = blockIdx.x, t = w / S, kb0 = (w % S) * KB / S, kb1 = (w % S + 1) * KB / S;
+    const int n0 = (t % args.ntile_n) * BN;
+    for (int kb = kb0; kb < kb1 && pre < STAGES; kb++) {
+      mbar_arrive_expect_tx(&pfull[pre], (uint32_t)(BN * pkb));
+      tma_load_2d(sPk + pre * PK_BYTES, &tmB, &pfull[pre], kb * pkb, n0);
+      pk_issued[pre++] = 1;
+    }
+  } else if (!QB && warp == 0 && lane == 0 && args.ep.w_static && (int)blockIdx.x < args.ntiles * S) {
     const int w = blockIdx.x, t = w / S, kb0 = (w % S) * KB / S, kb1 = (w % S + 1) * KB / S;
     const int n0 = (t % args.ntile_n) * BN;
     for (int kb = kb0; kb < kb1; kb++) {
@@ -617,11 +746,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       }
     }
   }
-  pdl_wait();  // the kernel that wrote the activations has completed
+  if (!QB) pdl_wait();  // the kernel that wrote the activations has completed
 
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
+      if (QB) pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -630,7 +760,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
         const int t = w / S, kb0 = (w % S) * KB / S, kb1 = (w % S + 1) * KB / S;
         int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
         for (int kb = kb0; kb < kb1; kb++, it++) {
-          if (it < pre) {
+          if (QB) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], A_BYTES);
+            tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, m0);
+            if (it >= pre) {
+              mbar_arrive_expect_tx(&pfull[stage], (uint32_t)(BN * pkb));
+              tma_load_2d(sPk + stage * PK_BYTES, &tmB, &pfull[stage], kb * pkb, n0);
+              pk_issued[stage] = 1;
+              pk_phase[stage] = phase;
+            }
+          } else if (it < pre) {
             tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, m0);
           } else {
             if (!mbar_wait(&empty[stage], phase ^ 1, abort, &g_gemm_err)) { ok = false; break; }
@@ -644,11 +784,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
         }
       }
       // drain: every copy this thread issued must have landed before the CTA exits
-      for (int s = 0; s < STAGES; s++)
+      for (int s = 0; s < STAGES; s++) {
         if (issued[s]) {
           uint64_t t0 = gtimer();
           while (!mbar_try_wait(&full[s], iss_phase[s]) && gtimer() - t0 < kWaitNs) {}
         }
+        if (QB && pk_issued[s]) {
+          uint64_t t0 = gtimer();
+          while (!mbar_try_wait(&pfull[s], pk_phase[s]) && gtimer() - t0 < kWaitNs) {}
+        }
+      }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
@@ -669,6 +814,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
         const uint32_t d = tmem + (uint32_t)(acc * BN);
         for (int kb = kb0; kb < kb1; kb++) {
           if (!mbar_wait(&full[stage], phase, abort, &g_gemm_err)) { ok = false; break; }
+          if (QB && !mbar_wait(&conv[stage], phase, abort, &g_gemm_err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * A_BYTES), b0 = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
@@ -691,6 +837,26 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       }
     }
   } else if constexpr (TMAE) {
+    if constexpr (QB) {  // dequantise the packed blocks as they land, then wait for the predecessor
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < args.ntiles * S && ok; w += gridDim.x) {
+        const int t = w / S, kb0 = (w % S) * KB / S, kb1 = (w % S + 1) * KB / S;
+        const int n0 = (t % args.ntile_n) * BN;
+        for (int kb = kb0; kb < kb1; kb++) {
+          float2 sbv[conv_tasks<BN>()];
+          load_packed_scales<BN>(args, n0, kb, (int)threadIdx.x - 64, sbv);  // in flight while the block lands
+          if (!mbar_wait(&pfull[stage], phase, abort, &g_gemm_err)) { ok = false; break; }
+          convert_packed_block<T, BN>(args, sPk + stage * PK_BYTES, sB + stage * B_BYTES, n0, kb, (int)threadIdx.x - 64, sbv);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      pdl_wait();  // the kernel that wrote the activations and the residual has completed
+    }
     epilogue_tma<T, BN, false, EPI_WARPS, 1, KS>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x / S,
                                                  gridDim.x / S, BM, 0, sP, (float*)sA, pbar);
   } else {
@@ -976,6 +1142,24 @@ const CUtensorMap& tensor_map(const void* ptr, int64_t rows, int64_t cols, int64
   LC_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return c.emplace(key, m).first->second;
 }
+// Bytes of a row-major [rows, cols] byte matrix (the packed weights), boxes of
+// box_rows x box_cols bytes, no swizzle.
+const CUtensorMap& tensor_map_u8(const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+  MapKey key{(uintptr_t)ptr, rows, cols, cols, box_cols * 1024 + box_rows, -1};
+  auto& c = map_cache();
+  auto it = c.find(key);
+  if (it != c.end()) return it->second;
+  if (c.size() > 8192) c.clear();
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LC_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return c.emplace(key, m).first->second;
+}
 
 template <typename T, int BN, int STAGES, bool TMAE>
 void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr, const GemmArgs& a,
@@ -991,14 +1175,15 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap
   lc::launch_chain(k_gemm_tc<T, BN, STAGES, TMAE>, dim3(grid), dim3(GEMM_THREADS), smem, st, ma, mb, my, mr, a);
 }
 
-// Split K: clusters of a.ksplit CTAs, one cluster per tile while they fit.
-template <typename T, int BN, int STAGES>
+// Split K: clusters of a.ksplit CTAs, one cluster per tile while they fit
+// (QB: the packed-weight instance).
+template <typename T, int BN, int STAGES, bool QB = false>
 cudaLaunchConfig_t split_config(int S, cudaLaunchAttribute* at, cudaStream_t st) {
-  constexpr size_t smem = gemm_smem_bytes<STAGES, BN>(true, true);
+  constexpr size_t smem = gemm_smem_bytes<STAGES, BN>(true, true, QB);
   static_assert(smem <= 232448, "GEMM shared memory above the 227 KB per-CTA limit");
   static bool attr = false;
   if (!attr) {
-    CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<T, BN, STAGES, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    CUDA_OK(cudaFuncSetAttribute(k_gemm_tc<T, BN, STAGES, true, true, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -1013,33 +1198,37 @@ cudaLaunchConfig_t split_config(int S, cudaLaunchAttribute* at, cudaStream_t st)
   return cfg;
 }
 // clusters of S of this instance that can be resident at once
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool QB = false>
 int split_capacity(int S) {
   static int cap[5] = {0, 0, 0, 0, 0};
   if (!cap[S]) {
     cudaLaunchAttribute at[2];
-    cudaLaunchConfig_t cfg = split_config<T, BN, STAGES>(S, at, nullptr);
+    cudaLaunchConfig_t cfg = split_config<T, BN, STAGES, QB>(S, at, nullptr);
     cfg.gridDim = dim3(S * (lc::num_sms() / S));
     int n = 0;
-    CUDA_OK(cudaOccupancyMaxActiveClusters(&n, k_gemm_tc<T, BN, STAGES, true, true>, &cfg));
+    CUDA_OK(cudaOccupancyMaxActiveClusters(&n, k_gemm_tc<T, BN, STAGES, true, true, QB>, &cfg));
     LC_CHECK(n > 0, "tcgen05 GEMM: no split-K cluster fits");
     cap[S] = n;
   }
   return cap[S];
 }
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool QB = false>
 void launch_gemm_split(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const CUtensorMap& mr, const GemmArgs& a,
                        cudaStream_t st) {
   const int S = a.ksplit;
   LC_CHECK(S == 1 || S == 2 || S == 4, "tcgen05 GEMM: split-K factor must be 1, 2 or 4");
   cudaLaunchAttribute at[2];
-  cudaLaunchConfig_t cfg = split_config<T, BN, STAGES>(S, at, st);
-  const int cap = split_capacity<T, BN, STAGES>(S);
-  LC_CHECK(S == 1 || a.ntiles <= cap, "tcgen05 GEMM: split K needs one resident cluster per tile");
+  cudaLaunchConfig_t cfg = split_config<T, BN, STAGES, QB>(S, at, st);
+  const int cap = split_capacity<T, BN, STAGES, QB>(S);
+  LC_CHECK((S == 1 && !QB) || a.ntiles <= cap, "tcgen05 GEMM: split K needs one resident cluster per tile");
   cfg.gridDim = dim3(S * std::min(a.ntiles, cap));
-  CUDA_OK(cudaLaunchKernelEx(&cfg, k_gemm_tc<T, BN, STAGES, true, true>, ma, mb, my, mr, a));
+  CUDA_OK(cudaLaunchKernelEx(&cfg, k_gemm_tc<T, BN, STAGES, true, true, QB>, ma, mb, my, mr, a));
 }
-int split_capacity_for(int dtype, int BN, int S) {
+int split_capacity_for(int dtype, int BN, int S, bool qb = false) {
+  if (qb) {
+    if (dtype == LC_F16) return BN == 64 ? split_capacity<__half, 64, 4, true>(S) : split_capacity<__half, 128, 3, true>(S);
+    return BN == 64 ? split_capacity<__nv_bfloat16, 64, 4, true>(S) : split_capacity<__nv_bfloat16, 128, 3, true>(S);
+  }
   if (dtype == LC_F16) return BN == 64 ? split_capacity<__half, 64, 4>(S) : split_capacity<__half, 128, 3>(S);
   return BN == 64 ? split_capacity<__nv_bfloat16, 64, 4>(S) : split_capacity<__nv_bfloat16, 128, 3>(S);
 }
@@ -1191,6 +1380,79 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
       if (BN == 256) launch_gemm<__nv_bfloat16, 256, 4, false>(ma, mb, ma, ma, a, st);
       else launch_gemm<__nv_bfloat16, 128, 6, false>(ma, mb, ma, ma, a, st);
     }
+  }
+  LC_LAUNCHED(1);
+  return true;
+}
+
+// In-kernel dequantisation for few rows; LAYA_CUDA_QGEMM_FUSED=0 makes
+// gemm_raw_q decline (the caller then dequantises into a dense scratch).
+bool gemm_use_qfused() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("LAYA_CUDA_QGEMM_FUSED");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+bool gemm_raw_q(const void* x, int64_t M, int64_t K, const GemmQuantB& q, int64_t N, const void* bias, int bias_dtype, void* y,
+                int64_t ldy, int dtype, const GemmEpilogue& ep, cudaStream_t st) {
+  if (!gemm_use_qfused()) return false;
+  if (!(dtype == LC_F16 || dtype == LC_BF16)) return false;
+  if (!(q.bits == 4 || q.bits == 8) || q.group < 8 || q.group % 8 || !q.w || !q.scales) return false;
+  if (M <= 0 || N <= 0 || K < BK || K % 8) return false;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
+  const int64_t rowb = K * q.bits / 8;  // packed bytes per weight row
+  if (rowb % 16 || (((uintptr_t)q.w | (uintptr_t)x | (uintptr_t)q.gamma) & 15)) return false;
+  const bool geglu = ep.kind == EPI_GEGLU;
+  const int64_t Nacc = geglu ? 2 * N : N;
+  if (ep.kind == EPI_ROPE_QKV && (ep.rope_cols % 64)) return false;
+  if (ep.stats_out && (ep.kind != EPI_RESIDUAL || N % 64)) return false;
+  if (ep.ln_stats && (Nacc % 64 || ((uintptr_t)ep.ln_wsum & 15) || ep.ln_parts < 1 || ep.ln_parts > LN_MAX_PARTS ||
+                      (int64_t)ep.ln_parts * ep.ln_part_cols < K || ep.ln_cols != K))
+    return false;
+  const bool vec_ok = ldy % 8 == 0 && ((uintptr_t)y & 15) == 0 && (ep.kind != EPI_RESIDUAL || (ep.ldr % 8 == 0 && ((uintptr_t)ep.resid & 15) == 0));
+  if (!vec_ok || N % 8 || (ep.kind == EPI_RESIDUAL && !ep.resid)) return false;
+  // few rows only: the natural tiles would fill at most a quarter of the SMs
+  const int sms = lc::num_sms();
+  const int64_t mt = (M + BM - 1) / BM;
+  const int BN0 = gemm_tile_n(Nacc, geglu);
+  if (mt * ((Nacc + BN0 - 1) / BN0) * 4 > sms) return false;
+  const int BNs = geglu ? 128 : 64;
+  const int64_t nt = (Nacc + BNs - 1) / BNs;
+  const int KB = (int)((K + BK - 1) / BK);
+  int S = 0;
+  for (int c : {4, 2, 1})
+    if (mt * nt * c <= sms && KB >= c && mt * nt <= split_capacity_for(dtype, BNs, c, true)) {
+      S = c;
+      break;
+    }
+  if (!S) return false;
+  GemmArgs a{};
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.ntile_n = (int)nt;
+  a.ntiles = (int)(mt * nt);
+  a.y = y;
+  a.ldy = ldy;
+  a.vec_ok = 1;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.ep = ep;
+  a.ksplit = S;
+  a.q = q;
+  const CUtensorMap& ma = tensor_map(x, M, K, K, BK, BM, dtype);
+  const CUtensorMap& mb = tensor_map_u8(q.w, Nacc, rowb, BK * q.bits / 8, BNs);
+  const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
+  const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
+  if (dtype == LC_F16) {
+    if (BNs == 64) launch_gemm_split<__half, 64, 4, true>(ma, mb, my, mr, a, st);
+    else launch_gemm_split<__half, 128, 3, true>(ma, mb, my, mr, a, st);
+  } else {
+    if (BNs == 64) launch_gemm_split<__nv_bfloat16, 64, 4, true>(ma, mb, my, mr, a, st);
+    else launch_gemm_split<__nv_bfloat16, 128, 3, true>(ma, mb, my, mr, a, st);
   }
   LC_LAUNCHED(1);
   return true;

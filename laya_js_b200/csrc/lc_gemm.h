@@ -35,6 +35,16 @@ struct GemmEpilogue {
   bool w_static = false;
 };
 
+// A weight in the native packed 4/8-bit layout (packages/tensor-backend/src/index.ts:98-108)
+// for gemm_raw_q: rows of K·bits/8 bytes, scales / biases [N, ceil(K/g)].
+struct GemmQuantB {
+  const uint8_t* w = nullptr;
+  const void* scales = nullptr;
+  const void* biases = nullptr;  // null for symmetric weights
+  int sdt = 0, bits = 0, group = 0, mode = 0;
+  const float* gamma = nullptr;  // optional column scale [K] (a folded LayerNorm weight)
+};
+
 namespace lc {
 // y[M, N] = x[M, K] · w[N, K]ᵀ (+ bias) with the tcgen05 kernel. Returns false
 // (and does nothing) when the shapes/dtypes/alignment do not fit the kernel.
@@ -42,6 +52,13 @@ bool gemm_linear(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, Lc
 // Raw-pointer form used by the fused encoder: all dense row-major, dtype f16/bf16.
 bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, const void* bias, int bias_dtype, void* y, int64_t ldy,
               int dtype, const GemmEpilogue& ep, cudaStream_t st);
+// The same product with the weight dequantised inside the GEMM (the packed
+// tile is loaded by TMA and turned into the MMA's 16-bit operand in shared
+// memory, bit-identical to dequantising into a dense matrix first). Taken for
+// few rows (one prompt, small batches), where the weight stream dominates;
+// returns false (nothing launched) otherwise.
+bool gemm_raw_q(const void* x, int64_t M, int64_t K, const GemmQuantB& q, int64_t N, const void* bias, int bias_dtype, void* y,
+                int64_t ldy, int dtype, const GemmEpilogue& ep, cudaStream_t st);
 // N-tile width gemm_raw uses for an accumulator of Nacc columns.
 int gemm_tile_n(int64_t Nacc, bool geglu);
 // Row statistics of a residual GEMM (GemmEpilogue::stats_out) come in parts of

@@ -225,6 +225,21 @@ int lc_quantized_embedding(lc_tensor* out, lc_tensor wh, lc_tensor sh, lc_tensor
   LC_API_END
 }
 
+// y = x · dequant(w)ᵀ (+ bias) with the dequantisation inside the GEMM, when
+// the shape suits it (few rows); false when nothing was launched.
+static bool fused_q(const LcTensor* x, const QW& q, int bits, int g, int mode, const LcTensor* bias, LcTensor* y, int64_t M) {
+  GemmQuantB qb;
+  qb.w = (const uint8_t*)q.w->data();
+  qb.scales = q.s->data();
+  qb.biases = q.b ? q.b->data() : nullptr;
+  qb.sdt = q.s->dtype;
+  qb.bits = bits;
+  qb.group = g;
+  qb.mode = mode;
+  return gemm_raw_q(x->data(), M, q.K, qb, q.N, bias ? bias->data() : nullptr, bias ? bias->dtype : 0, y->data(), q.N, y->dtype,
+                    GemmEpilogue{}, stream());
+}
+
 int lc_quantized_linear(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor sh, lc_tensor bh, int bits, int g, int mode, lc_tensor biash) {
   LC_API_BEGIN
   QW q = check_q(wh, sh, bh, bits, g, mode, "quantizedLinear");
@@ -246,6 +261,8 @@ int lc_quantized_linear(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor sh
                                                 q.s->dtype, bits, g, mode, q.N, q.K, bias ? bias->data() : nullptr, bias ? bias->dtype : 0,
                                                 y->data(), odt);
       LC_LAUNCHED(1);
+    } else if (is_half(odt) && x->dtype == odt && fused_q(x, q, bits, g, mode, bias, y, M)) {
+      // few rows: dequantised inside the tcgen05 GEMM
     } else {
       // dequantise once into x's dtype (scratch), then the dense GEMM
       LcTensor* wd = alloc(odt, {q.N, q.K});
@@ -320,12 +337,22 @@ extern "C" int lc_quantized_linear_noalloc(void* y, const void* x, int64_t m, in
   LC_CHECK(mode == 1 ? biases != nullptr : biases == nullptr, "quantizedLinearNoalloc: biases are required for affine and not allowed for symmetric");
   LC_CHECK(x && y && w && scales && m > 0, "quantizedLinearNoalloc: null pointer or empty input");
   LC_CHECK(k >= 64 && k % 8 == 0, "quantizedLinearNoalloc: in features must be a multiple of 8, at least 64");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // few rows: dequantised inside the GEMM, no scratch
+  GemmQuantB qb;
+  qb.w = w;
+  qb.scales = scales;
+  qb.biases = biases;
+  qb.sdt = sb_dtype;
+  qb.bits = bits;
+  qb.group = group_size;
+  qb.mode = mode;
+  if (gemm_raw_q(x, m, k, qb, n, bias, bias_dtype, y, n, dtype, GemmEpilogue{}, st)) return 0;
   const size_t need = (size_t)n * (size_t)k * 2;
   LC_CHECK(need <= kNoAllocScratchBytes,
            "quantizedLinearNoalloc: the dequantised weight needs " + std::to_string(need) + " bytes, above the " +
                std::to_string(kNoAllocScratchBytes) + "-byte scratch (out x in <= " + std::to_string(kNoAllocScratchBytes / 2) + ")");
   void* scratch = noalloc_scratch_for_current_device();
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   k_dequant<<<blocks_for(n * k, 256), 256, 0, st>>>(w, (const char*)scales, (const char*)biases, sb_dtype, bits, group_size, mode, n, k,
                                                     (char*)scratch, dtype);
   LC_LAUNCHED(1);

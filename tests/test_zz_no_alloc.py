@@ -67,11 +67,21 @@ def test_noalloc_matches_quantized_linear_on_consecutive_calls():
         assert np.max(np.abs(got - want)) <= tol, f"{M}x{N}x{K} q{bits}: max diff {np.max(np.abs(got - want))}"
 
 
-def test_noalloc_rejects_weights_larger_than_the_scratch():
+def test_noalloc_large_weight_few_rows_needs_no_scratch_many_rows_rejected():
     b = backend()
     rng = np.random.default_rng(1)
-    M, N, K = 4, 4608, 1024  # 4608 * 1024 f16 values = 9 MiB > 8 MiB
+    N, K = 4608, 1024  # 4608 * 1024 f16 values = 9 MiB > the 8 MiB scratch
+    # few rows: the weight is dequantised inside the GEMM, no scratch involved
+    M = 4
     q, x, bias = _case(b, rng, M, N, K, 4)
+    y = b.fromHost(HostTensor("f16", (M, N), np.zeros((M, N), np.float16)))
+    _noalloc(b, y, x, q, bias, M, N, K, 4)
+    # (the allocating entry runs four rows as a GEMV: same values, another summation order)
+    want = to_f32(b.read(b.quantizedLinear(x, q.w, q.scales, q.biases, q, bias)))
+    assert np.abs(to_f32(b.read(y)) - want).max() < 1e-2
+    # many rows: dequantise-first, and the dense weight does not fit the scratch
+    M = 4096
+    x = b.fromHost(HostTensor("f16", (M, K), rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)))
     y = b.fromHost(HostTensor("f16", (M, N), np.zeros((M, N), np.float16)))
     with pytest.raises(LayaCudaError, match="scratch"):
         _noalloc(b, y, x, q, bias, M, N, K, 4)
