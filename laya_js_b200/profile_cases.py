@@ -5,6 +5,8 @@ quick timing. Each case fits in a few GB and ends in seconds.
     python -m laya_js_b200.profile_cases gemm      # one 32768x2304x768 linear (f16)
     python -m laya_js_b200.profile_cases attention # varlen attention, 256 prompts, global + sliding
     python -m laya_js_b200.profile_cases hbm       # the HBM-bound contract ops on ~100-400 MB tensors
+    python -m laya_js_b200.profile_cases prompt    # configs[0]: one 128-token prompt, 22 layers, CUDA-graph replays
+    python -m laya_js_b200.profile_cases prompt_q4 # the same with 4-bit affine g64 weights (fused-dequant GEMMs)
 
 Every case prints one line with its shape and the device time per launch
 (CUDA events on the library stream, after warm-up).
@@ -77,6 +79,39 @@ def case_attention(b) -> str:
     return f"attention T={T}, 12 heads: " + ", ".join(out)
 
 
+def _prompt(b, bits: int) -> str:
+    import statistics
+    cfg_json = WL.BASE
+    W = WL.random_weights(cfg_json, seed=1)
+    enc = loadModernBert(b, parseModernBertConfig(cfg_json), WL.host_getter(W, quant_bits=bits, group=64), "f16")
+    fused = FusedEncoder(enc)
+    hw, hb = WL.classifier(cfg_json, 3, seed=7)
+    thw = b.fromHost(HostTensor("f16", hw.shape, hw))
+    thb = b.fromHost(HostTensor("f32", hb.shape, hb))
+    ids, cu = WL.token_batch(cfg_json, np.array([128]), seed=5)
+    out = np.empty((1, 3), np.float32)
+    g = fused.graph(cu, thw, thb)
+    for _ in range(3):
+        g.run(ids, out=out)
+    ts = []
+    for _ in range(20):
+        t0 = time.perf_counter()
+        g.run(ids, out=out)
+        ts.append((time.perf_counter() - t0) * 1e3)
+    g.free()
+    fused.free()
+    enc.dispose()
+    return f"prompt L=128, 22 layers, {'f16' if bits == 0 else f'{bits}-bit'} weights, graph replay: p50 {statistics.median(ts):.3f} ms host to host"
+
+
+def case_prompt(b) -> str:
+    return _prompt(b, 0)
+
+
+def case_prompt_q4(b) -> str:
+    return _prompt(b, 4)
+
+
 def case_hbm(b) -> str:
     """The HBM-bound contract ops on tensors larger than L2, each launch timed
     with its algorithmic bytes (read + write once) -> GB/s."""
@@ -132,7 +167,8 @@ def _event_time(b, fn, reps: int) -> float:
 
 def main(argv) -> None:
     b = createCudaBackend(0)
-    cases = {"encoder": case_encoder, "gemm": case_gemm, "attention": case_attention, "hbm": case_hbm}
+    cases = {"encoder": case_encoder, "gemm": case_gemm, "attention": case_attention, "hbm": case_hbm, "prompt": case_prompt,
+             "prompt_q4": case_prompt_q4}
     for name in argv[1:] or list(cases):
         print(cases[name](b), flush=True)
 
