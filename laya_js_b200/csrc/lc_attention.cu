@@ -247,9 +247,221 @@ __global__ void __launch_bounds__(128) k_flash_varlen(const AttnArgs a) {
   }
 }
 
+// ---- the contract's sdpa (index.ts:230-237) on tensor cores: softmax(q·kᵀ·scale
+// masked by a bool mask)·v with q [B, H, Lq, 64], k / v [B, H, Lk, 64] given by
+// strides (last dimension dense, rows 16-byte aligned: the views ModernBert.layer
+// makes with reshape / transpose / split, packages/modernbert/src/index.ts:342-352),
+// mask any bool tensor broadcast to [B, H, Lq, Lk] (the attentionMasks
+// [B, 1, 1, L] / [B, 1, L, L] of index.ts:240-259) or none. Same tiles and
+// online softmax as k_flash_varlen: one CTA = 64 query rows of one (b, h).
+// A fully masked row gets 0/0, as the generic kernel (the contract leaves it
+// undefined).
+struct SdpaArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const uint8_t* m;     // null: no mask
+  int64_t qs[3], ks[3], vs[3];  // element strides of batch, head, row
+  int64_t ms[4];        // mask strides of batch, head, query, key (0 where broadcast)
+  int H, Lq, Lk;
+  float scale_log2;     // scale * log2(e)
+  void* y;              // [B, H, Lq, 64] dense
+};
+
+// rows [r0, r0+64) of a [len, 64] strided matrix into a swizzled tile (rows past
+// the end repeat the last row; their scores are masked)
+template <typename T>
+__device__ __forceinline__ void load_rows(T* s, const T* base, int r0, int len, int64_t ld) {
+#pragma unroll
+  for (int i = 0; i < (64 * 8) / 128; i++) {
+    const int idx = threadIdx.x + i * 128;
+    const int row = idx >> 3, ch = idx & 7;
+    const int r = min(r0 + row, len - 1);
+    cp_async16(s + swz(row, ch), base + (int64_t)r * ld + ch * 8);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) k_sdpa_flash(const SdpaArgs a) {
+  __shared__ __align__(128) T sQ[QT * HD];
+  __shared__ __align__(128) T sK[2][KT * HD];
+  __shared__ __align__(128) T sV[2][KT * HD];
+  const int q0 = blockIdx.x * QT;
+  const int bh = blockIdx.y, bi = bh / a.H, h = bh % a.H;
+  const T* Q = (const T*)a.q + bi * a.qs[0] + h * a.qs[1];
+  const T* Kp = (const T*)a.k + bi * a.ks[0] + h * a.ks[1];
+  const T* Vp = (const T*)a.v + bi * a.vs[0] + h * a.vs[1];
+  const uint8_t* Mk = a.m ? a.m + bi * a.ms[0] + h * a.ms[1] : nullptr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int ntiles = (a.Lk + KT - 1) / KT;
+
+  load_rows<T>(sQ, Q, q0, a.Lq, a.qs[2]);
+  load_rows<T>(sK[0], Kp, 0, a.Lk, a.ks[2]);
+  load_rows<T>(sV[0], Vp, 0, a.Lk, a.vs[2]);
+  cp_commit();
+
+  float o[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  uint32_t qa[4][4];
+  const int qrow0 = q0 + warp * 16 + g;  // this thread's two query rows: qrow0, qrow0 + 8
+  const uint8_t* mrow0 = Mk ? Mk + (int64_t)min(qrow0, a.Lq - 1) * a.ms[2] : nullptr;
+  const uint8_t* mrow1 = Mk ? Mk + (int64_t)min(qrow0 + 8, a.Lq - 1) * a.ms[2] : nullptr;
+
+  for (int it = 0; it < ntiles; it++) {
+    const int buf = it & 1;
+    if (it + 1 < ntiles) {
+      load_rows<T>(sK[buf ^ 1], Kp, (it + 1) * KT, a.Lk, a.ks[2]);
+      load_rows<T>(sV[buf ^ 1], Vp, (it + 1) * KT, a.Lk, a.vs[2]);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    if (it == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        int ch = kk * 2 + (lane >> 4);
+        ldm_x4(qa[kk], sQ + swz(row, ch));
+      }
+    }
+    const T* K = sK[buf];
+    const T* V = sV[buf];
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+#pragma unroll
+      for (int jp = 0; jp < 4; jp++) {
+        uint32_t b[4];
+        int key = jp * 16 + (lane & 7) + (lane >> 4) * 8;
+        int ch = kk * 2 + ((lane >> 3) & 1);
+        ldm_x4(b, K + swz(key, ch));
+        Mma<T>::run(s[2 * jp], qa[kk], b[0], b[1]);
+        Mma<T>::run(s[2 * jp + 1], qa[kk], b[2], b[3]);
+      }
+    }
+    const int kbase = it * KT;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int key = kbase + j * 8 + 2 * t4 + (e & 1);
+        bool ok = key < a.Lk;
+        if (ok && Mk) ok = ((e >> 1) ? mrow1 : mrow0)[(int64_t)key * a.ms[3]] != 0;
+        const float v = ok ? s[j][e] * a.scale_log2 : -INFINITY;
+        s[j][e] = v;
+        if (e < 2) mx0 = fmaxf(mx0, v);
+        else mx1 = fmaxf(mx1, v);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float b0 = n0 == -INFINITY ? 0.f : n0, b1 = n1 == -INFINITY ? 0.f : n1;
+    const float c0 = exp2f(m0 - b0), c1 = exp2f(m1 - b1);
+    m0 = n0;
+    m1 = n1;
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      s[j][0] = exp2f(s[j][0] - b0);
+      s[j][1] = exp2f(s[j][1] - b0);
+      s[j][2] = exp2f(s[j][2] - b1);
+      s[j][3] = exp2f(s[j][3] - b1);
+      rs0 += s[j][0] + s[j][1];
+      rs1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * c0 + rs0;
+    l1 = l1 * c1 + rs1;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      o[j][0] *= c0;
+      o[j][1] *= c0;
+      o[j][2] *= c1;
+      o[j][3] *= c1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      uint32_t pa[4];
+      pa[0] = Mma<T>::pack(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = Mma<T>::pack(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = Mma<T>::pack(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = Mma<T>::pack(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < 4; dp++) {
+        uint32_t b[4];
+        int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        int ch = dp * 2 + (lane >> 4);
+        ldm_x4_t(b, V + swz(key, ch));
+        Mma<T>::run(o[2 * dp], pa, b[0], b[1]);
+        Mma<T>::run(o[2 * dp + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float i0 = 1.f / l0, i1 = 1.f / l1;
+  T* out = (T*)a.y + (int64_t)bh * a.Lq * HD;
+  const int r0 = qrow0, r1 = qrow0 + 8;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int col = j * 8 + 2 * t4;
+    if (r0 < a.Lq) *(uint32_t*)(out + (int64_t)r0 * HD + col) = Mma<T>::pack(o[j][0] * i0, o[j][1] * i0);
+    if (r1 < a.Lq) *(uint32_t*)(out + (int64_t)r1 * HD + col) = Mma<T>::pack(o[j][2] * i1, o[j][3] * i1);
+  }
+}
+
 }  // namespace
 
 namespace lc {
+
+// The contract's sdpa on tensor cores when the operands allow it (f16/bf16,
+// head dim 64, dense rows 16-byte aligned, y dense in q's dtype); false
+// (nothing launched) otherwise.
+bool sdpa_flash(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor* y) {
+  if (!is_half(q->dtype) || k->dtype != q->dtype || v->dtype != q->dtype || y->dtype != q->dtype || !y->contiguous()) return false;
+  const int64_t B = q->shape[0], H = q->shape[1], Lq = q->shape[2], Lk = k->shape[2];
+  if (q->shape[3] != HD || v->shape[3] != HD || Lq < 1 || Lk < 1 || B * H > 65535 || Lq > INT32_MAX || Lk > INT32_MAX) return false;
+  for (const LcTensor* t : {q, k, v}) {
+    if (t->strides[3] != 1 || (t->strides[0] % 8) || (t->strides[1] % 8) || (t->strides[2] % 8) || ((uintptr_t)t->data() & 15)) return false;
+  }
+  SdpaArgs a{};
+  a.q = q->data();
+  a.k = k->data();
+  a.v = v->data();
+  for (int i = 0; i < 3; i++) {
+    a.qs[i] = q->strides[i];
+    a.ks[i] = k->strides[i];
+    a.vs[i] = v->strides[i];
+  }
+  if (m) {
+    TV mv = tv_broadcast(m, {B, H, Lq, Lk});
+    a.m = (const uint8_t*)mv.ptr;
+    for (int i = 0; i < 4; i++) a.ms[i] = mv.strides[i];
+  }
+  a.H = (int)H;
+  a.Lq = (int)Lq;
+  a.Lk = (int)Lk;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.y = y->data();
+  dim3 grid((unsigned)((Lq + QT - 1) / QT), (unsigned)(B * H));
+  if (q->dtype == LC_F16) k_sdpa_flash<__half><<<grid, 128, 0, stream()>>>(a);
+  else k_sdpa_flash<__nv_bfloat16><<<grid, 128, 0, stream()>>>(a);
+  LC_LAUNCHED(1);
+  return true;
+}
 
 // Tile list for cu_seqlens (host): one entry per 64-row query tile of each sequence.
 std::vector<int4> attention_tiles(const int32_t* cu, int nseq) {

@@ -66,6 +66,9 @@ int gemm_tile_n(int64_t Nacc, bool geglu);
 int gemm_stats_part_cols(int64_t N);
 void linear_simt(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, LcTensor* y);
 const float* rope_table(int D, double base, int L, int* cap_out, bool position_minor = false);
+// The contract's sdpa on tensor cores (lc_attention.cu) when q/k/v/y suit it;
+// false, with nothing launched, otherwise.
+bool sdpa_flash(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor* y);
 // Reads and clears the device-side error words of the pipelined kernels.
 std::string take_device_errors();
 std::string take_attention_errors();

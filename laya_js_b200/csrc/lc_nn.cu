@@ -682,6 +682,10 @@ int lc_sdpa(lc_tensor* out, lc_tensor qh, lc_tensor kh, lc_tensor vh, lc_tensor 
   if (B * H * Lq && Dv) {
     TV mv{};
     if (m) mv = tv_broadcast(m, {B, H, Lq, Lk});
+    if (lc::sdpa_flash(q, k, v, m, (float)scale, y)) {
+      *out = handle(y);
+      return 0;
+    }
     LC_CHECK(D <= SDPA_MAXD && Dv <= SDPA_MAXD, "sdpa: head dim above 256 is not supported");
     unsigned blocks = (unsigned)((B * H * Lq + 3) / 4);
     k_sdpa_generic<<<blocks, 128, 0, stream()>>>(tv(q), tv(k), tv(v), mv, m ? 1 : 0, (float)scale, y->data(), odt, B, H, Lq, Lk,

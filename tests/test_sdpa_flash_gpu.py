@@ -1,0 +1,78 @@
+"""The contract's sdpa (index.ts:230-237) on its tensor-core path — f16/bf16,
+head dim 64 — against the oracle: no mask, the attentionMasks padding
+[B,1,1,L] and sliding [B,1,L,L] masks (packages/modernbert/src/index.ts:240-259),
+an arbitrary [B,H,Lq,Lk] mask, Lq != Lk, lengths off the 64-row tiles, and q/k/v
+as the strided views ModernBert.layer makes (reshape -> transpose -> split of the
+QKV projection) rather than dense tensors."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from gpu_util import backend
+from laya_js_b200.host import HostTensor, bf16_bits_to_f32, f32_to_bf16_bits, to_f32
+from oracle import models as M
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"f16": 4e-3, "bf16": 3e-2}
+
+
+def _up(b, a, dt):
+    a = np.asarray(a, np.float32)
+    if dt == "f16":
+        return b.fromHost(HostTensor("f16", a.shape, a.astype(np.float16))), a.astype(np.float16).astype(np.float32)
+    r = bf16_bits_to_f32(f32_to_bf16_bits(a))
+    return b.fromHost(HostTensor("bf16", a.shape, f32_to_bf16_bits(a))), r
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("mask_kind", ["none", "padding", "sliding", "random"])
+def test_sdpa_tensor_core_path(dt, mask_kind):
+    b = backend()
+    rng = np.random.default_rng(11)
+    B, H, L = 3, 4, 130
+    q, qr = _up(b, rng.standard_normal((B, H, L, 64)), dt)
+    k, kr = _up(b, rng.standard_normal((B, H, L, 64)), dt)
+    v, vr = _up(b, rng.standard_normal((B, H, L, 64)), dt)
+    valid = np.ones((B, L), bool)
+    valid[1, 77:] = False
+    valid[2, 5:] = False
+    mask = None
+    if mask_kind == "padding":
+        mask = M.attention_masks(valid, 128)[0]
+    elif mask_kind == "sliding":
+        mask = M.attention_masks(valid, 128)[1]
+    elif mask_kind == "random":
+        mask = rng.random((B, H, L, L)) < 0.7
+        mask[..., 0] = True  # no fully masked row (undefined in the contract)
+    tm = b.fromHost(HostTensor("bool", mask.shape, mask.astype(np.uint8))) if mask is not None else None
+    got = to_f32(b.read(b.sdpa(q, k, v, tm, 0.125)))
+    want = O.sdpa(qr, kr, vr, mask, 0.125)
+    err = np.abs(got - want).max()
+    assert err < TOL[dt], f"{dt} {mask_kind}: max err {err}"
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_sdpa_strided_views_and_unequal_lengths(dt):
+    b = backend()
+    rng = np.random.default_rng(12)
+    B, L, nh = 2, 300, 3
+    # the QKV projection as ModernBert.layer views it: [B, L, 3, nh, 64] -> [3, B, nh, L, 64] -> split
+    qkv, qkvr = _up(b, rng.standard_normal((B, L, 3 * nh * 64)), dt)
+    t = b.transpose(b.reshape(qkv, [B, L, 3, nh, 64]), [2, 0, 3, 1, 4])
+    q, k, v = [b.reshape(x, [B, nh, L, 64]) for x in b.split(t, 3, 0)]
+    valid = np.ones((B, L), bool)
+    valid[0, 200:] = False
+    full, sliding = M.attention_masks(valid, 128)
+    r = qkvr.reshape(B, L, 3, nh, 64).transpose(2, 0, 3, 1, 4)
+    for mask in (full, sliding):
+        got = to_f32(b.read(b.sdpa(q, k, v, b.fromHost(HostTensor("bool", mask.shape, mask.astype(np.uint8))), 0.125)))
+        want = O.sdpa(r[0], r[1], r[2], mask, 0.125)
+        assert np.abs(got - want).max() < TOL[dt]
+    # fewer queries than keys (a slice of q's rows)
+    qs = b.slice(q, [0, 0, 10, 0], [B, nh, 75, 64])
+    got = to_f32(b.read(b.sdpa(qs, k, v, None, 0.125)))
+    want = O.sdpa(r[0][:, :, 10:75], r[1], r[2], None, 0.125)
+    assert np.abs(got - want).max() < TOL[dt]
