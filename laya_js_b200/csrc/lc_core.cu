@@ -241,6 +241,21 @@ __global__ void k_copy_raw(TV src, U* dst, int64_t n) {
   LC_GRID_STRIDE(i, n) { dst[i] = ((const U*)src.ptr)[tv_offset(src, i)]; }
 }
 
+// Same-dtype strided copy whose innermost dimension is dense and spans whole
+// 16-byte vectors (every row start 16-byte aligned): one 16-byte load and
+// store per thread step, the row offset computed once per vector.
+__global__ void k_copy_vec16(TV src, uint4* __restrict__ dst, int64_t nvec, int vpr, int epv) {
+  LC_GRID_STRIDE(i, nvec) {
+    int64_t row = i / vpr, off = 0;
+    const int c = (int)(i % vpr);
+    for (int d = src.ndim - 2; d >= 0; d--) {
+      off += (row % src.shape[d]) * src.strides[d];
+      row /= src.shape[d];
+    }
+    dst[i] = *(const uint4*)(src.ptr + (off + (int64_t)c * epv) * (16 / epv));
+  }
+}
+
 namespace lc {
 // Compute type of a dtype conversion a -> b: 0 float, 1 int64, 2 double, 3 uint64.
 static int ct_for(int a, int b) {
@@ -261,6 +276,17 @@ void copy_into(const LcTensor* src, LcTensor* dst) {
   if (src->dtype == dst->dtype) {
     if (src->contiguous()) {
       CUDA_OK(cudaMemcpyAsync(dst->data(), src->data(), n * dtype_size(src->dtype), cudaMemcpyDeviceToDevice, st));
+      return;
+    }
+    const int es = (int)dtype_size(src->dtype), epv = 16 / es;
+    bool vec = src->ndim >= 1 && es <= 16 && src->strides[src->ndim - 1] == 1 && src->shape[src->ndim - 1] % epv == 0 &&
+               (((uintptr_t)src->data() | (uintptr_t)dst->data()) & 15) == 0;
+    for (int d = 0; vec && d < src->ndim - 1; d++) vec = (src->strides[d] * es) % 16 == 0;
+    if (vec) {
+      const int vpr = (int)(src->shape[src->ndim - 1] / epv);
+      const int64_t nvec = n / epv;
+      k_copy_vec16<<<blocks_for(nvec, threads), threads, 0, st>>>(s, (uint4*)dst->data(), nvec, vpr, epv);
+      LC_LAUNCHED(1);
       return;
     }
     switch (dtype_size(src->dtype)) {

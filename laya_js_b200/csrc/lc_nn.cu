@@ -199,6 +199,56 @@ __global__ void k_rope(TV x, const float* __restrict__ cs, int64_t rows, int64_t
   }
 }
 
+// Vectorised path: last dimension dense, half a multiple of 4, rows 4-element
+// aligned. One thread per 4 pairs (i, i + half): two 4-element loads, the
+// cos / sin quads of the position, two 4-element stores; 32-bit index math.
+template <typename T>
+__global__ void __launch_bounds__(256) k_rope_vec(TV x, const float* __restrict__ cs, int rows, int L, int half, int cap, T* __restrict__ out) {
+  const int qpr = half / 4;
+  const int64_t n = (int64_t)rows * qpr;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(t / qpr), i = (int)(t % qpr) * 4;
+    const int l = r % L;
+    int64_t off = 0;
+    int rr = r;
+    for (int d = x.ndim - 2; d >= 0; d--) {
+      const int sh = (int)x.shape[d];
+      off += (int64_t)(rr % sh) * x.strides[d];
+      rr /= sh;
+    }
+    const T* p = (const T*)x.ptr + off + i;
+    float a[4], b[4];
+    if constexpr (sizeof(T) == 4) {
+      const float4 va = *(const float4*)p, vb = *(const float4*)(p + half);
+      a[0] = va.x, a[1] = va.y, a[2] = va.z, a[3] = va.w;
+      b[0] = vb.x, b[1] = vb.y, b[2] = vb.z, b[3] = vb.w;
+    } else {
+      const uint2 ua = *(const uint2*)p, ub = *(const uint2*)(p + half);
+      const T* ha = (const T*)&ua;
+      const T* hb = (const T*)&ub;
+#pragma unroll
+      for (int j = 0; j < 4; j++) a[j] = to_f(ha[j]), b[j] = to_f(hb[j]);
+    }
+    const float4 c = __ldg((const float4*)(cs + (int64_t)l * half + i));
+    const float4 sn = __ldg((const float4*)(cs + (int64_t)cap * half + (int64_t)l * half + i));
+    const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+    T* o = out + (int64_t)r * 2 * half + i;
+    T ya[4], yb[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      ya[j] = from_f<T>(a[j] * cc[j] - b[j] * ss[j]);
+      yb[j] = from_f<T>(b[j] * cc[j] + a[j] * ss[j]);
+    }
+    if constexpr (sizeof(T) == 4) {
+      *(float4*)o = *(const float4*)ya;
+      *(float4*)(o + half) = *(const float4*)yb;
+    } else {
+      *(uint2*)o = *(const uint2*)ya;
+      *(uint2*)(o + half) = *(const uint2*)yb;
+    }
+  }
+}
+
 namespace {
 struct RopeTable {
   float* d = nullptr;
@@ -656,6 +706,17 @@ int lc_rope(lc_tensor* out, lc_tensor xh, double base) {
       v = tv(f);
       k_rope<<<blocks_for(rows * (D / 2), 256), 256, 0, stream()>>>(v, cs, rows, L, (int)(D / 2), cap, y->data());
       release(f);
+    } else if ((D / 2) % 4 == 0 && x->strides[x->ndim - 1] == 1 && rows < INT32_MAX && L < INT32_MAX && x->ndim <= 5 &&
+               (odt == LC_F32 || odt == LC_F16 || odt == LC_BF16) && ((uintptr_t)x->data() % (4 * dtype_size(odt))) == 0 &&
+               [&] {
+                 for (int d = 0; d < x->ndim - 1; d++)
+                   if (x->strides[d] % 4 || x->shape[d] >= INT32_MAX) return false;
+                 return true;
+               }()) {
+      const unsigned blocks = blocks_for(rows * (D / 8), 256);
+      if (odt == LC_F32) k_rope_vec<float><<<blocks, 256, 0, stream()>>>(v, cs, (int)rows, (int)L, (int)(D / 2), cap, (float*)y->data());
+      else if (odt == LC_F16) k_rope_vec<__half><<<blocks, 256, 0, stream()>>>(v, cs, (int)rows, (int)L, (int)(D / 2), cap, (__half*)y->data());
+      else k_rope_vec<__nv_bfloat16><<<blocks, 256, 0, stream()>>>(v, cs, (int)rows, (int)L, (int)(D / 2), cap, (__nv_bfloat16*)y->data());
     } else {
       k_rope<<<blocks_for(rows * (D / 2), 256), 256, 0, stream()>>>(v, cs, rows, L, (int)(D / 2), cap, y->data());
     }

@@ -119,15 +119,6 @@ __global__ void k_softmax_cols(const char* x, int dtype, char* out, int out_dtyp
 // (16-byte loads, each element read once): the fast paths of softmax and of
 // sum / mean / max / min over the last axis. n % (16 / sizeof(T)) == 0 and
 // n <= 32 * (16 / sizeof(T)) * MAXV.
-template <typename T> __device__ __forceinline__ float to_f(T v);
-template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
-template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
-template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
-template <typename T> __device__ __forceinline__ T from_f(float v);
-template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
-template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
-template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
-
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int n) {
   constexpr int VEC = 16 / sizeof(T);
