@@ -150,27 +150,47 @@ __device__ __forceinline__ void ln_apply(const GemmEpilogue& ep, int col, float 
     b[q * 4 + 3] = r * fmaf(-mu, w.w, b[q * 4 + 3]);
   }
 }
+// a pair rounded to the stored 16-bit type and back (one packed conversion)
+template <typename T>
+__device__ __forceinline__ float2 round_pair(float x, float y) {
+  if constexpr (std::is_same<T, __half>::value) return __half22float2(__floats2half2_rn(x, y));
+  else return __bfloat1622float2(__floats2bfloat162_rn(x, y));
+}
+// two packed 16-bit values as floats
+template <typename T>
+__device__ __forceinline__ float2 unpack_pair(uint32_t u) {
+  if constexpr (std::is_same<T, __half>::value) return __half22float2(*(const __half2*)&u);
+  else return __bfloat1622float2(*(const __nv_bfloat162*)&u);
+}
 // Producer side: round the 64 outputs of a unit to the stored type (so the
 // statistics describe the tensor the next layer reads) and return their
-// (mean, M2).
+// (mean, M2), summed in four independent chains.
 template <typename T>
 __device__ __forceinline__ float2 stats_unit(float* a, float* b) {
-  float s = 0.f;
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int j = 0; j < 32; j++) {
-    a[j] = TcFmt<T>::back(TcFmt<T>::cvt(a[j]));
-    b[j] = TcFmt<T>::back(TcFmt<T>::cvt(b[j]));
-    s += a[j] + b[j];
+  for (int j = 0; j < 32; j += 2) {
+    const float2 ra = round_pair<T>(a[j], a[j + 1]), rb = round_pair<T>(b[j], b[j + 1]);
+    a[j] = ra.x;
+    a[j + 1] = ra.y;
+    b[j] = rb.x;
+    b[j + 1] = rb.y;
+    s[0] += ra.x;
+    s[1] += ra.y;
+    s[2] += rb.x;
+    s[3] += rb.y;
   }
-  const float mu = s * (1.f / 64.f);
-  float q = 0.f;
+  const float mu = ((s[0] + s[1]) + (s[2] + s[3])) * (1.f / 64.f);
+  float q[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int j = 0; j < 32; j++) {
-    const float d0 = a[j] - mu, d1 = b[j] - mu;
-    q = fmaf(d0, d0, q);
-    q = fmaf(d1, d1, q);
+  for (int j = 0; j < 32; j += 2) {
+    const float d0 = a[j] - mu, d1 = a[j + 1] - mu, d2 = b[j] - mu, d3 = b[j + 1] - mu;
+    q[0] = fmaf(d0, d0, q[0]);
+    q[1] = fmaf(d1, d1, q[1]);
+    q[2] = fmaf(d2, d2, q[2]);
+    q[3] = fmaf(d3, d3, q[3]);
   }
-  return make_float2(mu, q);
+  return make_float2(mu, (q[0] + q[1]) + (q[2] + q[3]));
 }
 
 // store 32 consecutive values v[0..31] at columns [col, col+32) of row `row`, valid columns < ncols
@@ -578,11 +598,10 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
 #pragma unroll
           for (int c = 0; c < 8; c++) {
             uint4 v = *(const uint4*)(stg + lane * 128 + ((c ^ (lane & 7)) << 4));
-            const T* h = (const T*)&v;
+            const uint32_t* hw = (const uint32_t*)&v;
             float2* dst = c < 4 ? a + c * 4 : b + (c - 4) * 4;
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-              dst[j] = add2(dst[j], make_float2(TcFmt<T>::back(h[2 * j]), TcFmt<T>::back(h[2 * j + 1])));
+            for (int j = 0; j < 4; j++) dst[j] = add2(dst[j], unpack_pair<T>(hw[j]));
           }
           if (ep.stats_out && live) ep.stats_out[(int64_t)row * nparts + col / 64] = stats_unit<T>((float*)a, (float*)b);
         }
