@@ -319,23 +319,32 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
 #pragma unroll
         for (int c = 0; c < TK / 32; c++) {
           const int c0 = c * 32, c1 = c0 + 31;
-          live[c] = warp_live && __any_sync(0xffffffffu, c1 >= lo && c0 <= hi);
-          full[c] = __all_sync(0xffffffffu, c0 >= lo && c1 <= hi);
+          if (LOCAL) {
+            live[c] = warp_live && __any_sync(0xffffffffu, c1 >= lo && c0 <= hi);
+            full[c] = __all_sync(0xffffffffu, c0 >= lo && c1 <= hi);
+          } else {  // every row sees keys [0, L): lo <= 0 and hi are the same for the whole warp
+            live[c] = warp_live && c0 <= hi;
+            full[c] = c1 <= hi;
+          }
+        }
+        // per chunk, this row's visible keys as a bit mask (bit i = key c·32 + i of the block)
+        uint32_t vis[TK / 32];
+#pragma unroll
+        for (int c = 0; c < TK / 32; c++) {
+          const int a0 = max(lo - c * 32, 0), a1 = min(hi - c * 32, 31);
+          vis[c] = a0 <= a1 ? ((0xffffffffu >> (31 - a1)) & (0xffffffffu << a0)) : 0u;
         }
         float s[TK];
         {
           uint32_t sr[TK];
-#pragma unroll
-          for (int c = 0; c < TK / 32; c++)
-            if (live[c]) tmem_ld32(tmem + lane_off + b * TK + c * 32, sr + c * 32);
-          tmem_wait_ld();  // one wait for every load issued above
+          tmem_ld64(tmem + lane_off + b * TK, sr);
+          tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < TK; i++) s[i] = __uint_as_float(sr[i]);
         }
         // row max of the raw scores (the softmax scale is positive, so it
         // commutes), four independent chains of three-input maxima
         float mc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        const uint32_t span = (uint32_t)(hi - lo);  // k visible <=> (unsigned)(k - lo) <= span (hi >= lo)
 #pragma unroll
         for (int c = 0; c < TK / 32; c++) {
           if (!live[c]) continue;
@@ -346,8 +355,8 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
 #pragma unroll
             for (int i = 0; i < 16; i++) {
               const int k = c * 32 + 2 * i;
-              const float v0 = (hi >= lo && (uint32_t)(k - lo) <= span) ? s[k] : -INFINITY;
-              const float v1 = (hi >= lo && (uint32_t)(k + 1 - lo) <= span) ? s[k + 1] : -INFINITY;
+              const float v0 = (vis[c] >> (2 * i)) & 1u ? s[k] : -INFINITY;
+              const float v1 = (vis[c] >> (2 * i + 1)) & 1u ? s[k + 1] : -INFINITY;
               mc[i & 3] = max3(mc[i & 3], v0, v1);
             }
           }
@@ -361,37 +370,40 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
         if (grow) m = m_new;
         const float nbias = m == -INFINITY ? 0.f : -m * sl;
         float2 acc[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+        uint32_t pr[TK / 2];  // P as 16-bit pairs, packed as the exponentials are computed
 #pragma unroll
         for (int c = 0; c < TK / 32; c++) {
-          if (live[c]) {
+          if (live[c] && full[c]) {
 #pragma unroll
             for (int i = 0; i < 16; i++) {
               const int k = c * 32 + 2 * i;
               float2 x = fma2(make_float2(s[k], s[k + 1]), make_float2(sl, sl), make_float2(nbias, nbias));
               x.x = ex2(x.x);
               x.y = ex2(x.y);
-              if (!full[c]) {  // keys outside the row's range contribute 0
-                x.x = (hi >= lo && (uint32_t)(k - lo) <= span) ? x.x : 0.f;
-                x.y = (hi >= lo && (uint32_t)(k + 1 - lo) <= span) ? x.y : 0.f;
-              }
-              s[k] = x.x;
-              s[k + 1] = x.y;
+              pr[c * 16 + i] = pack2<T>(x.x, x.y);
+              acc[i & 3] = add2(acc[i & 3], x);
+            }
+          } else if (live[c]) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const int k = c * 32 + 2 * i;
+              float2 x = fma2(make_float2(s[k], s[k + 1]), make_float2(sl, sl), make_float2(nbias, nbias));
+              x.x = ex2(x.x);
+              x.y = ex2(x.y);
+              x.x = (vis[c] >> (2 * i)) & 1u ? x.x : 0.f;  // keys outside the row's range contribute 0
+              x.y = (vis[c] >> (2 * i + 1)) & 1u ? x.y : 0.f;
+              pr[c * 16 + i] = pack2<T>(x.x, x.y);
               acc[i & 3] = add2(acc[i & 3], x);
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; i++) s[c * 32 + i] = 0.f;
+            for (int i = 0; i < 16; i++) pr[c * 16 + i] = 0u;
           }
         }
         const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
         const float2 at = add2(a01, a23);
         l = fmaf(l, corr, at.x + at.y);
-        {
-          uint32_t pr[32];
-#pragma unroll
-          for (int i = 0; i < 32; i++) pr[i] = pack2<T>(s[2 * i], s[2 * i + 1]);
-          tmem_st32(tmem + lane_off + b * TK, pr);
-        }
+        tmem_st32(tmem + lane_off + b * TK, pr);
         tmem_wait_st();
         if (j >= 1 && __any_sync(0xffffffffu, grow)) {
           // O holds blocks < j once P_{j-1}·V_{j-1} is done; rescale it before P_j·V_j
@@ -419,20 +431,19 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
       tc_fence_after();
       const float inv = 1.f / l;
       T* out = (T*)a.out + ((int64_t)wk.tok0 + qi) * a.H + wk.h * HD;
-#pragma unroll
-      for (int c = 0; c < HD / 32; c++) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_off + O_COL + c * 32, r);
+      {
+        uint32_t r[HD];
+        tmem_ld64(tmem + lane_off + O_COL, r);
         tmem_wait_ld();
         if (qi < wk.L) {
 #pragma unroll
-          for (int q = 0; q < 4; q++) {
+          for (int q = 0; q < HD / 8; q++) {
             uint4 v;
             uint32_t* pv = (uint32_t*)&v;
 #pragma unroll
             for (int i = 0; i < 4; i++)
               pv[i] = pack2<T>(__uint_as_float(r[q * 8 + 2 * i]) * inv, __uint_as_float(r[q * 8 + 2 * i + 1]) * inv);
-            *(uint4*)(out + c * 32 + q * 8) = v;
+            *(uint4*)(out + q * 8) = v;
           }
         }
       }

@@ -546,16 +546,15 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
           tma_load_2d(stg, &tmR, &rb0[0], col, row0);
         }
       }
-      uint32_t ra[32], rbv[32];
-      tmem_ld32(tbase + u * 64, ra);
-      tmem_ld32(tbase + u * 64 + 32, rbv);
+      uint32_t racc[64];
+      tmem_ld64(tbase + u * 64, racc);
       tmem_wait_ld();
       // a = accumulator columns col..col+31, b = col+32..col+63, as packed pairs
       float2 a[16], b[16];
 #pragma unroll
       for (int j = 0; j < 16; j++) {
-        a[j] = make_float2(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
-        b[j] = make_float2(__uint_as_float(rbv[2 * j]), __uint_as_float(rbv[2 * j + 1]));
+        a[j] = make_float2(__uint_as_float(racc[2 * j]), __uint_as_float(racc[2 * j + 1]));
+        b[j] = make_float2(__uint_as_float(racc[32 + 2 * j]), __uint_as_float(racc[32 + 2 * j + 1]));
       }
       if (ep.ln_stats) {  // r·(acc − μ·wsum); wsum of columns col+2j, col+2j+1 sits in lane j
         const float2 nmu = make_float2(-ln_mu, -ln_mu), r2 = make_float2(ln_r, ln_r);
