@@ -74,7 +74,9 @@ def measured_peaks() -> dict:
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling during the timed region: the sampler is started and
+    its first sample read before the region begins (that sample is dropped),
+    then it samples every 50 ms until the region ends."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -86,7 +88,8 @@ class Clocks:
     def __enter__(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                       "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.p.stdout.readline()  # the sampler is running: this sample precedes the timed region
         except OSError:
             self.p = None
         return self
@@ -103,7 +106,7 @@ class Clocks:
             self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
+        sm, pw, mx, reasons = [], [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for l in getattr(self, "lines", []):
             f = [x.strip() for x in l.split(",")]
@@ -114,10 +117,15 @@ class Clocks:
                 mx = float(f[2])
             except ValueError:
                 continue
+            try:
+                pw.append(float(f[3]))
+            except ValueError:
+                pass
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "power_w": statistics.median(pw) if pw else None}
 
 
 def cpu_baseline(cfg_json: dict, W: dict, ids: np.ndarray, cu: np.ndarray, budget_s: float = 12.0) -> dict:

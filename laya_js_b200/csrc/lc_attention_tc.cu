@@ -17,17 +17,20 @@
 //                                from shared memory, MN-major)
 //               S is double-buffered in TMEM (columns 0-63 / 64-127), so
 //               S_{j+1} runs while the softmax works on S_j, also across work
-//               items; O lives at columns 128-191 (256 columns per CTA).
+//               items; O is double-buffered by work-item parity (columns
+//               128-191 / 192-255; 256 columns per CTA).
 //   warps 2-5   softmax: thread r owns query row r (= TMEM lane r), so the
 //               row max / sum need no cross-thread reduction. It loads S_j,
 //               masks (key in the sequence, |i − j| <= window/2 for sliding
 //               layers), writes P_j = exp2(S·scale·log2e − m) as 16-bit values
 //               packed two per column over the first 32 columns of S_j's
 //               buffer, and — only when the running max grew by more than
-//               2^8 — rescales O in TMEM once P_{j−1}·V_{j−1} is done. At the
-//               end of an item it normalises O by the row sum and stores
-//               [T, H]; the next item's first P_0·V_0 (which overwrites O)
-//               waits for that through the P-ready barrier.
+//               2^8 — rescales O in TMEM once P_{j−1}·V_{j−1} is done. An
+//               item's O is normalised by the row sum and stored to [T, H]
+//               after the next item's first block has been handed over (its
+//               last P·V completes meanwhile); the P·V that next overwrites
+//               that O buffer (two items later) waits for that through the
+//               P-ready barrier.
 // Every barrier counts phases with per-role counters that run across work
 // items; every mbarrier wait is bounded (2 s); a timeout sets g_attn_err and
 // all roles unwind.
@@ -46,9 +49,9 @@ namespace {
 constexpr int TQ = 128, TK = 64, HD = 64;
 constexpr uint32_t TILE_BYTES = TQ * HD * 2;  // the 128 x 64 Q tile
 constexpr uint32_t KV_BYTES = TK * HD * 2;    // one 64 x 64 K or V tile
-constexpr uint32_t TMEM_COLS = 256;           // S double buffer (2 x 64) + O (64): two CTAs fit an SM
+constexpr uint32_t TMEM_COLS = 256;           // S double buffer (2 x 64) + O double buffer (2 x 64): two CTAs fit an SM
 constexpr int NS = 2;                         // S buffers
-constexpr uint32_t O_COL = NS * TK;
+constexpr uint32_t O_COL = NS * TK;           // O of work item t at O_COL + (t & 1) * HD
 constexpr int NST = 4;                        // K/V ring depth
 constexpr size_t ATTN_SMEM = 2 * TILE_BYTES + 2 * NST * KV_BYTES + 1024 + 256;
 
@@ -275,7 +278,7 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
         const uint64_t dv = dv0 + ((st * KV_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < TK / 16; kk++)
-          tc_mma_ts(tmem + O_COL, tmem + b * TK + kk * 8, dv + kk * (2048 >> 4), id_pv, (pj > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_ts(tmem + O_COL + (pi.t & 1) * HD, tmem + b * TK + kk * 8, dv + kk * (2048 >> 4), id_pv, (pj > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&o_done[pg & 1]);
         tc_commit(&kv_empty[st]);
         last_bar = &o_done[pg & 1];
@@ -300,10 +303,40 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
     const float sl = a.scale_log2;
     uint32_t g = 0;
     bool ok = true;
+    // O is double-buffered by work-item parity: a finished item's rows are
+    // normalised and stored after the first block of the next item has been
+    // handed to the MMA warp, so the softmax does not idle while the item's
+    // last P·V completes. The next P·V into that buffer (two items later)
+    // waits for a P-ready arrival that follows this store.
+    bool pend = false;
+    uint32_t pend_gl = 0, pend_ocol = 0;
+    float pend_inv = 0.f;
+    T* pend_out = nullptr;  // null: this row is past its sequence end
+    auto flush = [&]() -> bool {
+      if (!mbar_wait(&o_done[pend_gl & 1], (pend_gl >> 1) & 1, abort, &g_attn_err)) return false;
+      tc_fence_after();
+      uint32_t r[HD];
+      tmem_ld64(tmem + lane_off + pend_ocol, r);
+      tmem_wait_ld();
+      if (pend_out) {
+#pragma unroll
+        for (int q = 0; q < HD / 8; q++) {
+          uint4 v;
+          uint32_t* pv = (uint32_t*)&v;
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            pv[i] = pack2<T>(__uint_as_float(r[q * 8 + 2 * i]) * pend_inv, __uint_as_float(r[q * 8 + 2 * i + 1]) * pend_inv);
+          *(uint4*)(pend_out + q * 8) = v;
+        }
+      }
+      pend = false;
+      return true;
+    };
     Items<LOCAL> it;
     for (it.start(a); ok && it.valid(a); it.step(a)) {
       const Work& wk = it.cur;
       const int qi = wk.q0 + row;
+      const uint32_t ocol = O_COL + (it.t & 1) * HD;
       const bool warp_live = wk.q0 + quarter * 32 < wk.L;  // warps wholly past the sequence end skip their exps
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < wk.nb; j++) {
@@ -413,42 +446,28 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
 #pragma unroll
           for (int c = 0; c < HD / 32; c++) {
             uint32_t r[32];
-            tmem_ld32(tmem + lane_off + O_COL + c * 32, r);
+            tmem_ld32(tmem + lane_off + ocol + c * 32, r);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-            tmem_st32(tmem + lane_off + O_COL + c * 32, r);
+            tmem_st32(tmem + lane_off + ocol + c * 32, r);
           }
           tmem_wait_st();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[b]);
+        if (j == 0 && pend && !flush()) { ok = false; break; }
       }
       if (!ok) break;
-      const uint32_t gl = g + wk.nb - 1;
-      if (!mbar_wait(&o_done[gl & 1], (gl >> 1) & 1, abort, &g_attn_err)) break;
-      tc_fence_after();
-      const float inv = 1.f / l;
-      T* out = (T*)a.out + ((int64_t)wk.tok0 + qi) * a.H + wk.h * HD;
-      {
-        uint32_t r[HD];
-        tmem_ld64(tmem + lane_off + O_COL, r);
-        tmem_wait_ld();
-        if (qi < wk.L) {
-#pragma unroll
-          for (int q = 0; q < HD / 8; q++) {
-            uint4 v;
-            uint32_t* pv = (uint32_t*)&v;
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-              pv[i] = pack2<T>(__uint_as_float(r[q * 8 + 2 * i]) * inv, __uint_as_float(r[q * 8 + 2 * i + 1]) * inv);
-            *(uint4*)(out + q * 8) = v;
-          }
-        }
-      }
+      pend = true;
+      pend_gl = g + wk.nb - 1;
+      pend_ocol = ocol;
+      pend_inv = 1.f / l;
+      pend_out = qi < wk.L ? (T*)a.out + ((int64_t)wk.tok0 + qi) * a.H + wk.h * HD : nullptr;
       g += wk.nb;
     }
+    if (ok && pend) flush();
   }
   tc_fence_before();
   __syncthreads();
