@@ -526,6 +526,19 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
         tmem_wait_st();
       }
     }
+    // The accumulator buffer is handed back to the MMA warp as soon as this
+    // warp has read its last unit into registers (the rest of the epilogue
+    // works from registers and shared memory).
+    bool released = false;
+    auto release = [&]() {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR && row_off != 0) mbar_arrive_cluster(tempty0 + 8 * acc);  // the pair's MMA runs in CTA 0
+        else mbar_arrive(&tempty[acc]);
+      }
+      released = true;
+    };
 #pragma unroll 1
     for (int u = u_lo; u < u_hi; u++) {
       const int col = n0 + u * 64;
@@ -549,6 +562,10 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
       uint32_t racc[64];
       tmem_ld64(tbase + u * 64, racc);
       tmem_wait_ld();
+      // the last unit this warp reads: the loop ends after it, or the next unit (output block) is past the weight rows
+      const bool last_ld = u + 1 >= u_hi ||
+                           (geglu ? ((u & 1) == 0 ? bcol + 64 >= ncols : n0 + ((u + 1) & ~1) * 64 >= ncols) : col + 64 >= ncols);
+      if (last_ld) release();
       // a = accumulator columns col..col+31, b = col+32..col+63, as packed pairs
       float2 a[16], b[16];
 #pragma unroll
@@ -636,12 +653,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
         if (geglu && (u & 1) == 0) break;  // the pair's second unit is past the weight rows
       }
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      if (PAIR && row_off != 0) mbar_arrive_cluster(tempty0 + 8 * acc);  // the pair's MMA runs in CTA 0
-      else mbar_arrive(&tempty[acc]);
-    }
+    if (!released) release();
     if (++acc == 2) { acc = 0; acc_phase ^= 1; }
   }
   if (lane == 0) bulk_wait_all();
