@@ -47,7 +47,7 @@ BATCH, LO, HI, CLASSES = 256, 32, 512, 8
 SEED = 20261201
 # DRAM bytes per GEMM launch of this workload (average over the four projections),
 # from the committed one-pass ncu capture in profiles/gemm_traffic_bench.md
-GEMM_TRAFFIC_BYTES = 307.1e6
+GEMM_TRAFFIC_BYTES = 306.6e6
 
 
 def parse():
