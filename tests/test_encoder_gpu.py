@@ -164,3 +164,32 @@ def test_encoder_graph_replays_forward_host(quant_bits):
     fused.free()
     g2.free()  # no-op after the encoder is gone
     enc.dispose()
+
+
+@pytest.mark.parametrize("half_window", [-1, 64])
+def test_attention_varlen_many_items_per_cta(half_window):
+    """Enough (query tile, head) items that every persistent CTA of the
+    tcgen05 kernel walks several of them: the Q double buffer, the K/V ring
+    running across items and the O buffer of one item stored while the next
+    item runs are all exercised, against the oracle for every sequence."""
+    b = backend()
+    rng = np.random.default_rng(11)
+    H, nh = 768, 12
+    lens = rng.integers(1, 700, size=96)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    items = sum(-(-int(L) // 128) for L in lens) * nh
+    assert items > 8 * 296  # several items per CTA at two CTAs per SM
+    qkv = (rng.standard_normal((T, 3 * H)) * 0.5).astype(np.float16)
+    att = to_f32(b.read(attention_varlen(b, b.fromHost(HostTensor("f16", qkv.shape, qkv)), cu, half_window, 0.125, 0)))
+    worst = 0.0
+    for s, L in enumerate(lens):
+        L = int(L)
+        seg = qkv[cu[s]:cu[s + 1]].astype(np.float32).reshape(L, 3, nh, 64).transpose(1, 2, 0, 3)
+        mask = None
+        if half_window >= 0:
+            i = np.arange(L)
+            mask = (np.abs(i[:, None] - i[None, :]) <= half_window)[None, None]
+        want = O.sdpa(seg[0][None], seg[1][None], seg[2][None], mask, 0.125)[0].transpose(1, 0, 2).reshape(L, H)
+        worst = max(worst, float(np.abs(att[cu[s]:cu[s + 1]] - want).max()))
+    assert worst < 6e-3, f"max err {worst}"
