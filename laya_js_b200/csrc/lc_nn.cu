@@ -417,13 +417,16 @@ __global__ void k_geglu_generic(const char* x, int xdt, char* y, int ydt, int64_
 }
 
 // Dense f16 / bf16 / f32 x with D % (16 / sizeof(T)) == 0: block (b, 32*VEC-column
-// chunk); its 8 warps split the L positions, each lane sums VEC columns from
-// 16-byte loads (the masked-out rows are skipped), then the warps' partial
-// sums and counts combine in shared memory.
+// chunk); its 8 warps take 32-row chunks of the L positions in turn. A warp
+// reads the 32 mask entries of a chunk at once (one per lane, a ballot gives
+// the kept rows), then each lane sums VEC columns of the kept rows from
+// 16-byte loads, eight rows in flight; the warps' partial sums and counts
+// combine in shared memory.
 template <typename T>
 __global__ void __launch_bounds__(256) k_mean_pool_vec(const T* __restrict__ x, const char* mask, int mdt, float* __restrict__ out,
                                                        int64_t L, int64_t D) {
   constexpr int VEC = 16 / sizeof(T);
+  constexpr int UNR = 8;
   __shared__ float part[8][32 * VEC];
   __shared__ float cnt[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -434,14 +437,25 @@ __global__ void __launch_bounds__(256) k_mean_pool_vec(const T* __restrict__ x, 
 #pragma unroll
   for (int j = 0; j < VEC; j++) acc[j] = 0.f;
   float n = 0.f;
-  for (int64_t l = warp; l < L; l += 8) {
-    if (ld_as<int64_t>(mask, mdt, b * L + l) == 0) continue;  // warp-uniform
-    n += 1.f;
-    if (on) {
-      const uint4 raw = *(const uint4*)(x + (b * L + l) * D + c0);
-      const T* e = (const T*)&raw;
+  for (int64_t l0 = (int64_t)warp * 32; l0 < L; l0 += 8 * 32) {
+    const int64_t lr = l0 + lane;
+    const bool keep = lr < L && ld_as<int64_t>(mask, mdt, b * L + lr) != 0;
+    const uint32_t bits = __ballot_sync(0xffffffffu, keep);
+    n += (float)__popc(bits);
+    if (!on) continue;
+#pragma unroll 1
+    for (int i0 = 0; i0 < 32; i0 += UNR) {
+      if (((bits >> i0) & ((1u << UNR) - 1u)) == 0u) continue;  // warp-uniform
+      uint4 raw[UNR];
 #pragma unroll
-      for (int j = 0; j < VEC; j++) acc[j] += ld_as<float>((const char*)e, std::is_same<T, float>::value ? LC_F32 : (std::is_same<T, __half>::value ? LC_F16 : LC_BF16), j);
+      for (int u = 0; u < UNR; u++)
+        raw[u] = (bits >> (i0 + u)) & 1u ? *(const uint4*)(x + (b * L + l0 + i0 + u) * D + c0) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int u = 0; u < UNR; u++) {
+        const T* e = (const T*)&raw[u];
+#pragma unroll
+        for (int j = 0; j < VEC; j++) acc[j] += to_f<T>(e[j]);
+      }
     }
   }
 #pragma unroll

@@ -150,7 +150,10 @@ __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ 
       if (t * 32 + lane < nv)
 #pragma unroll
         for (int j = 0; j < VEC; j++) {
-          v[t][j] = expf(v[t][j] - m);
+          // 16-bit outputs: the hardware exp2 (relative error ~2^-22, far below
+          // the output's 2^-11 rounding); f32 outputs keep the full expf
+          if constexpr (sizeof(T) == 2) v[t][j] = __expf(v[t][j] - m);
+          else v[t][j] = expf(v[t][j] - m);
           s += v[t][j];
         }
 #pragma unroll
@@ -176,15 +179,17 @@ __device__ __forceinline__ float pick(int op, float a, float b) {
   return op == R_MAX ? fmaxf(a, b) : fminf(a, b);
 }
 
-// sum (f32 accumulation), mean (f64), max, min over each row
-template <typename T, int MAXV>
-__global__ void __launch_bounds__(256) k_reduce_rows_vec(const T* __restrict__ x, char* out, int out_dtype, int op, int64_t rows, int n) {
+// sum (f32 accumulation), mean (f64), max, min over each row; the operation
+// is a template parameter so the per-element loop carries no branch on it
+template <typename T, int MAXV, int OP>
+__global__ void __launch_bounds__(256) k_reduce_rows_vec(const T* __restrict__ x, char* out, int out_dtype, int64_t rows, int n) {
   constexpr int VEC = 16 / sizeof(T);
+  constexpr int op = OP;
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int nv = n / VEC;
-  const bool mm = op == R_MAX || op == R_MIN;
+  constexpr bool mm = op == R_MAX || op == R_MIN;
   for (int64_t r = warp; r < rows; r += nwarps) {
     float acc = 0.f, best = op == R_MAX ? -INFINITY : INFINITY;
     double dacc = 0.0;
@@ -197,21 +202,21 @@ __global__ void __launch_bounds__(256) k_reduce_rows_vec(const T* __restrict__ x
 #pragma unroll
         for (int j = 0; j < VEC; j++) {
           const float f = to_f<T>(e[j]);
-          if (mm) best = pick(op, best, f);
-          else if (op == R_MEAN) dacc += (double)f;
+          if constexpr (mm) best = pick(op, best, f);
+          else if constexpr (op == R_MEAN) dacc += (double)f;
           else acc += f;
         }
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      if (mm) best = pick(op, best, __shfl_xor_sync(0xffffffffu, best, o));
-      else if (op == R_MEAN) dacc += __shfl_xor_sync(0xffffffffu, dacc, o);
+      if constexpr (mm) best = pick(op, best, __shfl_xor_sync(0xffffffffu, best, o));
+      else if constexpr (op == R_MEAN) dacc += __shfl_xor_sync(0xffffffffu, dacc, o);
       else acc += __shfl_xor_sync(0xffffffffu, acc, o);
     }
     if (lane == 0) {
-      if (mm) st_as<float>(out, out_dtype, r, best);
-      else if (op == R_MEAN) st_as<double>(out, out_dtype, r, dacc / (double)n);
+      if constexpr (mm) st_as<float>(out, out_dtype, r, best);
+      else if constexpr (op == R_MEAN) st_as<double>(out, out_dtype, r, dacc / (double)n);
       else st_as<float>(out, out_dtype, r, acc);
     }
   }
@@ -323,6 +328,25 @@ int row_vec_maxv(int dtype, int64_t n) {
     default: KERNEL<T, 8><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;   \
   }
 
+template <typename T, int MAXV>
+void launch_reduce_vec_op(unsigned blocks, int op, const T* x, char* out, int odt, int64_t rows, int n) {
+  switch (op) {
+    case R_SUM: k_reduce_rows_vec<T, MAXV, R_SUM><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+    case R_MEAN: k_reduce_rows_vec<T, MAXV, R_MEAN><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+    case R_MAX: k_reduce_rows_vec<T, MAXV, R_MAX><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+    default: k_reduce_rows_vec<T, MAXV, R_MIN><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+  }
+}
+template <typename T>
+void launch_reduce_vec(unsigned blocks, int maxv, int op, const T* x, char* out, int odt, int64_t rows, int n) {
+  switch (maxv) {
+    case 1: launch_reduce_vec_op<T, 1>(blocks, op, x, out, odt, rows, n); break;
+    case 2: launch_reduce_vec_op<T, 2>(blocks, op, x, out, odt, rows, n); break;
+    case 4: launch_reduce_vec_op<T, 4>(blocks, op, x, out, odt, rows, n); break;
+    default: launch_reduce_vec_op<T, 8>(blocks, op, x, out, odt, rows, n); break;
+  }
+}
+
 template <typename CT, typename AT>
 void launch_reduce(LcTensor* c, LcTensor* y, int op, Axis3 s) {
   cudaStream_t st = stream();
@@ -357,9 +381,9 @@ LcTensor* reduce(int op, uint64_t xh, int axis, bool keep, const char* name) {
     const unsigned blocks = blocks_for(s.outer * 32, 256);
     const int mv = row_vec_maxv(d, s.n);
     const int n = (int)s.n;
-    if (d == LC_F16) { LC_ROWVEC_DISPATCH(k_reduce_rows_vec, __half, mv, blocks, (const __half*)c->data(), y->data(), y->dtype, op, s.outer, n) }
-    else if (d == LC_BF16) { LC_ROWVEC_DISPATCH(k_reduce_rows_vec, __nv_bfloat16, mv, blocks, (const __nv_bfloat16*)c->data(), y->data(), y->dtype, op, s.outer, n) }
-    else { LC_ROWVEC_DISPATCH(k_reduce_rows_vec, float, mv, blocks, (const float*)c->data(), y->data(), y->dtype, op, s.outer, n) }
+    if (d == LC_F16) launch_reduce_vec<__half>(blocks, mv, op, (const __half*)c->data(), y->data(), y->dtype, s.outer, n);
+    else if (d == LC_BF16) launch_reduce_vec<__nv_bfloat16>(blocks, mv, op, (const __nv_bfloat16*)c->data(), y->data(), y->dtype, s.outer, n);
+    else launch_reduce_vec<float>(blocks, mv, op, (const float*)c->data(), y->data(), y->dtype, s.outer, n);
     LC_LAUNCHED(1);
     if (c != x) release(c);
     return y;

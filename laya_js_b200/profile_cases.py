@@ -127,6 +127,9 @@ def case_hbm(b) -> str:
     B, L = 128, 512
     mask = b.fromHost(HostTensor("i32", (B, L), np.ones((B, L), np.int32)))
     xb = b.reshape(x, [B, L, H])
+    R2, N2 = 16384, 2304  # a configs[1] shape in f32
+    xf = b.fromHost(HostTensor("f32", (R2, N2), rng.standard_normal((R2, N2), dtype=np.float32)))
+    gf = b.fromHost(HostTensor("f32", (N2,), np.ones(N2, np.float32)))
     e = 2
     cases = [
         ("add [65536,768] f16", lambda: b.add(x, y), 3 * R * H * e),
@@ -137,6 +140,11 @@ def case_hbm(b) -> str:
         ("sum rows [65536,768] f16", lambda: b.sum(x, -1), R * H * e),
         ("embedding 65536 ids of [50368,768] f16", lambda: b.embedding(table, ids), 2 * R * H * e),
         ("meanPool [128,512,768] f16", lambda: b.meanPool(xb, mask), R * H * e),
+        ("max rows [65536,768] f16", lambda: b.max(x, -1), R * H * e),
+        ("mul row broadcast [65536,768]*[768] f16", lambda: b.mul(x, g), 2 * R * H * e),
+        ("softmax rows [16384,2304] f32", lambda: b.softmax(xf, -1), 2 * R2 * N2 * 4),
+        ("layerNorm [16384,2304] f32", lambda: b.layerNorm(xf, gf, None, 1e-5), 2 * R2 * N2 * 4),
+        ("sum rows [16384,2304] f32", lambda: b.sum(xf, -1), R2 * N2 * 4),
     ]
     out = []
     for name, fn, nbytes in cases:
