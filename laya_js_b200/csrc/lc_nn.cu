@@ -89,6 +89,91 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
   }
 }
 
+// Rows longer than one warp's register tile: one 256-thread block per row (rows
+// taken in turn by the grid), each thread holding up to MAXV 16-byte vectors;
+// the mean and the centred sum of squares go through warp shuffles and the 8
+// warps' partials in shared memory (read by every thread in the same order).
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) k_layernorm_blk(const T* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                                                       T* __restrict__ y, int64_t rows, int N, float eps) {
+  constexpr int VN = 16 / sizeof(T);
+  __shared__ float sm[8];
+  const int nv = N / VN;
+  auto bsum = [&](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = sm[0];
+#pragma unroll
+    for (int k = 1; k < 8; k++) t += sm[k];
+    __syncthreads();
+    return t;
+  };
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    float v[MAXV][VN];
+    float s = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      const int c = t * 256 + threadIdx.x;
+      if (c < nv) {
+        const uint4 raw = *(const uint4*)(x + r * N + (int64_t)c * VN);
+        const T* e = (const T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VN; j++) {
+          v[t][j] = to_f<T>(e[j]);
+          s += v[t][j];
+        }
+      }
+    }
+    const float mu = bsum(s) / N;
+    float q = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++)
+      if (t * 256 + (int)threadIdx.x < nv)
+#pragma unroll
+        for (int j = 0; j < VN; j++) {
+          const float d = v[t][j] - mu;
+          q += d * d;
+        }
+    const float rs = rsqrtf(bsum(q) / N + eps);
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      const int c = t * 256 + threadIdx.x;
+      if (c < nv) {
+        uint4 raw;
+        T* e = (T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VN; j += 4) {
+          const float4 a4 = w ? __ldg((const float4*)(w + c * VN + j)) : make_float4(1.f, 1.f, 1.f, 1.f);
+          const float4 b4 = b ? __ldg((const float4*)(b + c * VN + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float wv[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const float o = (v[t][j + k] - mu) * rs * wv[k] + bv[k];
+            if constexpr (sizeof(T) == 4) ((float*)e)[j + k] = o;
+            else if constexpr (std::is_same<T, __half>::value) e[j + k] = __float2half_rn(o);
+            else e[j + k] = __float2bfloat16_rn(o);
+          }
+        }
+        *(uint4*)(y + r * N + (int64_t)c * VN) = raw;
+      }
+    }
+  }
+}
+template <typename T>
+void launch_layernorm_blk(const T* x, const float* w, const float* b, T* y, int64_t rows, int N, float eps, cudaStream_t st) {
+  constexpr int VN = 16 / sizeof(T);
+  const int per = (N / VN + 255) / 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>(rows, (int64_t)lc::num_sms() * 8);
+  switch (per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8) {
+    case 1: k_layernorm_blk<T, 1><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 2: k_layernorm_blk<T, 2><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 4: k_layernorm_blk<T, 4><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    default: k_layernorm_blk<T, 8><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+  }
+}
+
 // The register tile is sized to the row (vectors per lane = ceil(N / VN / 32)) so
 // that short rows (H = 768 -> 3 vectors) keep full occupancy.
 template <typename T>
@@ -635,15 +720,20 @@ int lc_layer_norm(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh, doub
     int wdt = w ? w->dtype : 0, bdt = b ? b->dtype : 0;
     unsigned blocks = blocks_for(rows * 32, 256);
     cudaStream_t st = stream();
-    bool aligned = (((uintptr_t)x->data() | (uintptr_t)y->data()) & 15) == 0;
+    bool aligned = (((uintptr_t)x->data() | (uintptr_t)y->data() | (uintptr_t)wp | (uintptr_t)bp) & 15) == 0;
     int vn = x->dtype == LC_F32 ? 4 : 8;
     bool vec = aligned && x->dtype == odt && (odt == LC_F32 || is_half(odt)) && N % vn == 0 && N / vn <= 32 * 8;
+    bool blk = aligned && x->dtype == odt && (odt == LC_F32 || is_half(odt)) && N % vn == 0 && N / vn <= 256 * 8;
     const float* wf = (const float*)wp;
     const float* bf = (const float*)bp;
     if (vec) {
       if (odt == LC_F16) launch_layernorm_vec<__half>((const __half*)x->data(), wf, bf, (__half*)y->data(), rows, (int)N, (float)eps, st);
       else if (odt == LC_BF16) launch_layernorm_vec<__nv_bfloat16>((const __nv_bfloat16*)x->data(), wf, bf, (__nv_bfloat16*)y->data(), rows, (int)N, (float)eps, st);
       else launch_layernorm_vec<float>((const float*)x->data(), wf, bf, (float*)y->data(), rows, (int)N, (float)eps, st);
+    } else if (blk) {
+      if (odt == LC_F16) launch_layernorm_blk<__half>((const __half*)x->data(), wf, bf, (__half*)y->data(), rows, (int)N, (float)eps, st);
+      else if (odt == LC_BF16) launch_layernorm_blk<__nv_bfloat16>((const __nv_bfloat16*)x->data(), wf, bf, (__nv_bfloat16*)y->data(), rows, (int)N, (float)eps, st);
+      else launch_layernorm_blk<float>((const float*)x->data(), wf, bf, (float*)y->data(), rows, (int)N, (float)eps, st);
     } else if (x->dtype == LC_F64) {
       k_layernorm_generic<double><<<blocks, 256, 0, st>>>(x->data(), x->dtype, wp, wdt, bp, bdt, y->data(), odt, rows, N, eps);
     } else {

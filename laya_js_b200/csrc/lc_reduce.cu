@@ -222,6 +222,125 @@ __global__ void __launch_bounds__(256) k_reduce_rows_vec(const T* __restrict__ x
   }
 }
 
+// ---- rows longer than one warp's register tile: one 256-thread block per row
+// (rows taken in turn by the grid), each thread holding up to MAXV 16-byte
+// vectors; warp shuffles, then the 8 warps' partials through shared memory,
+// read by every thread in the same order.
+template <typename A>
+__device__ __forceinline__ A block_sum256(A v, A* sm) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
+  __syncthreads();
+  A t = sm[0];
+#pragma unroll
+  for (int w = 1; w < 8; w++) t += sm[w];
+  __syncthreads();
+  return t;
+}
+template <int OP>
+__device__ __forceinline__ float block_pick256(float v, float* sm) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = pick(OP, v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = sm[0];
+#pragma unroll
+  for (int w = 1; w < 8; w++) t = pick(OP, t, sm[w]);
+  __syncthreads();
+  return t;
+}
+
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) k_softmax_rows_blk(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int n) {
+  constexpr int VEC = 16 / sizeof(T);
+  __shared__ float sm[8];
+  const int nv = n / VEC;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    float v[MAXV][VEC];
+    float m = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      const int c = t * 256 + threadIdx.x;
+      if (c < nv) {
+        const uint4 raw = *(const uint4*)(x + r * n + (int64_t)c * VEC);
+        const T* e = (const T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VEC; j++) {
+          v[t][j] = to_f<T>(e[j]);
+          m = fmaxf(m, v[t][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < 8; w++) m = fmaxf(m, sm[w]);
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++)
+      if (t * 256 + (int)threadIdx.x < nv)
+#pragma unroll
+        for (int j = 0; j < VEC; j++) {
+          if constexpr (sizeof(T) == 2) v[t][j] = __expf(v[t][j] - m);
+          else v[t][j] = expf(v[t][j] - m);
+          s += v[t][j];
+        }
+    s = block_sum256<float>(s, sm);
+    const float inv = 1.f / s;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      const int c = t * 256 + threadIdx.x;
+      if (c < nv) {
+        uint4 raw;
+        T* e = (T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VEC; j++) e[j] = from_f<T>(v[t][j] * inv);
+        *(uint4*)(y + r * n + (int64_t)c * VEC) = raw;
+      }
+    }
+  }
+}
+
+template <typename T, int MAXV, int OP>
+__global__ void __launch_bounds__(256) k_reduce_rows_blk(const T* __restrict__ x, char* out, int out_dtype, int64_t rows, int n) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr bool mm = OP == R_MAX || OP == R_MIN;
+  __shared__ double smd[8];
+  __shared__ float smf[8];
+  const int nv = n / VEC;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    float acc = 0.f, best = OP == R_MAX ? -INFINITY : INFINITY;
+    double dacc = 0.0;
+#pragma unroll
+    for (int t = 0; t < MAXV; t++) {
+      const int c = t * 256 + threadIdx.x;
+      if (c < nv) {
+        const uint4 raw = *(const uint4*)(x + r * n + (int64_t)c * VEC);
+        const T* e = (const T*)&raw;
+#pragma unroll
+        for (int j = 0; j < VEC; j++) {
+          const float f = to_f<T>(e[j]);
+          if constexpr (mm) best = pick(OP, best, f);
+          else if constexpr (OP == R_MEAN) dacc += (double)f;
+          else acc += f;
+        }
+      }
+    }
+    if constexpr (mm) best = block_pick256<OP>(best, smf);
+    else if constexpr (OP == R_MEAN) dacc = block_sum256<double>(dacc, smd);
+    else acc = block_sum256<float>(acc, smf);
+    if (threadIdx.x == 0) {
+      if constexpr (mm) st_as<float>(out, out_dtype, r, best);
+      else if constexpr (OP == R_MEAN) st_as<double>(out, out_dtype, r, dacc / (double)n);
+      else st_as<float>(out, out_dtype, r, acc);
+    }
+  }
+}
+
 // inclusive prefix sum, one thread per column, wrapping in the output dtype
 template <typename CT>
 __global__ void k_cumsum(const char* x, int dtype, char* out, int out_dtype, int64_t outer, int64_t n, int64_t inner) {
@@ -314,6 +433,19 @@ bool row_vec_ok(int dtype, int64_t n, int64_t rows) {
   const int vec = dtype == LC_F32 ? 4 : 8;
   return n > 0 && n % vec == 0 && n <= 32 * vec * 8 && n < INT32_MAX;
 }
+// Block-per-row path: dense f16 / bf16 / f32 rows longer than the warp path
+// takes, up to 256 threads x 8 vectors, 16-byte aligned.
+bool row_blk_ok(int dtype, int64_t n, int64_t rows, const void* p) {
+  if (!(dtype == LC_F16 || dtype == LC_BF16 || dtype == LC_F32) || rows <= 0 || ((uintptr_t)p & 15)) return false;
+  const int vec = dtype == LC_F32 ? 4 : 8;
+  return n > 0 && n % vec == 0 && n <= 256 * vec * 8 && n < INT32_MAX;
+}
+int row_blk_maxv(int dtype, int64_t n) {
+  const int vec = dtype == LC_F32 ? 4 : 8;
+  const int per = (int)((n / vec + 255) / 256);
+  return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8;
+}
+unsigned row_blk_grid(int64_t rows) { return (unsigned)std::min<int64_t>(rows, (int64_t)num_sms() * 8); }
 int row_vec_maxv(int dtype, int64_t n) {
   const int vec = dtype == LC_F32 ? 4 : 8;
   const int per = (int)((n / vec + 31) / 32);
@@ -337,6 +469,24 @@ void launch_reduce_vec_op(unsigned blocks, int op, const T* x, char* out, int od
     default: k_reduce_rows_vec<T, MAXV, R_MIN><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
   }
 }
+template <typename T, int MAXV>
+void launch_reduce_blk_op(unsigned blocks, int op, const T* x, char* out, int odt, int64_t rows, int n) {
+  switch (op) {
+    case R_SUM: k_reduce_rows_blk<T, MAXV, R_SUM><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+    case R_MEAN: k_reduce_rows_blk<T, MAXV, R_MEAN><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+    case R_MAX: k_reduce_rows_blk<T, MAXV, R_MAX><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+    default: k_reduce_rows_blk<T, MAXV, R_MIN><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+  }
+}
+template <typename T>
+void launch_reduce_blk(unsigned blocks, int maxv, int op, const T* x, char* out, int odt, int64_t rows, int n) {
+  switch (maxv) {
+    case 1: launch_reduce_blk_op<T, 1>(blocks, op, x, out, odt, rows, n); break;
+    case 2: launch_reduce_blk_op<T, 2>(blocks, op, x, out, odt, rows, n); break;
+    case 4: launch_reduce_blk_op<T, 4>(blocks, op, x, out, odt, rows, n); break;
+    default: launch_reduce_blk_op<T, 8>(blocks, op, x, out, odt, rows, n); break;
+  }
+}
 template <typename T>
 void launch_reduce_vec(unsigned blocks, int maxv, int op, const T* x, char* out, int odt, int64_t rows, int n) {
   switch (maxv) {
@@ -346,6 +496,14 @@ void launch_reduce_vec(unsigned blocks, int maxv, int op, const T* x, char* out,
     default: launch_reduce_vec_op<T, 8>(blocks, op, x, out, odt, rows, n); break;
   }
 }
+
+#define LC_ROWBLK_DISPATCH(KERNEL, T, MAXV_RT, BLOCKS, ...)                     \
+  switch (MAXV_RT) {                                                           \
+    case 1: KERNEL<T, 1><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    case 2: KERNEL<T, 2><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    case 4: KERNEL<T, 4><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    default: KERNEL<T, 8><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;   \
+  }
 
 template <typename CT, typename AT>
 void launch_reduce(LcTensor* c, LcTensor* y, int op, Axis3 s) {
@@ -377,13 +535,24 @@ LcTensor* reduce(int op, uint64_t xh, int axis, bool keep, const char* name) {
   if (y->numel() == 0) return y;
   LcTensor* c = contiguous(x);
   int d = x->dtype;
-  if (s.inner == 1 && op != R_ARGMAX && op != R_ARGMIN && row_vec_ok(d, s.n, s.outer)) {
+  if (s.inner == 1 && op != R_ARGMAX && op != R_ARGMIN && row_vec_ok(d, s.n, s.outer) && ((uintptr_t)c->data() & 15) == 0) {
     const unsigned blocks = blocks_for(s.outer * 32, 256);
     const int mv = row_vec_maxv(d, s.n);
     const int n = (int)s.n;
     if (d == LC_F16) launch_reduce_vec<__half>(blocks, mv, op, (const __half*)c->data(), y->data(), y->dtype, s.outer, n);
     else if (d == LC_BF16) launch_reduce_vec<__nv_bfloat16>(blocks, mv, op, (const __nv_bfloat16*)c->data(), y->data(), y->dtype, s.outer, n);
     else launch_reduce_vec<float>(blocks, mv, op, (const float*)c->data(), y->data(), y->dtype, s.outer, n);
+    LC_LAUNCHED(1);
+    if (c != x) release(c);
+    return y;
+  }
+  if (s.inner == 1 && op != R_ARGMAX && op != R_ARGMIN && row_blk_ok(d, s.n, s.outer, c->data())) {
+    const unsigned blocks = row_blk_grid(s.outer);
+    const int mv = row_blk_maxv(d, s.n);
+    const int n = (int)s.n;
+    if (d == LC_F16) launch_reduce_blk<__half>(blocks, mv, op, (const __half*)c->data(), y->data(), y->dtype, s.outer, n);
+    else if (d == LC_BF16) launch_reduce_blk<__nv_bfloat16>(blocks, mv, op, (const __nv_bfloat16*)c->data(), y->data(), y->dtype, s.outer, n);
+    else launch_reduce_blk<float>(blocks, mv, op, (const float*)c->data(), y->data(), y->dtype, s.outer, n);
     LC_LAUNCHED(1);
     if (c != x) release(c);
     return y;
@@ -427,13 +596,21 @@ int lc_softmax(lc_tensor* out, lc_tensor xh, int axis) {
     LcTensor* c = contiguous(x);
     cudaStream_t st = stream();
     bool dbl = x->dtype == LC_F64;
-    if (s.inner == 1 && odt == x->dtype && row_vec_ok(x->dtype, s.n, s.outer)) {
+    if (s.inner == 1 && odt == x->dtype && row_vec_ok(x->dtype, s.n, s.outer) && (((uintptr_t)c->data() | (uintptr_t)y->data()) & 15) == 0) {
       const unsigned blocks = blocks_for(s.outer * 32, 256);
       const int mv = row_vec_maxv(x->dtype, s.n);
       const int n = (int)s.n;
       if (x->dtype == LC_F16) { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, __half, mv, blocks, (const __half*)c->data(), (__half*)y->data(), s.outer, n) }
       else if (x->dtype == LC_BF16) { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, __nv_bfloat16, mv, blocks, (const __nv_bfloat16*)c->data(), (__nv_bfloat16*)y->data(), s.outer, n) }
       else { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, float, mv, blocks, (const float*)c->data(), (float*)y->data(), s.outer, n) }
+    } else if (s.inner == 1 && odt == x->dtype && row_blk_ok(x->dtype, s.n, s.outer, c->data()) &&
+               ((uintptr_t)y->data() & 15) == 0) {
+      const unsigned blocks = row_blk_grid(s.outer);
+      const int mv = row_blk_maxv(x->dtype, s.n);
+      const int n = (int)s.n;
+      if (x->dtype == LC_F16) { LC_ROWBLK_DISPATCH(k_softmax_rows_blk, __half, mv, blocks, (const __half*)c->data(), (__half*)y->data(), s.outer, n) }
+      else if (x->dtype == LC_BF16) { LC_ROWBLK_DISPATCH(k_softmax_rows_blk, __nv_bfloat16, mv, blocks, (const __nv_bfloat16*)c->data(), (__nv_bfloat16*)y->data(), s.outer, n) }
+      else { LC_ROWBLK_DISPATCH(k_softmax_rows_blk, float, mv, blocks, (const float*)c->data(), (float*)y->data(), s.outer, n) }
     } else if (s.inner == 1) {
       unsigned blocks = blocks_for(s.outer * 32, 256);
       if (dbl) k_softmax_rows<double><<<blocks, 256, 0, st>>>(c->data(), c->dtype, y->data(), odt, s.outer, s.n);

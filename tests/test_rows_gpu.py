@@ -1,6 +1,7 @@
-"""The row fast paths (softmax, sum / mean / max / min over the last axis,
-meanPool) against float64 numpy, across the widths that select them (a
-multiple of the 16-byte vector, at most 32 lanes x 8 vectors) and the widths
+"""The row fast paths (softmax, layerNorm, sum / mean / max / min over the
+last axis, meanPool) against float64 numpy, across the widths that select
+them (a multiple of the 16-byte vector: one warp per row up to 32 lanes x 8
+vectors, one 256-thread block per row up to 256 x 8 vectors) and the widths
 that fall back to the generic kernels, in f32 / f16 / bf16; NaN propagation
 of max / min; meanPool with masked-out and fully masked rows."""
 from __future__ import annotations
@@ -13,7 +14,8 @@ from laya_js_b200.host import HostTensor, f32_to_bf16_bits, to_f32
 
 pytestmark = pytest.mark.gpu
 
-WIDTHS = {"f32": [4, 256, 1024, 1028, 770], "f16": [8, 768, 2048, 2056, 770], "bf16": [8, 512, 2048, 2056, 770]}
+WIDTHS = {"f32": [4, 256, 1024, 1028, 770, 2304, 8192, 8196], "f16": [8, 768, 2048, 2056, 770, 2304, 16384, 16392],
+          "bf16": [8, 512, 2048, 2056, 770, 1152, 16384]}
 EPS = {"f32": 1e-5, "f16": 2e-3, "bf16": 1.6e-2}
 
 
@@ -46,13 +48,32 @@ def test_softmax_and_reductions_over_rows(dt):
         b.dispose(t)
 
 
-def test_max_min_propagate_nan():
+@pytest.mark.parametrize("n", [768, 2304])
+def test_max_min_propagate_nan(n):
     b = backend()
-    a = np.arange(2 * 768, dtype=np.float32).reshape(2, 768)
+    a = (np.arange(2 * n, dtype=np.float32).reshape(2, n) % 1000)
     a[1, 500] = np.nan
     t = b.fromHost(HostTensor("f16", a.shape, a.astype(np.float16)))
     mx, mn = to_f32(b.read(b.max(t, -1))), to_f32(b.read(b.min(t, -1)))
     assert not np.isnan(mx[0]) and np.isnan(mx[1]) and np.isnan(mn[1])
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_layer_norm_over_rows(dt):
+    b = backend()
+    rng = np.random.default_rng(9)
+    for n in WIDTHS[dt]:
+        a = (rng.standard_normal((23, n)) * 2 + 0.5).astype(np.float32)
+        h = _host(dt, a)
+        x = to_f32(h).astype(np.float64)
+        w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+        bias = (0.1 * rng.standard_normal(n)).astype(np.float32)
+        got = to_f32(b.read(b.layerNorm(b.fromHost(h), b.fromHost(HostTensor("f32", (n,), w)),
+                                        b.fromHost(HostTensor("f32", (n,), bias)), 1e-5))).astype(np.float64)
+        mu = x.mean(-1, keepdims=True)
+        ref = (x - mu) / np.sqrt(((x - mu) ** 2).mean(-1, keepdims=True) + 1e-5) * w + bias
+        tol = {"f32": 2e-5, "f16": 8e-3, "bf16": 6e-2}[dt]
+        assert np.abs(got - ref).max() <= tol, f"layerNorm n={n}"
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
