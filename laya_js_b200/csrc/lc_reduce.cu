@@ -179,6 +179,42 @@ __device__ __forceinline__ float pick(int op, float a, float b) {
   return op == R_MAX ? fmaxf(a, b) : fminf(a, b);
 }
 
+// max / min of the values of one 16-byte vector folded into a running value:
+// 16-bit types as packed pairs with NaN propagation (__hmax2_nan / __hmin2_nan,
+// exact), f32 with fmaxf / fminf and a NaN flag, so no per-element NaN branch
+template <typename T> struct Pair2;
+template <> struct Pair2<__half> { using type = __half2; };
+template <> struct Pair2<__nv_bfloat16> { using type = __nv_bfloat162; };
+template <typename T, int OP>
+struct VecPick {
+  using P = typename Pair2<T>::type;
+  P acc;
+  __device__ __forceinline__ VecPick() {
+    const T init = from_f<T>(OP == R_MAX ? -INFINITY : INFINITY);
+    acc = P(init, init);
+  }
+  __device__ __forceinline__ void add(const uint4& raw) {
+    const P* p = (const P*)&raw;
+#pragma unroll
+    for (int k = 0; k < 4; k++) acc = OP == R_MAX ? __hmax2_nan(acc, p[k]) : __hmin2_nan(acc, p[k]);
+  }
+  __device__ __forceinline__ float value() const { return pick(OP, to_f<T>(acc.x), to_f<T>(acc.y)); }
+};
+template <int OP>
+struct VecPick<float, OP> {
+  float acc = OP == R_MAX ? -INFINITY : INFINITY;
+  bool nan = false;
+  __device__ __forceinline__ void add(const uint4& raw) {
+    const float* f = (const float*)&raw;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      acc = OP == R_MAX ? fmaxf(acc, f[k]) : fminf(acc, f[k]);
+      nan |= f[k] != f[k];
+    }
+  }
+  __device__ __forceinline__ float value() const { return nan ? __int_as_float(0x7fc00000) : acc; }
+};
+
 // sum (f32 accumulation), mean (f64), max, min over each row; the operation
 // is a template parameter so the per-element loop carries no branch on it
 template <typename T, int MAXV, int OP>
@@ -193,21 +229,26 @@ __global__ void __launch_bounds__(256) k_reduce_rows_vec(const T* __restrict__ x
   for (int64_t r = warp; r < rows; r += nwarps) {
     float acc = 0.f, best = op == R_MAX ? -INFINITY : INFINITY;
     double dacc = 0.0;
+    VecPick<T, mm ? op : R_MAX> vp;
 #pragma unroll
     for (int t = 0; t < MAXV; t++) {
       const int c = t * 32 + lane;
       if (c < nv) {
         const uint4 raw = *(const uint4*)(x + r * n + (int64_t)c * VEC);
-        const T* e = (const T*)&raw;
+        if constexpr (mm) {
+          vp.add(raw);
+        } else {
+          const T* e = (const T*)&raw;
 #pragma unroll
-        for (int j = 0; j < VEC; j++) {
-          const float f = to_f<T>(e[j]);
-          if constexpr (mm) best = pick(op, best, f);
-          else if constexpr (op == R_MEAN) dacc += (double)f;
-          else acc += f;
+          for (int j = 0; j < VEC; j++) {
+            const float f = to_f<T>(e[j]);
+            if constexpr (op == R_MEAN) dacc += (double)f;
+            else acc += f;
+          }
         }
       }
     }
+    if constexpr (mm) best = vp.value();
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       if constexpr (mm) best = pick(op, best, __shfl_xor_sync(0xffffffffu, best, o));
@@ -315,21 +356,26 @@ __global__ void __launch_bounds__(256) k_reduce_rows_blk(const T* __restrict__ x
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     float acc = 0.f, best = OP == R_MAX ? -INFINITY : INFINITY;
     double dacc = 0.0;
+    VecPick<T, mm ? OP : R_MAX> vp;
 #pragma unroll
     for (int t = 0; t < MAXV; t++) {
       const int c = t * 256 + threadIdx.x;
       if (c < nv) {
         const uint4 raw = *(const uint4*)(x + r * n + (int64_t)c * VEC);
-        const T* e = (const T*)&raw;
+        if constexpr (mm) {
+          vp.add(raw);
+        } else {
+          const T* e = (const T*)&raw;
 #pragma unroll
-        for (int j = 0; j < VEC; j++) {
-          const float f = to_f<T>(e[j]);
-          if constexpr (mm) best = pick(OP, best, f);
-          else if constexpr (OP == R_MEAN) dacc += (double)f;
-          else acc += f;
+          for (int j = 0; j < VEC; j++) {
+            const float f = to_f<T>(e[j]);
+            if constexpr (OP == R_MEAN) dacc += (double)f;
+            else acc += f;
+          }
         }
       }
     }
+    if constexpr (mm) best = vp.value();
     if constexpr (mm) best = block_pick256<OP>(best, smf);
     else if constexpr (OP == R_MEAN) dacc = block_sum256<double>(dacc, smd);
     else acc = block_sum256<float>(acc, smf);
