@@ -543,6 +543,16 @@ void launch_reduce_vec(unsigned blocks, int maxv, int op, const T* x, char* out,
   }
 }
 
+#define LC_ROWVEC_DISPATCH6(KERNEL, T, MAXV_RT, BLOCKS, ...)                    \
+  switch (MAXV_RT) {                                                           \
+    case 1: KERNEL<T, 1><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    case 2: KERNEL<T, 2><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    case 3: KERNEL<T, 3><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    case 4: KERNEL<T, 4><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    case 6: KERNEL<T, 6><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    default: KERNEL<T, 8><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;   \
+  }
+
 #define LC_ROWBLK_DISPATCH(KERNEL, T, MAXV_RT, BLOCKS, ...)                     \
   switch (MAXV_RT) {                                                           \
     case 1: KERNEL<T, 1><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
@@ -644,11 +654,14 @@ int lc_softmax(lc_tensor* out, lc_tensor xh, int axis) {
     bool dbl = x->dtype == LC_F64;
     if (s.inner == 1 && odt == x->dtype && row_vec_ok(x->dtype, s.n, s.outer) && (((uintptr_t)c->data() | (uintptr_t)y->data()) & 15) == 0) {
       const unsigned blocks = blocks_for(s.outer * 32, 256);
-      const int mv = row_vec_maxv(x->dtype, s.n);
+      // the register tile holds the whole row: sized to it (3 vectors per lane
+      // for 768 16-bit values) so short rows keep more warps resident
+      const int per = (int)((s.n / (x->dtype == LC_F32 ? 4 : 8) + 31) / 32);
+      const int mv = per <= 4 ? per : per <= 6 ? 6 : 8;
       const int n = (int)s.n;
-      if (x->dtype == LC_F16) { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, __half, mv, blocks, (const __half*)c->data(), (__half*)y->data(), s.outer, n) }
-      else if (x->dtype == LC_BF16) { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, __nv_bfloat16, mv, blocks, (const __nv_bfloat16*)c->data(), (__nv_bfloat16*)y->data(), s.outer, n) }
-      else { LC_ROWVEC_DISPATCH(k_softmax_rows_vec, float, mv, blocks, (const float*)c->data(), (float*)y->data(), s.outer, n) }
+      if (x->dtype == LC_F16) { LC_ROWVEC_DISPATCH6(k_softmax_rows_vec, __half, mv, blocks, (const __half*)c->data(), (__half*)y->data(), s.outer, n) }
+      else if (x->dtype == LC_BF16) { LC_ROWVEC_DISPATCH6(k_softmax_rows_vec, __nv_bfloat16, mv, blocks, (const __nv_bfloat16*)c->data(), (__nv_bfloat16*)y->data(), s.outer, n) }
+      else { LC_ROWVEC_DISPATCH6(k_softmax_rows_vec, float, mv, blocks, (const float*)c->data(), (float*)y->data(), s.outer, n) }
     } else if (s.inner == 1 && odt == x->dtype && row_blk_ok(x->dtype, s.n, s.outer, c->data()) &&
                ((uintptr_t)y->data() & 15) == 0) {
       const unsigned blocks = row_blk_grid(s.outer);
