@@ -68,20 +68,18 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
       if (c < nv) {
         uint4 raw;
         T* e = (T*)&raw;
-        float wv[VN], bv[VN];
 #pragma unroll
-        for (int j = 0; j < VN; j += 4) {
-          float4 a4 = w ? __ldg((const float4*)(w + c * VN + j)) : make_float4(1.f, 1.f, 1.f, 1.f);
-          float4 b4 = b ? __ldg((const float4*)(b + c * VN + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
-          wv[j] = a4.x, wv[j + 1] = a4.y, wv[j + 2] = a4.z, wv[j + 3] = a4.w;
-          bv[j] = b4.x, bv[j + 1] = b4.y, bv[j + 2] = b4.z, bv[j + 3] = b4.w;
-        }
+        for (int j = 0; j < VN; j += 4) {  // weight and bias four at a time (fewer live registers)
+          const float4 a4 = w ? __ldg((const float4*)(w + c * VN + j)) : make_float4(1.f, 1.f, 1.f, 1.f);
+          const float4 b4 = b ? __ldg((const float4*)(b + c * VN + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float wv[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-        for (int j = 0; j < VN; j++) {
-          float o = (v[t][j] - mu) * rs * wv[j] + bv[j];
-          if constexpr (sizeof(T) == 4) ((float*)e)[j] = o;
-          else if constexpr (std::is_same<T, __half>::value) e[j] = __float2half_rn(o);
-          else e[j] = __float2bfloat16_rn(o);
+          for (int k = 0; k < 4; k++) {
+            const float o = (v[t][j + k] - mu) * rs * wv[k] + bv[k];
+            if constexpr (sizeof(T) == 4) ((float*)e)[j + k] = o;
+            else if constexpr (std::is_same<T, __half>::value) e[j + k] = __float2half_rn(o);
+            else e[j + k] = __float2bfloat16_rn(o);
+          }
         }
         *(uint4*)(y + r * N + (int64_t)c * VN) = raw;
       }
