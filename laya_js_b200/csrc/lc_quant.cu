@@ -7,17 +7,17 @@
 // and biases [N, ceil(K/g)] are stored in the dequantisation dtype.
 //
 // Every dequantised value is fl(q·s + b) rounded ONCE to the target dtype,
-// the rule of the reference's host dequantiser (packages/laya/src/quant.ts:189-243):
-//  * f32 target: fmaf(q, s, b) is a single rounding of the exact q·s + b;
-//  * f16/bf16 target (s, b have <= 11 significant bits): q·s is exact in f32
-//    (<= 8 + 11 bits); the sum is formed in f32 with round-to-odd and then
-//    rounded to nearest into the 16-bit type. Round-to-odd at >= 2 extra bits
-//    makes the double rounding innocuous (Boldo & Melquiond, "Emulation of
-//    FMA and correctly rounded sums: proved algorithms using rounding to odd",
-//    IEEE Trans. Computers 57(4), 2008).
+// the rule of the reference's host dequantiser (packages/laya/src/quant.ts:189-243),
+// which computes q·s + b in JS doubles and stores the double into the typed
+// array: here q·s + b is one f64 FMA (q·s is exact in f64, so the only
+// rounding before the store is the FMA's own, as in the reference's double
+// expression) and the double is then rounded once to f32, f16 or bf16
+// (dequant_f64 / store_dequant in lc_quant.cuh).
 #include "lc_api.h"
 #include "lc_gemm.h"
 #include "lc_quant.cuh"
+
+#include <mutex>
 
 using namespace lc;
 
@@ -306,17 +306,23 @@ int lc_quantized_linear(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor sh
 // calls share the one array and it keeps the last call's contents: each call
 // overwrites exactly the N·K values it reads, so nothing needs clearing, but
 // calls that overlap on the GPU (different streams, no ordering between them)
-// race on it.
+// race on it. Like every other entry of this library, calls are expected from
+// one host thread at a time (the GEMM's tensor-map cache is not locked).
 
-static __device__ __align__(256) uint8_t g_noalloc_scratch[(size_t)8 << 20];
-static constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // room for an 4M-element f16/bf16 weight
+static constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // room for a 4M-element f16/bf16 weight
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
+// The scratch address of the current device, looked up once per device. The
+// mutex keeps two host threads that make their first call at the same time
+// from racing on the table.
 void* noalloc_scratch_for_current_device() {
   static void* ptrs[128] = {};
+  static std::mutex mu;
   int dev = -1;
   CUDA_OK(cudaGetDevice(&dev));
   LC_CHECK(dev >= 0 && dev < 128, "quantizedLinearNoalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
   if (!ptrs[dev]) {
     void* p = nullptr;
     CUDA_OK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
@@ -335,6 +341,8 @@ extern "C" int lc_quantized_linear_noalloc(void* y, const void* x, int64_t m, in
   LC_CHECK(dtype == LC_F16 || dtype == LC_BF16, "quantizedLinearNoalloc: x and y must be f16 or bf16");
   LC_CHECK(sb_dtype == LC_F32 || sb_dtype == LC_F16 || sb_dtype == LC_BF16, "quantizedLinearNoalloc: scales/biases must be f32, f16 or bf16");
   LC_CHECK(mode == 1 ? biases != nullptr : biases == nullptr, "quantizedLinearNoalloc: biases are required for affine and not allowed for symmetric");
+  LC_CHECK(!bias || bias_dtype == LC_F32 || bias_dtype == LC_F16 || bias_dtype == LC_BF16,
+           "quantizedLinearNoalloc: bias must be f32, f16 or bf16");
   LC_CHECK(x && y && w && scales && m > 0, "quantizedLinearNoalloc: null pointer or empty input");
   LC_CHECK(k >= 64 && k % 8 == 0, "quantizedLinearNoalloc: in features must be a multiple of 8, at least 64");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
