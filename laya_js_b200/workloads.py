@@ -118,3 +118,113 @@ def host_getter(W: dict, quant_bits: int = 0, group: int = 64):
         cache[name] = h
         return h
     return get
+
+
+# ---------------------------------------------------------------- the benchmark configurations
+#
+# One seed family for every configuration, shared by bench.py and the parity
+# tests, so the tests check exactly the inputs the bench times.
+
+SEED = 20261201
+
+
+def cfg2_prompts(n_prompts: int = 256):
+    """n prompts with lengths uniform in [32, 512] (256 per GPU; a
+    multi-GPU run draws one global batch of 256·N and shards it)."""
+    lens = lengths(n_prompts, 32, 512, seed=SEED + 1)
+    ids, cu = token_batch(BASE, lens, seed=SEED + 2)
+    return lens, ids, cu
+
+
+def cfg0_prompt():
+    """batch 1, one 128-token prompt (CLS ... SEP)."""
+    lens = np.array([128])
+    ids, cu = token_batch(BASE, lens, seed=SEED + 5)
+    return lens, ids, cu
+
+
+def cfg3_prompts(n_prompts: int = 512):
+    """n prompts with lengths uniform in [64, 1024]."""
+    lens = lengths(n_prompts, 64, 1024, seed=SEED + 7)
+    ids, cu = token_batch(BASE, lens, seed=SEED + 8)
+    return lens, ids, cu
+
+
+def cfg4_lengths(n_prompts: int = 65536) -> np.ndarray:
+    """prompt lengths log-uniform in [16, 4096]."""
+    return lengths(n_prompts, 16, 4096, seed=SEED + 9, dist="loguniform")
+
+
+def cfg4_tokens(lens: np.ndarray):
+    return token_batch(LARGE, lens, seed=SEED + 10)
+
+
+def base_weights() -> dict:
+    """ModernBERT-base fp16 weights N(0, 0.02), LayerNorm weights 1 (the bench's)."""
+    return random_weights(BASE, seed=SEED)
+
+
+def large_weights_bf16() -> dict:
+    """ModernBERT-large / mmBERT-shape weights N(0, 0.02) rounded to bf16 (held
+    as f32 values that bf16 represents exactly), LayerNorm weights 1."""
+    from .host import bf16_bits_to_f32, f32_to_bf16_bits
+    W = random_weights(LARGE, seed=SEED + 11, dtype=np.float32)
+    return {k: (bf16_bits_to_f32(f32_to_bf16_bits(v)) if v.ndim == 2 else v) for k, v in W.items()}
+
+
+def head(cfg: dict, classes: int):
+    """The CLS classifier of a configuration: 3-way, 8-way
+    (configs[2], [3]) or 16-way; N(0, 0.02) fp16, zero bias."""
+    seeds = {3: SEED + 4, 8: SEED + 3, 16: SEED + 12}
+    return classifier(cfg, classes, seed=seeds[classes])
+
+
+def decision_head_weights(cfg: dict, seed: int = SEED + 20, head_layers: int = 2, n_act: int = 2) -> dict:
+    """Random-init Laya DecisionModel head weights (laya-mlx names, the layout
+    of packages/laya/src/model.ts:368-405) for an encoder of `cfg`'s width:
+    two pre-norm head layers (4·D ReLU FFN), the marker scorer, the action
+    head and the question-type embedding; N(0, 0.02) matrices, zero biases,
+    LayerNorm weights 1 (f32)."""
+    rng = np.random.default_rng(seed)
+    D = cfg["hidden_size"]
+    n = lambda *sh: (rng.standard_normal(sh, dtype=np.float32) * 0.02)
+    z = lambda *sh: np.zeros(sh, np.float32)
+    one = lambda *sh: np.ones(sh, np.float32)
+    W = {"type_emb.weight": n(3, D)}
+    for j in range(head_layers):
+        p = f"head.layers.{j}."
+        W.update({p + "norm1.weight": one(D), p + "norm1.bias": z(D), p + "norm2.weight": one(D), p + "norm2.bias": z(D),
+                  p + "self_attn.in_proj.weight": n(3 * D, D), p + "self_attn.in_proj.bias": z(3 * D),
+                  p + "self_attn.out_proj.weight": n(D, D), p + "self_attn.out_proj.bias": z(D),
+                  p + "linear1.weight": n(4 * D, D), p + "linear1.bias": z(4 * D),
+                  p + "linear2.weight": n(D, 4 * D), p + "linear2.bias": z(D)})
+    W.update({"scorer.layers.0.weight": one(D), "scorer.layers.0.bias": z(D), "scorer.layers.1.weight": n(D, D),
+              "scorer.layers.1.bias": z(D), "scorer.layers.3.weight": n(1, D), "scorer.layers.3.bias": z(1),
+              "act_head.layers.0.weight": n(256, D + 4), "act_head.layers.0.bias": z(256),
+              "act_head.layers.2.weight": n(n_act, 256), "act_head.layers.2.bias": z(n_act)})
+    return W
+
+
+def decision_batch(cfg: dict, lens, markers: int = 4, seed: int = SEED + 21) -> dict:
+    """A collated DecisionModel batch (packages/laya/src/model.ts:146-170
+    fields): prompts padded to the longest, `markers` marker positions per
+    prompt inside it (the last slot masked off for odd rows), a question type
+    per prompt."""
+    rng = np.random.default_rng(seed)
+    lens = np.asarray(lens, np.int64)
+    B, L = len(lens), int(lens.max())
+    ids, cu = token_batch(cfg, lens, seed=seed + 1)
+    pad = np.zeros((B, L), np.int32)
+    valid = np.zeros((B, L), np.uint8)
+    pos = np.zeros((B, markers), np.int32)
+    mm = np.ones((B, markers), np.uint8)
+    for b in range(B):
+        n = int(lens[b])
+        pad[b, :n] = ids[cu[b]:cu[b + 1]]
+        valid[b, :n] = 1
+        pos[b] = np.sort(rng.choice(np.arange(1, max(n - 1, markers + 1)), size=markers, replace=False))
+        pos[b] = np.minimum(pos[b], n - 1)
+        if b % 2:
+            mm[b, -1] = 0
+    return {"size": B, "length": L, "markerCount": markers, "inputIds": pad.reshape(-1), "attentionMask": valid.reshape(-1),
+            "markerPos": pos.reshape(-1), "markerMask": mm.reshape(-1), "qtype": rng.integers(0, 3, size=B).astype(np.int32)}

@@ -1,0 +1,189 @@
+"""Parity at the benchmark configurations' full depth: the 22-layer
+ModernBERT-base and the 28-layer ModernBERT-large / mmBERT-shape forwards, on
+the very inputs bench.py times (laya_js_b200.workloads: same seeds, LayerNorm
+weights 1, the unscaled N(0, 0.02) classifier heads), against the CPU oracle's
+outputs in tests/golden/fulldepth.npz (written by make_fulldepth.py).
+
+The fused varlen encoder runs the whole benchmark batch (256 prompts for
+configs[2], 512 for configs[3]) and the checked prompts are read out of it, so
+the batch context is the timed one; the contract path (ModernBert.forward over
+Backend<T> ops, padded batch + host masks: what laya's load()/predict() run)
+is checked on the same prompts.
+
+Tolerances are the north star's, stated per case: logits within 2e-2 max-abs
+for fp16 weights (8-bit weights compute in fp16 too) and 5e-2 for 4-bit,
+identical argmax, probabilities within 1e-3. configs[4] computes in bf16
+(8 significand bits against fp16's 11: every stored activation carries 8x
+fp16's rounding error), for which the north star states no bound; it is held
+to the 4-bit logit bound (5e-2) and to probabilities within 4e-3 (measured
+2.0e-3 over 28 layers and a 16-way head, against 3e-4 for the fp16 model).
+Logits are compared as the f64 product of the
+device's CLS row with the head weights, and as the device head's log
+probabilities centred per row (softmax is shift-invariant, so centred log
+probabilities equal centred logits).
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from gpu_util import backend
+from laya_js_b200 import workloads as WL
+from laya_js_b200.encoder import FusedEncoder
+from laya_js_b200.host import HostTensor, to_f32
+from laya_js_b200.modernbert import loadModernBert, parseModernBertConfig
+
+pytestmark = pytest.mark.gpu
+
+G = np.load(Path(__file__).resolve().parent / "golden" / "fulldepth.npz")
+PROB_TOL = 1e-3
+
+
+def _rows_of(b, hid, starts, lens):
+    """Device rows 0, L//2, L-1 of each prompt (packed [T, H]) → host [n, 3, H]."""
+    pos = np.stack([[s, s + L // 2, s + L - 1] for s, L in zip(starts, lens)]).astype(np.int32)
+    t = b.fromHost(HostTensor("i32", (pos.size,), pos.reshape(-1)))
+    r = b.embedding(hid, t)
+    out = to_f32(b.read(r)).reshape(len(starts), 3, -1)
+    b.dispose(r)
+    b.dispose(t)
+    return out
+
+
+def _head(classes, cfg):
+    hw, hb = WL.head(cfg, classes)
+    b = backend()
+    return hw, hb, b.fromHost(HostTensor("f16", hw.shape, hw)), b.fromHost(HostTensor("f32", hb.shape, hb))
+
+
+def _check(name, rows, probs, hw, hb, logit_tol, row_tol, prob_tol=PROB_TOL):
+    """rows: device hidden rows [n, 3, H]; probs: device head [n, C]."""
+    ref_rows, ref_logits, ref_probs = G[f"{name}.rows"], G[f"{name}.logits"], G[f"{name}.probs"]
+    row_err = float(np.abs(rows - ref_rows).max())
+    logits = rows[:, 0].astype(np.float64) @ hw.astype(np.float64).T + hb.astype(np.float64)
+    logit_err = float(np.abs(logits - ref_logits).max())
+    lp = np.log(np.maximum(probs.astype(np.float64), 1e-30))
+    centred = lp - lp.mean(1, keepdims=True)
+    head_err = float(np.abs(centred - (ref_logits - ref_logits.mean(1, keepdims=True))).max())
+    prob_err = float(np.abs(probs - ref_probs).max())
+    msg = (f"{name}: hidden rows max err {row_err:.3e}, logits {logit_err:.3e}, head centred log-probs {head_err:.3e}, "
+           f"probs {prob_err:.3e}")
+    print(msg)
+    assert np.array_equal(probs.argmax(1), ref_probs.argmax(1)), msg
+    assert logit_err <= logit_tol and head_err <= logit_tol, msg
+    assert prob_err <= prob_tol, msg
+    assert row_err <= row_tol, msg
+
+
+@pytest.fixture(scope="module")
+def base_fp16():
+    b = backend()
+    W = WL.base_weights()
+    enc = loadModernBert(b, parseModernBertConfig(WL.BASE), WL.host_getter(W), "f16")
+    yield enc
+    enc.dispose()
+
+
+def test_cfg2_fused_22_layers_full_batch(base_fp16):
+    b = backend()
+    lens, ids, cu = WL.cfg2_prompts()
+    assert np.array_equal(lens, G["cfg2.lens"])
+    idx = G["cfg2.idx"]
+    hw, hb, thw, thb = _head(8, WL.BASE)
+    fused = FusedEncoder(base_fp16)
+    tids = b.fromHost(HostTensor("i32", ids.shape, ids))
+    hid, probs = fused.forward(tids, cu, thw, thb)
+    rows = _rows_of(b, hid, cu[idx], lens[idx])
+    probs = to_f32(b.read(probs))
+    _check("cfg2", rows, probs[idx], hw, hb, 2e-2, 4e-2)
+    # the end-to-end host call gives the same probabilities
+    assert np.array_equal(fused.forward_host(ids, cu, thw, thb), probs)
+    fused.free()
+
+
+def _contract(b, enc, seqs, hw_t, hb_t):
+    """ModernBert.forward on a padded batch (host masks) + the CLS head as contract ops."""
+    B, L = len(seqs), max(len(s) for s in seqs)
+    pad = np.zeros((B, L), np.int32)
+    valid = np.zeros((B, L), np.uint8)
+    for i, s in enumerate(seqs):
+        pad[i, :len(s)] = s
+        valid[i, :len(s)] = 1
+    hid = enc.forward(pad, valid, B, L)
+    H = hid.shape[-1]
+    flat = b.reshape(hid, [B * L, H])
+    rows = _rows_of(b, flat, np.arange(B) * L, [len(s) for s in seqs])
+    cls = b.reshape(b.slice(hid, [0, 0, 0], [B, 1, H]), [B, H])
+    probs = to_f32(b.read(b.softmax(b.linear(cls, hw_t, hb_t), -1)))
+    return rows, probs
+
+
+def test_cfg2_contract_path_22_layers(base_fp16):
+    b = backend()
+    lens, ids, cu = WL.cfg2_prompts()
+    idx = G["cfg2.idx"]
+    hw, hb, thw, thb = _head(8, WL.BASE)
+    hb16 = b.fromHost(HostTensor("f16", hb.shape, hb.astype(np.float16)))
+    rows, probs = b.scope(lambda: _contract(b, base_fp16, [ids[cu[s]:cu[s + 1]] for s in idx], thw, hb16))
+    _check("cfg2", rows, probs, hw, hb, 2e-2, 4e-2)
+
+
+def test_cfg0_one_prompt_3way_fused_graph_and_contract(base_fp16):
+    b = backend()
+    lens, ids, cu = WL.cfg0_prompt()
+    hw, hb, thw, thb = _head(3, WL.BASE)
+    fused = FusedEncoder(base_fp16)
+    hid, probs = fused.forward(b.fromHost(HostTensor("i32", ids.shape, ids)), cu, thw, thb)
+    rows = _rows_of(b, hid, cu[:1], lens)
+    probs = to_f32(b.read(probs))
+    _check("cfg0", rows, probs, hw, hb, 2e-2, 4e-2)
+    g = fused.graph(cu, thw, thb)
+    assert np.array_equal(g.run(ids), probs)
+    g.free()
+    fused.free()
+    hb16 = b.fromHost(HostTensor("f16", hb.shape, hb.astype(np.float16)))
+    rows, probs = b.scope(lambda: _contract(b, base_fp16, [ids], thw, hb16))
+    _check("cfg0", rows, probs, hw, hb, 2e-2, 4e-2)
+
+
+@pytest.mark.parametrize("bits,logit_tol", [(4, 5e-2), (8, 2e-2)])
+def test_cfg3_quantized_22_layers_full_batch(bits, logit_tol):
+    b = backend()
+    W = WL.base_weights()
+    enc = loadModernBert(b, parseModernBertConfig(WL.BASE), WL.host_getter(W, quant_bits=bits, group=64), "f16")
+    name = f"cfg3_q{bits}"
+    lens, ids, cu = WL.cfg3_prompts()
+    assert np.array_equal(lens, G[f"{name}.lens"])
+    idx = G[f"{name}.idx"]
+    hw, hb, thw, thb = _head(8, WL.BASE)
+    fused = FusedEncoder(enc)
+    hid, probs = fused.forward(b.fromHost(HostTensor("i32", ids.shape, ids)), cu, thw, thb)
+    rows = _rows_of(b, hid, cu[idx], lens[idx])
+    probs = to_f32(b.read(probs))
+    b.dispose(hid)
+    _check(name, rows, probs[idx], hw, hb, logit_tol, 4e-2)
+    fused.free()
+    hb16 = b.fromHost(HostTensor("f16", hb.shape, hb.astype(np.float16)))
+    rows, probs = b.scope(lambda: _contract(b, enc, [ids[cu[s]:cu[s + 1]] for s in idx], thw, hb16))
+    _check(name, rows, probs, hw, hb, logit_tol, 4e-2)
+    enc.dispose()
+
+
+def test_cfg4_large_bf16_28_layers_with_4096_token_prompt():
+    b = backend()
+    W = WL.large_weights_bf16()
+    enc = loadModernBert(b, parseModernBertConfig(WL.LARGE), WL.host_getter(W), "bf16")
+    del W
+    lens = G["cfg4.lens"]
+    assert lens.max() == 4096 and np.array_equal(lens[:7], WL.cfg4_lengths()[:7])
+    ids, cu = WL.cfg4_tokens(lens)
+    hw, hb, thw, thb = _head(16, WL.LARGE)
+    fused = FusedEncoder(enc)
+    hid, probs = fused.forward(b.fromHost(HostTensor("i32", ids.shape, ids)), cu, thw, thb)
+    rows = _rows_of(b, hid, cu[:-1], lens)
+    probs = to_f32(b.read(probs))
+    _check("cfg4", rows, probs, hw, hb, 5e-2, 0.2, prob_tol=4e-3)
+    fused.free()
+    enc.dispose()
