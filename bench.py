@@ -2,28 +2,38 @@
 
 Workload: ModernBERT-base shape (22 layers, hidden
 768, 12 heads, GeGLU 1152, window 128, RoPE 160000/10000), random-init fp16
-weights N(0, 0.02), 256 prompts per GPU with lengths uniform in [32, 512]
-(seeded), token ids uniform in [5, 50368) with CLS/SEP, an 8-way CLS
-classifier + softmax. One step = one forward of that batch (ids -> class
+weights N(0, 0.02), LayerNorm weights 1, prompts with lengths uniform in
+[32, 512] (seeded), token ids uniform in [5, 50368) with CLS/SEP, an 8-way CLS
+classifier + softmax. One step = one forward of the batch (ids -> class
 probabilities) through the fused varlen encoder (lc_encoder_forward).
 
-Multi-GPU (torchrun): one process per GPU, full weight replica on each,
-every rank runs its own 256-prompt batch (weak scaling); no collective on the
-data path — NCCL is used only for the barrier and the max-over-ranks time.
+Multi-GPU (torchrun, N ranks): ONE global batch of 256·N prompts is drawn and
+sharded over the ranks by longest-processing-time on each prompt's FLOPs
+(laya_js_b200.dp.lpt_shards); every rank holds a full weight replica and runs
+its shard. In the end-to-end leg each step's probabilities are gathered to
+rank 0 on the host (a gloo group, 32 bytes per prompt). NCCL carries only the
+start/stop barriers and the max-over-ranks time: no collective on the data
+path. Inputs and all inputs of a step exceed L2 (activations ~0.5 GB).
 
-Keys beyond the driver's contract:
+Keys beyond the driver's contract (extras run on rank 0 of a 1-GPU run):
   e2e        the same metric through lc_encoder_forward_host (host ids in,
-             host probabilities out, copies inside the timed region);
+             host probabilities out, copies and the host gather inside the
+             timed region);
+  shards     tokens per rank and the cost imbalance of the LPT split;
   roofline   the tcgen05 GEMMs (dominant kernel class) vs the measured
-             sustained bf16 tensor peak, with their DRAM traffic per launch
-             from the committed ncu capture;
-  cpu_baseline  the numpy oracle (float64) on a bounded sample, all cores;
-  int4       configs[3]-style 4-bit affine g64 weights (batch 512, lengths
-             U[64, 1024]) tokens/s on the same GPU, and the p50 graph latency
-             of one 128-token prompt with those weights (fused-dequant GEMMs);
-  p50_latency_ms  configs[0] (batch 1, seq 128) end-to-end latency;
-  p50_latency_graph_ms  the same through a captured CUDA graph
-             (lc_encoder_graph_run).
+             sustained bf16 tensor peak, with their DRAM traffic per launch;
+  cpu_baseline  the C++ oracle (f32 storage, f64 accumulation) timed on one
+             thread and on all host threads over a fixed sample of the batch;
+  quantized  configs[3]: 4-bit and 8-bit affine g64 weights (batch 512,
+             lengths U[64, 1024]) tokens/s, plus the configs[0]-shape graph
+             latency with those weights (fused-dequant GEMMs);
+  large_bf16 configs[4]: ModernBERT-large / mmBERT shape in bf16 on a fixed
+             subset (the first 1024) of the 65,536-prompt length draw;
+  contract   ModernBert.encode through Backend<T> ops (what laya's
+             load()/predict() run), host buffers in and out: configs[0] p50
+             and a padded configs[2] batch;
+  p50_latency_ms / p50_latency_graph_ms  configs[0] (batch 1, seq 128,
+             3-way head) end to end, eager and as a captured CUDA graph.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -35,7 +45,6 @@ import os
 import statistics
 import subprocess
 import sys
-import time
 from pathlib import Path
 
 import numpy as np
@@ -44,9 +53,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 BATCH, LO, HI, CLASSES = 256, 32, 512, 8
-SEED = 20261201
-# DRAM bytes per GEMM launch of this workload (average over the four projections),
-# from the committed one-pass ncu capture in profiles/gemm_traffic_bench.md
+WORKLOAD = "configs[2]: ModernBERT-base fp16, 256 prompts per GPU (one global batch of 256·N, LPT-sharded), L~U[32,512], 8-way CLS head + softmax"
+METRIC = "modernbert_base_fp16_tokens_per_s"
+# DRAM bytes per GEMM launch of this workload (average over the four
+# projections), scaled from the small-case capture in profiles/gemm_traffic_bench.md
 GEMM_TRAFFIC_BYTES = 306.6e6
 
 
@@ -56,7 +66,7 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--no-extras", action="store_true", help="skip the int4 / latency / CPU-baseline legs")
+    p.add_argument("--no-extras", action="store_true", help="skip the extra legs (latency, quantized, large, contract, CPU)")
     return p.parse_args()
 
 
@@ -71,6 +81,20 @@ def measured_peaks() -> dict:
         d = json.loads(f.read_text())
         return {"bf16": d.get("bf16_tflops_sustained", 1417.5), "hbm": d.get("hbm_gbs", 6449.7), "src": "measured"}
     return {"bf16": 1400.0, "hbm": 6650.0, "src": "fallback"}
+
+
+def shard(lens: np.ndarray, ids: np.ndarray, cu: np.ndarray, rank: int, world: int):
+    """This rank's prompts of the global batch (LPT on prompt FLOPs), re-packed."""
+    from laya_js_b200.dp import lpt_shards, prompt_cost
+    shards = lpt_shards([prompt_cost(int(L)) for L in lens], world)
+    mine = np.asarray(shards[rank], np.int64)
+    parts = [ids[cu[i]:cu[i + 1]] for i in mine]
+    my_ids = np.concatenate(parts).astype(np.int32)
+    my_cu = np.concatenate([[0], np.cumsum([len(p) for p in parts])]).astype(np.int32)
+    costs = [sum(prompt_cost(int(lens[i])) for i in s) for s in shards]
+    info = {"tokens_per_rank": [int(lens[s].sum()) for s in shards], "prompts_per_rank": [len(s) for s in shards],
+            "cost_imbalance": max(costs) / (sum(costs) / world), "split": "LPT on per-prompt FLOPs (linear + attention)"}
+    return mine, my_ids, my_cu, info
 
 
 class Clocks:
@@ -128,52 +152,242 @@ class Clocks:
                 "power_w": statistics.median(pw) if pw else None}
 
 
-def cpu_baseline(cfg_json: dict, W: dict, ids: np.ndarray, cu: np.ndarray, budget_s: float = 12.0) -> dict:
-    """The oracle (numpy float64 restatement of the reference CPU backend) on a
-    bounded sample of the same batch: whole sequences until `budget_s` elapse."""
-    from oracle import models as M
-    ocfg = M.parse_config(cfg_json)
-    Wf = {k: v.astype(np.float32) for k, v in W.items()}
-    t0 = time.perf_counter()
-    tokens = n = 0
-    for s in range(len(cu) - 1):
-        seq = ids[cu[s]:cu[s + 1]]
-        M.encoder_varlen(ocfg, Wf, [seq])
-        tokens += len(seq)
-        n += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
-    dt = time.perf_counter() - t0
-    return {"value": tokens / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n} of {len(cu) - 1} sequences ({tokens} tokens) of the same batch, numpy float64 oracle, {dt:.1f} s"}
+# ---------------------------------------------------------------- CPU baseline / reference arm
+
+def cpu_sample(lens: np.ndarray, every: int = 32) -> np.ndarray:
+    """The fixed sample of the batch the CPU times: every 32nd prompt (8 of
+    256: the same length distribution, ~2.2 k tokens)."""
+    return np.arange(0, len(lens), every)
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_forward_rate(threads: int, steps: int, warmup: int) -> dict:
+    """tokens/s of the C++ oracle (oracle/cpu_encoder.cpp: the encoder + head in
+    f32 storage with f64 accumulation) over the fixed sample, `threads` threads."""
+    from laya_js_b200 import workloads as WL
+    from oracle import cpu
+    W = WL.base_weights()
+    lens, ids, cu = WL.cfg2_prompts()
+    hw, hb = WL.head(WL.BASE, CLASSES)
+    sel = cpu_sample(lens)
+    seqs = [ids[cu[i]:cu[i + 1]] for i in sel]
+    enc = cpu.Encoder(WL.BASE, W)
+    times = []
+    for i in range(warmup + steps):
+        dt = enc.timed_forward(seqs, hw, hb, threads)
+        if i >= warmup:
+            times.append(dt)
+    tokens = int(sum(len(s) for s in seqs))
+    v = tokens / statistics.median(times)
+    return {"value": v, "unit": "tokens/s", "cores": threads, "tokens_per_step": tokens, "ms_per_step": statistics.median(times) * 1e3}
+
+
+def cpu_baseline() -> dict:
+    """Rank 0 at N=1: the C++ oracle on one thread and on all host threads."""
+    allt = cpu_threads()
+    one = cpu_forward_rate(1, 1, 0)
+    many = cpu_forward_rate(allt, 2, 1)
+    return {"value": many["value"], "unit": "tokens/s", "cores": allt, "kind": "port",
+            "single_thread": {"value": one["value"], "unit": "tokens/s", "cores": 1},
+            "nproc": os.cpu_count(), "cpu_model": cpu_model(),
+            "sample": f"every 32nd prompt of the configs[2] batch (8 prompts, {many['tokens_per_step']} tokens) per step, "
+                      "C++ oracle (f32 storage, f64 accumulation, std::thread workers), same weights and head"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
-    """--impl reference: the reference's CPU path (here: the oracle port, since
-    backend-cpu is an un-vendored npm package and no JS runtime exists) on this
-    box's host cores, same config/metric; rank 0 only."""
+    """--impl reference: the reference's CPU path on this box's host cores. The
+    reference's own CPU backend (npm @johnhenry/math-plus-tensor-cpu) is not
+    vendored and no JS runtime exists, so the C++ port of its semantics
+    (oracle/cpu_encoder.cpp) stands in, with every host thread; each step is the
+    fixed sample of the configs[2] batch. Rank 0 alone runs and prints."""
     if rank != 0:
         return
-    from laya_js_b200 import workloads as WL
-    cfg_json = WL.BASE
-    W = WL.random_weights(cfg_json, seed=SEED)
-    lens = WL.lengths(BATCH, LO, HI, seed=SEED + 1)
-    ids, cu = WL.token_batch(cfg_json, lens, seed=SEED + 2)
-    steps = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(cfg_json, W, ids, cu, budget_s=4.0 if i < args.warmup else 8.0)
-        if i >= args.warmup:
-            steps.append(r)
-    v = statistics.median(s["value"] for s in steps)
-    line = {"impl": "reference", "metric": "modernbert_base_fp16_tokens_per_s", "value": v, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f64", "data": "synthetic (seeded random-init weights and token ids)",
-            "config": {"workload": "configs[2]: ModernBERT-base, batch 256 varlen L~U[32,512], 8-way CLS head", "global_batch": BATCH,
-                       "seq_len": f"U[{LO},{HI}]"},
-            "cpu_baseline": {**steps[-1], "value": v},
+    threads = cpu_threads()
+    r = cpu_forward_rate(threads, args.steps, args.warmup)
+    v = r["value"]
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init N(0,0.02) weights, uniform token ids)",
+            "config": {"workload": WORKLOAD, "global_batch": BATCH * world, "seq_len": f"U[{LO},{HI}]", "parallelism": f"dp{world}"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "nproc": os.cpu_count(),
+                             "cpu_model": cpu_model(),
+                             "sample": f"every 32nd prompt of the configs[2] batch ({r['tokens_per_step']} tokens) per step"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "reference CPU backend (npm math-plus-tensor-cpu) is not vendored and no JS runtime exists; the numpy port of its semantics stands in"}
+            "note": "the reference CPU backend (npm math-plus-tensor-cpu) is not vendored and no JS runtime exists; "
+                    "the C++ port of its semantics (f32 storage, f64 accumulation) stands in"}
     print(json.dumps(line))
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def b_stream(b) -> int:
+    import ctypes as C
+    from laya_js_b200 import _lib
+    s = C.c_uint64()
+    _lib.call("lc_get_stream", C.byref(s))
+    return s.value
+
+
+class Events:
+    """CUDA events on the library stream (wrapped as a torch ExternalStream)."""
+
+    def __init__(self, b):
+        import torch
+        self.torch = torch
+        self.stream = torch.cuda.ExternalStream(b_stream(b))
+
+    def time(self, fn, reps: int) -> float:
+        """Device ms from before the first to after the last of `reps` calls."""
+        t = self.torch
+        t.cuda.synchronize()
+        e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
+        with t.cuda.stream(self.stream):
+            e0.record(self.stream)
+            for _ in range(reps):
+                fn()
+            e1.record(self.stream)
+        t.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    def p50(self, fn, reps: int = 50, warm: int = 5) -> float:
+        for _ in range(warm):
+            fn()
+        return statistics.median(self.time(fn, 1) for _ in range(reps))
+
+
+def latency_cfg0(b, ev, fused, thw, thb, graph: bool = False) -> float:
+    """batch 1, seq 128 (CLS ... SEP), the 3-way head; p50 over 50
+    end-to-end calls (host ids in, host probabilities out), eager or as a
+    captured CUDA graph; CUDA events on the library stream around each call."""
+    from laya_js_b200 import workloads as WL
+    _, ids, cu = WL.cfg0_prompt()
+    out = np.empty((1, thw.shape[0]), np.float32)
+    g = fused.graph(cu, thw, thb) if graph else None
+    call = (lambda: g.run(ids, out=out)) if graph else (lambda: fused.forward_host(ids, cu, thw, thb, out=out))
+    ms = ev.p50(call)
+    if g is not None:
+        g.free()
+    return ms
+
+
+def quantized_leg(b, ev, bits: int, steps: int) -> dict:
+    """all Linear weights `bits`-bit affine g64 (fp16 scales/biases), 512 prompts, L~U[64,1024]."""
+    from laya_js_b200 import encoder as E, workloads as WL
+    from laya_js_b200.host import HostTensor
+    from laya_js_b200.modernbert import loadModernBert, parseModernBertConfig
+    W = WL.base_weights()
+    enc = loadModernBert(b, parseModernBertConfig(WL.BASE), WL.host_getter(W, quant_bits=bits, group=64), "f16")
+    fused = E.FusedEncoder(enc)
+    lens, ids, cu = WL.cfg3_prompts()
+    tids = b.fromHost(HostTensor("i32", ids.shape, ids))
+    hw, hb = WL.head(WL.BASE, CLASSES)
+    thw, thb = b.fromHost(HostTensor("f16", hw.shape, hw)), b.fromHost(HostTensor("f32", hb.shape, hb))
+
+    def step():
+        _, p = fused.forward(tids, cu, thw, thb, want_hidden=False)
+        b.dispose(p)
+    for _ in range(3):
+        step()
+    ms = ev.time(step, steps)
+    T = int(cu[-1])
+    hw3, hb3 = WL.head(WL.BASE, 3)
+    t3w, t3b = b.fromHost(HostTensor("f16", hw3.shape, hw3)), b.fromHost(HostTensor("f32", hb3.shape, hb3))
+    lat = latency_cfg0(b, ev, fused, t3w, t3b, graph=True)
+    for t in (tids, thw, thb, t3w, t3b):
+        b.dispose(t)
+    fused.free()
+    enc.dispose()
+    return {"value": T * steps / (ms / 1e3), "unit": "tokens/s", "steps": steps, "ms_per_step": ms / steps, "tokens_per_step": T,
+            "config": f"configs[3]: {bits}-bit affine g64 (fp16 scales and biases), batch 512, L~U[64,1024], 8-way head",
+            "p50_latency_graph_ms": lat, "latency_config": f"configs[0] (one 128-token prompt, 3-way head) with these {bits}-bit weights"}
+
+
+def large_leg(b, ev, steps: int, n_prompts: int = 1024) -> dict:
+    """ModernBERT-large / mmBERT shape (28 layers, hidden 1024, 16
+    heads, GeGLU 2624, vocab 256000) in bf16, 16-way CLS head; the first
+    `n_prompts` of the 65,536-prompt log-uniform [16, 4096] length draw."""
+    from laya_js_b200 import encoder as E, workloads as WL
+    from laya_js_b200.host import HostTensor
+    from laya_js_b200.modernbert import loadModernBert, parseModernBertConfig
+    W = WL.large_weights_bf16()
+    enc = loadModernBert(b, parseModernBertConfig(WL.LARGE), WL.host_getter(W), "bf16")
+    del W
+    fused = E.FusedEncoder(enc)
+    lens = WL.cfg4_lengths()[:n_prompts]
+    ids, cu = WL.cfg4_tokens(lens)
+    tids = b.fromHost(HostTensor("i32", ids.shape, ids))
+    hw, hb = WL.head(WL.LARGE, 16)
+    thw, thb = b.fromHost(HostTensor("f16", hw.shape, hw)), b.fromHost(HostTensor("f32", hb.shape, hb))
+
+    def step():
+        _, p = fused.forward(tids, cu, thw, thb, want_hidden=False)
+        b.dispose(p)
+    step()
+    ms = ev.time(step, steps)
+    T = int(cu[-1])
+    flops = linear_flops_per_token(WL.LARGE) * T
+    for t in (tids, thw, thb):
+        b.dispose(t)
+    fused.free()
+    enc.dispose()
+    return {"value": T * steps / (ms / 1e3), "unit": "tokens/s", "steps": steps, "ms_per_step": ms / steps, "tokens_per_step": T,
+            "linear_tflops": flops / (ms / steps / 1e3) / 1e12,
+            "config": f"configs[4]: ModernBERT-large/mmBERT shape bf16, 28 layers, the first {n_prompts} prompts of the 65,536 "
+                      "log-uniform [16,4096] draw, 16-way head"}
+
+
+def contract_leg(b, ev, enc, thw3, thb3, thw8, thb8) -> dict:
+    """ModernBert.encode through the Backend<T> ops (modernbert.py, the path of
+    laya's load()/predict()): host ids + mask in (masks built on the host and
+    uploaded, as packages/modernbert/src/index.ts:369-384 does), the CLS head as
+    slice → linear → softmax, probabilities read back to the host."""
+    from laya_js_b200 import workloads as WL
+
+    def run(seqs, tw, tb):
+        B, L = len(seqs), max(len(s) for s in seqs)
+        pad = np.zeros((B, L), np.int32)
+        valid = np.zeros((B, L), np.uint8)
+        for i, s in enumerate(seqs):
+            pad[i, :len(s)] = s
+            valid[i, :len(s)] = 1
+
+        def f():
+            hid = enc.forward(pad, valid, B, L)
+            H = hid.shape[-1]
+            cls = b.reshape(b.slice(hid, [0, 0, 0], [B, 1, H]), [B, H])
+            return b.read(b.softmax(b.linear(cls, tw, tb), -1))
+        return lambda: b.scope(f)
+
+    _, ids0, cu0 = WL.cfg0_prompt()
+    lat = ev.p50(run([ids0], thw3, thb3), reps=30)
+    lens, ids, cu = WL.cfg2_prompts()
+    seqs = [ids[cu[i]:cu[i + 1]] for i in range(len(lens))]
+    call = run(seqs, thw8, thb8)
+    call()
+    ms = ev.time(call, 3) / 3
+    T = int(lens.sum())
+    return {"p50_latency_ms_cfg0": lat,
+            "cfg2_padded": {"value": T / (ms / 1e3), "unit": "tokens/s (valid tokens)", "ms_per_step": ms,
+                            "padded_tokens": int(len(lens) * lens.max()), "valid_tokens": T},
+            "what": "ModernBert.forward over Backend<T> ops (tcgen05 linear, sdpa on the padded batch with host masks, "
+                    "row kernels) + CLS head, host buffers in and out, CUDA events on the library stream"}
 
 
 def main() -> None:
@@ -186,32 +400,32 @@ def main() -> None:
         return
 
     import torch
-    dist = None
+    dist = gloo = None
+    torch.cuda.set_device(local)
     if world > 1:
         import datetime
         import torch.distributed as dist
-        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(f"cuda:{local}"))
-    else:
-        torch.cuda.set_device(local)
+        gloo = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
 
     from laya_js_b200 import createCudaBackend, encoder as E, workloads as WL
     from laya_js_b200.host import HostTensor
     from laya_js_b200.modernbert import loadModernBert, parseModernBertConfig
 
     b = createCudaBackend(local)
-    stream = torch.cuda.ExternalStream(b_stream(b))
+    ev = Events(b)
+    stream = ev.stream
     cfg_json = WL.BASE
-    cfg = parseModernBertConfig(cfg_json)
-    W = WL.random_weights(cfg_json, seed=SEED)
-    enc = loadModernBert(b, cfg, WL.host_getter(W), "f16")
+    W = WL.base_weights()
+    enc = loadModernBert(b, parseModernBertConfig(cfg_json), WL.host_getter(W), "f16")
     fused = E.FusedEncoder(enc)
-    hw, hb = WL.classifier(cfg_json, CLASSES, seed=SEED + 3)
+    hw, hb = WL.head(cfg_json, CLASSES)
     thw = b.fromHost(HostTensor("f16", hw.shape, hw))
     thb = b.fromHost(HostTensor("f32", hb.shape, hb))
-    lens = WL.lengths(BATCH, LO, HI, seed=SEED + 1 + 1000 * rank)
-    ids, cu = WL.token_batch(cfg_json, lens, seed=SEED + 2 + 1000 * rank)
+    lens_all, ids_all, cu_all = WL.cfg2_prompts(BATCH * world)
+    mine, ids, cu, shard_info = shard(lens_all, ids_all, cu_all, rank, world)
     T = int(cu[-1])
+    tok_total = int(lens_all.sum())
     tids = b.fromHost(HostTensor("i32", ids.shape, ids))
 
     def step():
@@ -258,47 +472,51 @@ def main() -> None:
     ms, launches, _, clocks = timed(False)
     # ---- second timed region: per-kernel-class CUDA events (roofline, breakdown)
     ms_prof, _, prof, _ = timed(True)
-    tok_total = T * world  # every rank's batch has its own lengths; sum them exactly
-    if dist is not None:
-        t = torch.tensor([T], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t)
-        tok_total = int(t.item())
     value = tok_total * args.steps / (ms / 1e3)
 
-    # ---- e2e: host ids -> host probabilities through the C ABI (copies inside the timed region)
-    probs = np.empty((BATCH, CLASSES), np.float32)
-    for _ in range(2):
+    # ---- e2e: host ids -> host probabilities through the C ABI (copies inside
+    # the timed region), then this step's probabilities gathered to rank 0 on the host
+    probs = np.empty((len(mine), CLASSES), np.float32)
+    gathered = np.zeros((len(lens_all), CLASSES), np.float32) if rank == 0 else None
+
+    def e2e_step():
         fused.forward_host(ids, cu, thw, thb, out=probs)
+        if gloo is not None:
+            parts = [None] * world if rank == 0 else None
+            dist.gather_object((mine, probs), parts, dst=0, group=gloo)
+            if rank == 0:
+                for idx, p in parts:
+                    gathered[idx] = p
+        else:
+            gathered[mine] = probs
+
+    for _ in range(2):
+        e2e_step()
     barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for _ in range(args.steps):
-            fused.forward_host(ids, cu, thw, thb, out=probs)
-        f1.record(stream)
-    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ev.time(e2e_step, args.steps))
     barrier()
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
     e2e_value = tok_total * args.steps / (e2e_ms / 1e3)
+    if rank == 0:
+        assert np.all(np.abs(gathered.sum(1) - 1) < 1e-3), "gathered probabilities incomplete"
 
     peaks = measured_peaks()
     gemm_flops = linear_flops_per_token(cfg_json) * T * args.steps
     g = prof["gemm"]
     achieved = gemm_flops / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else None
     line = {
-        "metric": "modernbert_base_fp16_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16", "data": "synthetic (seeded random-init N(0,0.02) weights, uniform token ids)",
-        "config": {"workload": "configs[2]: ModernBERT-base fp16, 256 prompts/GPU varlen L~U[32,512], 8-way CLS head + softmax",
-                   "global_batch": BATCH * world, "seq_len": f"U[{LO},{HI}]", "tokens_per_gpu_step": T, "parallelism": f"dp{world}",
+        "config": {"workload": WORKLOAD, "global_batch": BATCH * world, "seq_len": f"U[{LO},{HI}]", "tokens_per_gpu_step": T,
+                   "tokens_per_step": tok_total, "parallelism": f"dp{world}",
                    "l2": "inputs larger than L2 (activations ~0.5 GB per step)"},
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * 4 + (BATCH + 1) * 4,
-                "d2h_bytes_per_step": BATCH * CLASSES * 4},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * 4 + (len(mine) + 1) * 4,
+                "d2h_bytes_per_step": len(mine) * CLASSES * 4,
+                "what": "lc_encoder_forward_host per rank (H2D ids + cu_seqlens, D2H probabilities) and the host gather to rank 0"},
+        "shards": shard_info,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
                      "frac": (achieved / peaks["bf16"]) if achieved else None, "traffic": GEMM_TRAFFIC_BYTES,
-                     "traffic_src": "profiles/gemm_traffic_bench.md: ncu dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch, "
-                                    "one-pass capture of this workload",
+                     "traffic_src": "profiles/gemm_traffic_bench.md: ncu dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch",
                      "flop_per_launch": gemm_flops / max(g["launches"], 1),
                      "kernel": "k_gemm_pair (tcgen05 CTA-pair GEMMs: Wqkv+RoPE+folded LN, Wo+residual, Wi+GeGLU+folded LN, mlp.Wo+residual)",
                      "peak_src": f"{peaks['src']} sustained bf16 (MEASURED_PEAKS.json)",
@@ -309,100 +527,47 @@ def main() -> None:
         "gpu_launches": launches,
         "clocks": clocks,
     }
-    if rank == 0 and not args.no_extras:
+    extras = rank == 0 and world == 1 and not args.no_extras
+    if extras:
+        hw3, hb3 = WL.head(cfg_json, 3)
+        thw3, thb3 = b.fromHost(HostTensor("f16", hw3.shape, hw3)), b.fromHost(HostTensor("f32", hb3.shape, hb3))
+        for key, fn in (("p50_latency_ms", lambda: latency_cfg0(b, ev, fused, thw3, thb3)),
+                        ("p50_latency_graph_ms", lambda: latency_cfg0(b, ev, fused, thw3, thb3, graph=True))):
+            try:
+                line[key] = fn()
+            except Exception as ex:  # noqa: BLE001
+                line[key] = f"failed: {ex}"
+        line["latency_config"] = "configs[0]: one 128-token prompt, 3-way CLS head, host ids in, host probabilities out"
         try:
-            line["p50_latency_ms"] = latency_cfg0(b, fused, thw, thb, cfg_json)
-            line["p50_latency_graph_ms"] = latency_cfg0(b, fused, thw, thb, cfg_json, graph=True)
+            hb3_16 = b.fromHost(HostTensor("f16", hb3.shape, hb3.astype(np.float16)))
+            hb8_16 = b.fromHost(HostTensor("f16", hb.shape, hb.astype(np.float16)))
+            line["contract"] = contract_leg(b, ev, enc, thw3, hb3_16, thw, hb8_16)
         except Exception as ex:  # noqa: BLE001
-            line["p50_latency_ms"] = f"failed: {ex}"
-        try:
-            line["cpu_baseline"] = cpu_baseline(cfg_json, W, ids, cu)
-        except Exception as ex:  # noqa: BLE001
-            line["cpu_baseline"] = f"failed: {ex}"
+            line["contract"] = f"failed: {ex}"
     fused.free()
     enc.dispose()
-    if rank == 0 and not args.no_extras:
+    b.dispose(tids)
+    if extras:
+        q = {}
+        for bits in (4, 8):
+            try:
+                q[f"int{bits}"] = quantized_leg(b, ev, bits, min(args.steps, 10))
+            except Exception as ex:  # noqa: BLE001
+                q[f"int{bits}"] = f"failed: {ex}"
+        line["quantized"] = q
         try:
-            line["int4"] = int4_leg(b, min(args.steps, 10))
+            line["large_bf16"] = large_leg(b, ev, min(args.steps, 3))
         except Exception as ex:  # noqa: BLE001
-            line["int4"] = f"failed: {ex}"
+            line["large_bf16"] = f"failed: {ex}"
+        try:
+            line["cpu_baseline"] = cpu_baseline()
+        except Exception as ex:  # noqa: BLE001
+            line["cpu_baseline"] = f"failed: {ex}"
     if rank == 0:
         print(json.dumps(line))
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
-
-
-def b_stream(b) -> int:
-    import ctypes as C
-    from laya_js_b200 import _lib
-    s = C.c_uint64()
-    _lib.call("lc_get_stream", C.byref(s))
-    return s.value
-
-
-def latency_cfg0(b, fused, thw, thb, cfg_json, graph: bool = False) -> float:
-    """batch 1, seq 128 (CLS ... SEP), p50 over 50 end-to-end calls
-    (host ids in, host probabilities out), eager or as a captured CUDA graph."""
-    from laya_js_b200 import workloads as WL
-    ids, cu = WL.token_batch(cfg_json, np.array([128]), seed=SEED + 5)
-    out = np.empty((1, thw.shape[0]), np.float32)
-    g = fused.graph(cu, thw, thb) if graph else None
-    call = (lambda: g.run(ids, out=out)) if graph else (lambda: fused.forward_host(ids, cu, thw, thb, out=out))
-    for _ in range(5):
-        call()
-    ts = []
-    for _ in range(50):
-        t0 = time.perf_counter()
-        call()
-        ts.append((time.perf_counter() - t0) * 1e3)
-    if g is not None:
-        g.free()
-    return statistics.median(ts)
-
-
-def int4_leg(b, steps: int) -> dict:
-    """all Linear weights 4-bit affine g64 (fp16 scales/biases), 512 prompts, L~U[64,1024]."""
-    import torch
-    from laya_js_b200 import encoder as E, workloads as WL
-    from laya_js_b200.host import HostTensor
-    from laya_js_b200.modernbert import loadModernBert, parseModernBertConfig
-    cfg_json = WL.BASE
-    W = WL.random_weights(cfg_json, seed=SEED)
-    enc = loadModernBert(b, parseModernBertConfig(cfg_json), WL.host_getter(W, quant_bits=4, group=64), "f16")
-    fused = E.FusedEncoder(enc)
-    lens = WL.lengths(512, 64, 1024, seed=SEED + 7)
-    ids, cu = WL.token_batch(cfg_json, lens, seed=SEED + 8)
-    tids = b.fromHost(HostTensor("i32", ids.shape, ids))
-    for _ in range(3):
-        h, _ = fused.forward(tids, cu, want_hidden=True)
-        b.dispose(h)
-    stream = torch.cuda.ExternalStream(b_stream(b))
-    torch.cuda.synchronize()
-    b.flush()
-    with torch.cuda.stream(stream):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            h, _ = fused.forward(tids, cu, want_hidden=True)
-            b.dispose(h)
-        e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    T = int(cu[-1])
-    b.dispose(tids)
-    # one 128-token prompt with these weights (the packed-weight GEMMs), as a CUDA graph
-    hw, hb = WL.classifier(cfg_json, CLASSES, seed=SEED + 3)
-    thw = b.fromHost(HostTensor("f16", hw.shape, hw))
-    thb = b.fromHost(HostTensor("f32", hb.shape, hb))
-    lat = latency_cfg0(b, fused, thw, thb, cfg_json, graph=True)
-    b.dispose(thw)
-    b.dispose(thb)
-    fused.free()
-    enc.dispose()
-    return {"value": T * steps / (ms / 1e3), "unit": "tokens/s", "steps": steps, "tokens_per_step": T,
-            "config": "configs[3]: 4-bit affine g64, batch 512, L~U[64,1024], hidden states out",
-            "p50_latency_graph_ms": lat, "latency_config": "configs[0] shape (one 128-token prompt) with these 4-bit weights"}
 
 
 if __name__ == "__main__":
