@@ -139,11 +139,40 @@ int lc_dequantize(lc_tensor* out, lc_tensor w, lc_tensor scales, lc_tensor biase
  * pointers; w/scales/biases as lc_from_host_quantized stores them (sb_dtype);
  * bias optional ([n], bias_dtype). Allocates nothing. The first call on each
  * device resolves the scratch address; make it before any stream capture.
- * Calls share the scratch: calls that overlap on the GPU race.
+ * Calls share the scratch: calls that overlap on the GPU race. As for the
+ * rest of this library, make calls from one host thread at a time.
  */
 int lc_quantized_linear_noalloc(void* y, const void* x, int64_t m, int64_t k, int dtype, const uint8_t* w, const void* scales,
                                 const void* biases, int64_t n, int bits, int group_size, int mode, int sb_dtype,
                                 const void* bias, int bias_dtype, uint64_t stream);
+
+/* ---- optional compile (index.ts:244-245) as CUDA-graph capture ----
+ * The ops issued on the library stream between _begin and _end are recorded
+ * (relaxed stream capture) into a graph that _launch replays; allocations
+ * made while capturing belong to the graph and must be released before _end
+ * (copy results out with lc_copy_into first). Memory released while
+ * capturing that predates the capture is kept until lc_graph_destroy. An op
+ * that synchronises with the host fails the capture; _abort discards it. */
+int lc_graph_capture_begin(void);
+int lc_graph_capture_end(uint64_t* graph);
+int lc_graph_capture_abort(void);
+int lc_graph_launch(uint64_t graph);
+int lc_graph_destroy(uint64_t graph);
+/* dst (dense) <- src, same dtype and shape, on the library stream (capturable). */
+int lc_copy_into(lc_tensor dst, lc_tensor src);
+
+/* ---- failure-path test hooks (no counterpart in the reference) ----
+ * Every mbarrier wait in the pipelined kernels gives up after a limit (2 s),
+ * records the timeout in a device error word and returns; lc_flush / lc_read
+ * report it. lc_debug_set_wait_limit(ns) shortens that limit (0 restores 2 s)
+ * and lc_debug_stuck_wait launches one kernel whose wait nothing satisfies,
+ * so a test can check the error path without faulting or hanging the GPU.
+ * lc_debug_set_alloc_cap(bytes) makes tensor allocations fail with the
+ * out-of-memory error once the live tensor bytes would pass `bytes` (0 = no
+ * cap), so the out-of-memory path can be exercised on any GPU. */
+int lc_debug_set_wait_limit(uint64_t ns);
+int lc_debug_stuck_wait(void);
+int lc_debug_set_alloc_cap(int64_t bytes);
 
 /* ---- optional general numerics (index.ts:265-316) ---- */
 int lc_equal(lc_tensor* out, lc_tensor a, lc_tensor b);

@@ -255,6 +255,18 @@ class CudaBackend:
         return self._op("lc_quantized_embedding", self._t(w), self._t(scales), self._t(biases), int(opts.bits),
                         int(opts.groupSize), _MODE[opts.mode], self._t(ids))
 
+    # ------------------------------------------------------------ optional: compile
+    def compile(self, fn: Callable[..., Any]) -> Callable[..., Any]:
+        """index.ts:244-245 compile: ``fn`` (a pure function of its tensor
+        arguments; tensors it captures from outside are constants, as under
+        MLX's compile, packages/backend-mlx/src/index.ts:773-781) is run
+        eagerly on the first call of each input signature (dtypes and shapes)
+        and recorded as a CUDA graph on that call's tensors; later calls with
+        the same signature copy their arguments into the recorded inputs,
+        replay the graph in one launch and return fresh copies of its outputs.
+        Outputs may be a tensor, a list/tuple of tensors or a dict of tensors."""
+        return _Compiled(self, fn)
+
     # ------------------------------------------------------------ optional general numerics
     def equal(self, a, b): return self._op("lc_equal", self._t(a), self._t(b))
     def notEqual(self, a, b): return self._op("lc_not_equal", self._t(a), self._t(b))
@@ -278,6 +290,98 @@ class CudaBackend:
     def mean(self, x, axis, keepDims=False): return self._op("lc_mean", self._t(x), int(axis), int(bool(keepDims)))
     def min(self, x, axis, keepDims=False): return self._op("lc_min", self._t(x), int(axis), int(bool(keepDims)))
     def cumsum(self, x, axis): return self._op("lc_cumsum", self._t(x), int(axis))
+
+
+def _flatten(r):
+    """(flat tensor list, rebuild(list) -> same structure) of a compiled fn's result."""
+    if isinstance(r, CudaTensor):
+        return [r], lambda xs: xs[0]
+    if isinstance(r, (list, tuple)):
+        if not all(isinstance(x, CudaTensor) for x in r):
+            raise TypeError("compile: outputs must be tensors (a tensor, a list/tuple or a dict of tensors)")
+        kind = type(r)
+        return list(r), lambda xs: kind(xs)
+    if isinstance(r, dict):
+        keys = list(r)
+        if not all(isinstance(r[k], CudaTensor) for k in keys):
+            raise TypeError("compile: outputs must be tensors (a tensor, a list/tuple or a dict of tensors)")
+        return [r[k] for k in keys], lambda xs: dict(zip(keys, xs))
+    raise TypeError("compile: outputs must be tensors (a tensor, a list/tuple or a dict of tensors)")
+
+
+class _Graph:
+    """One recorded signature: input and output tensors owned by the graph."""
+
+    def __init__(self, b: "CudaBackend", handle: int, ins: list, outs: list, rebuild):
+        self.b, self.handle, self.ins, self.outs, self.rebuild = b, handle, ins, outs, rebuild
+        self._fin = weakref.finalize(self, _Graph._release, b, handle, ins + outs)
+
+    @staticmethod
+    def _release(b, handle, ts):
+        if b._destroyed:
+            return
+        try:
+            _lib.call("lc_graph_destroy", C.c_uint64(handle))
+        finally:
+            for t in ts:
+                b.dispose(t)
+
+    def run(self, args):
+        b = self.b
+        for slot, a in zip(self.ins, args):
+            _lib.call("lc_copy_into", C.c_uint64(slot.handle), C.c_uint64(b._h(a, "compiled call")))
+        _lib.call("lc_graph_launch", C.c_uint64(self.handle))
+        return self.rebuild([b.cast(o, o.dtype) for o in self.outs])
+
+
+class _Compiled:
+    """The function ``Backend.compile`` returns (CUDA graph per input signature)."""
+
+    def __init__(self, b: "CudaBackend", fn: Callable[..., Any]):
+        self.b, self.fn = b, fn
+        self.graphs: dict[tuple, _Graph] = {}
+
+    def __call__(self, *args):
+        b = self.b
+        sig = tuple((a.dtype, tuple(a.shape)) if isinstance(a, CudaTensor) else ("?", type(a).__name__) for a in args)
+        if not all(isinstance(a, CudaTensor) for a in args):
+            raise TypeError("compile: arguments must be tensors")
+        g = self.graphs.get(sig)
+        if g is not None:
+            return g.run(args)
+        result = self.fn(*args)  # the first call of a signature runs eagerly
+        self.graphs[sig] = self._record(args, result)
+        return result
+
+    def _record(self, args, result) -> _Graph:
+        b = self.b
+        flat, rebuild = _flatten(result)
+        zeros = lambda dt, sh: b.fromHost(HostTensor(dt, tuple(sh), np.zeros(tuple(sh), NP_STORAGE[dt])))
+        saved, b._scopes = b._scopes, []  # the graph's tensors belong to no caller scope
+        try:
+            ins = [zeros(a.dtype, a.shape) for a in args]
+            outs = [zeros(t.dtype, t.shape) for t in flat]
+            _lib.call("lc_graph_capture_begin")
+            try:
+                def body():
+                    views = [b.reshape(t, list(t.shape)) for t in ins]  # fn may dispose its arguments
+                    got, _ = _flatten(self.fn(*views))
+                    if [(t.dtype, tuple(t.shape)) for t in got] != [(t.dtype, tuple(t.shape)) for t in outs]:
+                        raise ValueError("compile: fn returned different outputs for the same input signature")
+                    for o, t in zip(outs, got):
+                        _lib.call("lc_copy_into", C.c_uint64(o.handle), C.c_uint64(t.handle))
+                    return None
+                b.scope(body)
+                h = C.c_uint64()
+                _lib.call("lc_graph_capture_end", C.byref(h))
+            except BaseException:
+                _lib.call("lc_graph_capture_abort")
+                for t in ins + outs:
+                    b.dispose(t)
+                raise
+        finally:
+            b._scopes = saved
+        return _Graph(b, h.value, ins, outs, rebuild)
 
 
 _BACKENDS: dict[int, CudaBackend] = {}

@@ -9,6 +9,7 @@
 #include "lc_gemm.h"
 
 #include <algorithm>
+#include <memory>
 #include <mutex>
 #include <unordered_map>
 #include <unordered_set>
@@ -25,6 +26,14 @@ struct State {
   std::unordered_set<LcTensor*> live;
   int64_t live_bytes = 0;
   int64_t launches = 0;
+  // stream capture (lc_graph_capture_*): allocations made while capturing
+  // become the graph's own (alloc nodes, freed by free nodes inside it);
+  // memory that existed before the capture and is released during it stays
+  // allocated until the graph is destroyed, since its kernels may read it.
+  int64_t alloc_cap = 0;  // lc_debug_set_alloc_cap: tensor bytes allowed at once (0 = no cap)
+  bool capturing = false;
+  std::unordered_set<void*> cap_allocs;
+  std::vector<void*> cap_deferred;
 };
 State& S() {
   static State s;
@@ -72,10 +81,19 @@ void* dmalloc(size_t bytes) {
     cudaGetLastError();
     fail("out of device memory allocating " + std::to_string(bytes) + " bytes (" + cudaGetErrorString(e) + ")");
   }
+  if (S().capturing) S().cap_allocs.insert(p);
   return p;
 }
 void dfree(void* p) {
-  if (p) cudaFreeAsync(p, S().cur);
+  if (!p) return;
+  State& s = S();
+  if (s.capturing) {
+    if (!s.cap_allocs.erase(p)) {
+      s.cap_deferred.push_back(p);
+      return;
+    }
+  }
+  cudaFreeAsync(p, s.cur);
 }
 
 LcTensor* check(uint64_t h, const char* what) {
@@ -108,8 +126,12 @@ static LcTensor* new_tensor(LcStorage* st, int dtype, const std::vector<int64_t>
 LcTensor* alloc(int dtype, const std::vector<int64_t>& shape) {
   int64_t n = 1;
   for (auto d : shape) n *= d;
+  const size_t bytes = (size_t)n * dtype_size(dtype);
+  if (S().alloc_cap && S().live_bytes + (int64_t)bytes > S().alloc_cap)
+    fail("out of device memory allocating " + std::to_string(bytes) + " bytes (the allocation cap of " +
+         std::to_string(S().alloc_cap) + " bytes would be exceeded)");
   LcStorage* st = new LcStorage();
-  st->bytes = (size_t)n * dtype_size(dtype);
+  st->bytes = bytes;
   st->ptr = dmalloc(st->bytes);
   S().live_bytes += (int64_t)st->bytes;
   return new_tensor(st, dtype, shape);
@@ -634,6 +656,173 @@ int lc_cast(lc_tensor* out, lc_tensor xh, int dtype) {
   LcTensor* y = alloc(dtype, x->dims());
   copy_into(x, y);
   *out = handle(y);
+  LC_API_END
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------- captured graphs (Backend.compile)
+//
+// The op sequence issued between lc_graph_capture_begin and _end is recorded
+// from the library stream into a CUDA graph and replayed by lc_graph_launch
+// on the same tensors' memory. Memory the captured ops allocate is the
+// graph's (stream-ordered alloc/free nodes); whatever a replay must hand
+// back has to be copied out to memory that existed before the capture
+// (lc_copy_into) and the captured tensors disposed before _end.
+
+namespace {
+constexpr uint64_t kGraphMagic = 0x4c43475241504831ull;
+struct LcGraph {
+  uint64_t magic = kGraphMagic;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  std::vector<void*> deferred;  // freed with the graph
+};
+std::unordered_set<LcGraph*>& graphs() {
+  static std::unordered_set<LcGraph*> g;
+  return g;
+}
+void end_capture_state(std::vector<void*>* keep) {
+  State& s = S();
+  s.capturing = false;
+  s.cap_allocs.clear();
+  if (keep) keep->swap(s.cap_deferred);
+  for (void* p : s.cap_deferred) cudaFreeAsync(p, s.cur);
+  s.cap_deferred.clear();
+}
+LcGraph* check_graph(uint64_t h) {
+  LcGraph* g = reinterpret_cast<LcGraph*>(h);
+  LC_CHECK(h && graphs().count(g) && g->magic == kGraphMagic, "graph: not a live graph handle");
+  return g;
+}
+}  // namespace
+
+extern "C" {
+
+int lc_graph_capture_begin(void) {
+  LC_API_BEGIN
+  ensure_init();
+  State& s = S();
+  LC_CHECK(!s.capturing, "graph capture: a capture is already in progress");
+  CUDA_OK(cudaStreamBeginCapture(s.cur, cudaStreamCaptureModeRelaxed));
+  s.capturing = true;
+  LC_API_END
+}
+
+int lc_graph_capture_end(uint64_t* out) {
+  LC_API_BEGIN
+  ensure_init();
+  State& s = S();
+  LC_CHECK(s.capturing, "graph capture: no capture in progress");
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s.cur, &graph);
+  const size_t unfreed = s.cap_allocs.size();
+  auto g = std::make_unique<LcGraph>();
+  end_capture_state(&g->deferred);
+  if (e != cudaSuccess || !graph || unfreed) {
+    cudaGetLastError();
+    if (graph) cudaGraphDestroy(graph);
+    for (void* p : g->deferred) cudaFreeAsync(p, s.cur);
+    if (e != cudaSuccess || !graph)
+      fail(std::string("graph capture failed: ") + cudaGetErrorString(e) +
+           " (an op synchronised with the host or used another stream while capturing)");
+    fail("graph capture: " + std::to_string(unfreed) + " allocations made while capturing were not released before the end");
+  }
+  g->graph = graph;
+  e = cudaGraphInstantiateWithFlags(&g->exec, graph, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cudaGraphDestroy(graph);
+    for (void* p : g->deferred) cudaFreeAsync(p, s.cur);
+    fail(std::string("graph instantiate failed: ") + cudaGetErrorString(e));
+  }
+  LcGraph* raw = g.release();
+  graphs().insert(raw);
+  *out = reinterpret_cast<uint64_t>(raw);
+  LC_API_END
+}
+
+int lc_graph_capture_abort(void) {
+  LC_API_BEGIN
+  ensure_init();
+  State& s = S();
+  if (!s.capturing) return 0;
+  cudaGraph_t graph = nullptr;
+  cudaStreamEndCapture(s.cur, &graph);
+  cudaGetLastError();
+  if (graph) cudaGraphDestroy(graph);
+  end_capture_state(nullptr);
+  LC_API_END
+}
+
+int lc_graph_launch(uint64_t h) {
+  LC_API_BEGIN
+  ensure_init();
+  LcGraph* g = check_graph(h);
+  LC_CHECK(!S().capturing, "graph launch: not allowed while capturing");
+  CUDA_OK(cudaGraphLaunch(g->exec, S().cur));
+  S().launches += 1;
+  LC_API_END
+}
+
+int lc_graph_destroy(uint64_t h) {
+  LC_API_BEGIN
+  ensure_init();
+  LcGraph* g = check_graph(h);
+  graphs().erase(g);
+  // launches already queued on the stream finish before the stream-ordered frees
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  for (void* p : g->deferred) cudaFreeAsync(p, S().cur);
+  g->magic = 0;
+  delete g;
+  LC_API_END
+}
+
+int lc_copy_into(lc_tensor dsth, lc_tensor srch) {
+  LC_API_BEGIN
+  LcTensor* dst = check(dsth, "copyInto dst");
+  LcTensor* src = check(srch, "copyInto src");
+  LC_CHECK(dst->dtype == src->dtype && dst->dims() == src->dims(),
+           "copyInto: dst " + std::string(dtype_name(dst->dtype)) + shape_str(dst->dims()) + " vs src " + dtype_name(src->dtype) +
+               shape_str(src->dims()));
+  LC_CHECK(dst->contiguous(), "copyInto: the destination must be dense");
+  copy_into(src, dst);
+  LC_API_END
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------- failure-path test hooks
+void lc_internal_wait_limit_gemm(unsigned long long ns);
+void lc_internal_wait_limit_attention(unsigned long long ns);
+void lc_internal_wait_limit_encoder(unsigned long long ns);
+void lc_internal_launch_wait_probe();
+
+extern "C" {
+
+int lc_debug_set_wait_limit(uint64_t ns) {
+  LC_API_BEGIN
+  ensure_init();
+  const unsigned long long v = ns ? (unsigned long long)ns : 2000000000ull;
+  lc_internal_wait_limit_gemm(v);
+  lc_internal_wait_limit_attention(v);
+  lc_internal_wait_limit_encoder(v);
+  LC_API_END
+}
+
+int lc_debug_set_alloc_cap(int64_t bytes) {
+  LC_API_BEGIN
+  ensure_init();
+  LC_CHECK(bytes >= 0, "allocation cap must be >= 0");
+  S().alloc_cap = bytes;
+  LC_API_END
+}
+
+int lc_debug_stuck_wait(void) {
+  LC_API_BEGIN
+  ensure_init();
+  lc_internal_launch_wait_probe();
   LC_API_END
 }
 

@@ -924,3 +924,6 @@ int lc_encoder_graph_free(uint64_t gh) {
 }
 
 }  // extern "C"
+
+// Sets this unit's bounded-wait limit (lc_debug_set_wait_limit).
+void lc_internal_wait_limit_encoder(unsigned long long ns) { CUDA_OK(cudaMemcpyToSymbol(sm100::g_wait_limit_ns, &ns, sizeof(ns))); }

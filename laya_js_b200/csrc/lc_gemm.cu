@@ -1516,6 +1516,8 @@ std::string take_device_errors() {
   return "tcgen05 GEMM: " + what + (msg.empty() ? std::string() : "; " + msg);
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
+
 const CUtensorMap& tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype) {
   return tensor_map(ptr, rows, cols, ld, box_cols, box_rows, dtype);
 }
@@ -1523,3 +1525,27 @@ const CUtensorMap& tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, in
 }  // namespace lc
 
 void lc_gemm_destroy_caches() { map_cache().clear(); }
+
+// Sets this unit's bounded-wait limit (lc_debug_set_wait_limit).
+void lc_internal_wait_limit_gemm(unsigned long long ns) { CUDA_OK(cudaMemcpyToSymbol(sm100::g_wait_limit_ns, &ns, sizeof(ns))); }
+
+// A kernel whose one wait nothing satisfies: it gives up after the bounded
+// wait's limit, records the timeout in the GEMM error word and returns, so
+// the host sees the error at its next lc_flush / lc_read while the context
+// stays usable. Only lc_debug_stuck_wait launches it.
+__global__ void k_wait_probe() {
+  __shared__ uint64_t bar;
+  __shared__ int abort;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) sm100::mbar_wait(&bar, 0, (volatile int*)&abort, &g_gemm_err);
+}
+
+void lc_internal_launch_wait_probe() {
+  k_wait_probe<<<1, 32, 0, lc::stream()>>>();
+  LC_LAUNCHED(1);
+}

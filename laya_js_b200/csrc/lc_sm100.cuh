@@ -9,6 +9,10 @@ namespace sm100 {
 // helpers are static: every translation unit gets its own copy
 
 constexpr uint64_t kWaitNs = 2000000000ull;  // every mbarrier wait gives up after 2 s
+// The limit the bounded waits use (kWaitNs unless lc_debug_set_wait_limit
+// shortened it, so a test can make a wait run out in a millisecond). One copy
+// per translation unit; each unit with such waits exports a setter.
+static __device__ unsigned long long g_wait_limit_ns = kWaitNs;
 
 static __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 static __device__ __forceinline__ uint64_t gtimer() {
@@ -44,7 +48,7 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63) == 63) {
       if (*abort) return false;
-      if (gtimer() - t0 > kWaitNs) {
+      if (gtimer() - t0 > g_wait_limit_ns) {
         *abort = 1;
         atomicOr(err, 1u);
         return false;
@@ -61,6 +65,13 @@ static __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap*
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+static __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 // Pull a tile of a tensor map into L2 (no shared-memory destination).

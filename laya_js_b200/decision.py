@@ -5,6 +5,7 @@ contract — the host-side mirror of packages/laya/src/model.ts:
 - ``DecisionModel.headLayer``    model.ts:124-137
 - ``DecisionModel.uploadBatch``  model.ts:146-170
 - ``DecisionModel.forwardCore``  model.ts:182-235
+- ``DecisionModel.compiled``     model.ts:250-272 (Backend.compile = CUDA graphs)
 - ``DecisionModel.readOutputs``  model.ts:275-285
 - ``loadDecisionModel``          model.ts:319-366 (+ buildHeadWeights :368-405)
 
@@ -145,6 +146,29 @@ class DecisionModel:
             return self.forwardCore(inp, onStage)
         finally:
             self.disposeInputs(inp)
+
+    def compiled(self) -> Optional[Callable[[dict], dict]]:
+        """model.ts:250-272: a ``forwardTensors`` equivalent through
+        ``backend.compile`` (here one CUDA graph per input shape signature),
+        or None when the backend has no ``compile``. No stage observation."""
+        b = self.backend
+        if not hasattr(b, "compile"):
+            return None
+        names = ("inputIds", "fullMask", "slidingMask", "headMask", "qtype", "markerPos", "markerMask", "k")
+
+        def core(*ts):
+            r = self.forwardCore(dict(zip(names, ts)))
+            return [r["logits"], r["act"]]
+        fn = b.compile(core)
+
+        def run(batch: dict) -> dict:
+            inp = self.uploadBatch(batch)
+            try:
+                logits, act = fn(*[inp[n] for n in names])
+                return {"logits": logits, "act": act}
+            finally:
+                self.disposeInputs(inp)
+        return run
 
     def readOutputs(self, r: dict) -> dict:
         """model.ts:275-285: flush, read both (f32), free."""

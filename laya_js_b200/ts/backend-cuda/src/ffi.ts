@@ -37,6 +37,8 @@ export const SYMBOLS: Record<string, A[]> = {
   lc_logical_and: OP2, lc_logical_or: OP2, lc_logical_not: OP1, lc_sqrt: OP1, lc_rsqrt: OP1, lc_pow: OP2,
   lc_neg: OP1, lc_abs: OP1, lc_tanh: OP1, lc_sigmoid: OP1, lc_erf: OP1,
   lc_argmax: RED, lc_argmin: RED, lc_mean: RED, lc_min: RED, lc_cumsum: ["p", "h", "i"],
+  lc_graph_capture_begin: [], lc_graph_capture_end: ["p"], lc_graph_capture_abort: [], lc_graph_launch: ["h"],
+  lc_graph_destroy: ["h"], lc_copy_into: ["h", "h"],
 };
 
 type Fn = (...a: unknown[]) => number;

@@ -174,6 +174,70 @@ export function createCudaBackend(opts: CudaBackendOptions = {}): Backend<CudaTe
     tanh: un("lc_tanh"), sigmoid: un("lc_sigmoid"), erf: un("lc_erf"),
     argmax: red("lc_argmax"), argmin: red("lc_argmin"), mean: red("lc_mean"), min: red("lc_min"),
     cumsum: (x: CudaTensor, axis: number) => op("lc_cumsum", H(x, "cumsum"), axis),
+
+    /**
+     * index.ts:244-245. CUDA-graph capture per input signature (dtypes and
+     * shapes): the first call of a signature runs `fn` eagerly, then records
+     * it on graph-owned input tensors; later calls copy their arguments in,
+     * replay the graph (one launch) and return copies of its outputs. `fn`
+     * must be pure in its tensor arguments (captured tensors are constants,
+     * as under backend-mlx's compile).
+     */
+    compile<A extends CudaTensor[], R>(fn: (...args: A) => R): (...args: A) => R {
+      type Rec = { graph: number; ins: CudaTensor[]; outs: CudaTensor[]; rebuild: (xs: CudaTensor[]) => R };
+      const recs = new Map<string, Rec>();
+      const flatten = (r: unknown): { flat: CudaTensor[]; rebuild: (xs: CudaTensor[]) => R } => {
+        if (r instanceof CudaTensor) return { flat: [r], rebuild: (xs) => xs[0] as R };
+        if (Array.isArray(r)) return { flat: r as CudaTensor[], rebuild: (xs) => xs as R };
+        if (r && typeof r === "object") {
+          const keys = Object.keys(r);
+          return { flat: keys.map((k) => (r as Record<string, CudaTensor>)[k]!), rebuild: (xs) => Object.fromEntries(keys.map((k, i) => [k, xs[i]])) as R };
+        }
+        throw new TypeError("compile: outputs must be a tensor, an array or an object of tensors");
+      };
+      const zeros = (t: CudaTensor) => {
+        const n = t.shape.reduce((a, d) => a * d, 1);
+        const data = allocHost(t.dtype, n) as ArrayBufferView;
+        return op("lc_from_host", CODE.get(t.dtype)!, shapeArg(t.shape), t.shape.length, data, data.byteLength);
+      };
+      const record = (args: A, result: R): Rec => {
+        const { flat, rebuild } = flatten(result);
+        const saved = scopes.splice(0, scopes.length);  // graph tensors belong to no caller scope
+        try {
+          const ins = args.map(zeros);
+          const outs = flat.map(zeros);
+          N.call("lc_graph_capture_begin");
+          try {
+            b.scope(() => {
+              const views = ins.map((t) => b.reshape(t, t.shape)) as unknown as A;
+              const got = flatten(fn(...views)).flat;
+              got.forEach((t, i) => N.call("lc_copy_into", outs[i]!.handle, H(t, "compile")));
+              return null;
+            });
+            N.call("lc_graph_capture_end", out);
+          } catch (e) {
+            N.call("lc_graph_capture_abort");
+            for (const t of [...ins, ...outs]) b.dispose(t);
+            throw e;
+          }
+          return { graph: Number(out[0]), ins, outs, rebuild };
+        } finally {
+          scopes.push(...saved);
+        }
+      };
+      return (...args: A): R => {
+        const sig = args.map((t) => `${t.dtype}[${t.shape.join(",")}]`).join(";");
+        const rec = recs.get(sig);
+        if (!rec) {
+          const result = fn(...args);
+          recs.set(sig, record(args, result));
+          return result;
+        }
+        rec.ins.forEach((slot, i) => N.call("lc_copy_into", slot.handle, H(args[i], "compiled call")));
+        N.call("lc_graph_launch", rec.graph);
+        return rec.rebuild(rec.outs.map((o) => b.cast(o, o.dtype)));
+      };
+    },
   };
   return b as unknown as Backend<CudaTensor> & { stats(): Record<string, number> };
 }
