@@ -34,6 +34,17 @@
 // Every barrier counts phases with per-role counters that run across work
 // items; every mbarrier wait is bounded (2 s); a timeout sets g_attn_err and
 // all roles unwind.
+//
+// MODE 0 / 1: the fused encoder's varlen attention (global / sliding window)
+// over the [T, 3H] projection. MODE 2: the contract's sdpa
+// (packages/tensor-backend/src/index.ts:230-237) on padded [B, nh, L, 64]
+// q / k / v views of any 16-byte strides, read through 4-D tensor maps, with
+// the bool mask (broadcast to [B, nh, Lq, Lk]) read per row and key block:
+// a pre-pass (k_mask_ranges) gives each (batch, mask head, query tile) the
+// range of key blocks holding a visible key, and only those are visited; the
+// output is written as [B, Lq, nh, 64] rows, which the caller returns as the
+// transposed [B, nh, Lq, 64] view (ModernBert.layer's transpose + reshape
+// back to [B, L, H] then moves no bytes).
 #include "lc_api.h"
 #include "lc_gemm.h"
 #include "lc_sm100.cuh"
@@ -57,27 +68,46 @@ constexpr size_t ATTN_SMEM = 2 * TILE_BYTES + 2 * NST * KV_BYTES + 1024 + 256;
 
 struct AttnTcArgs {
   const int4* tiles;  // (first token of the sequence, its length, first query row (multiple of 128), 0)
-  void* out;          // [T, H]
+  void* out;          // [T, H] (MODE 2: [B, Lq, nh, 64])
   int H;
   int half_window;  // < 0: global attention
   float scale_log2;
   int heads;
-  int nwork;  // tiles x heads
+  int nwork;  // tiles x heads (MODE 2: B x heads x query tiles)
+  // MODE 2 only
+  int Lq, Lk, nqt, mheads;
+  const uint8_t* mask;  // bool; element strides over [B, nh, Lq, Lk] (0 = broadcast); null = every key visible
+  long long ms[4];
+  const int2* ranges;  // per (b, mask head, query tile): first key block, block count (null: every block)
 };
 
 struct Work {
-  int tok0, L, q0, h, kv_lo, nb;
+  int tok0, L, q0, h, kv_lo, nb, b;
 };
 
-template <bool LOCAL>
+template <int MODE>
 __device__ __forceinline__ Work decode(const AttnTcArgs& a, int4 t, int w) {
   Work r;
+  if constexpr (MODE == 2) {
+    r.h = w % a.heads;
+    const int rest = w / a.heads, qt = rest % a.nqt;
+    r.b = rest / a.nqt;
+    r.tok0 = 0;
+    r.L = a.Lq;
+    r.q0 = qt * TQ;
+    const int2 rg = a.ranges ? a.ranges[((int64_t)r.b * a.mheads + (a.mheads > 1 ? r.h : 0)) * a.nqt + qt]
+                             : make_int2(0, (a.Lk + TK - 1) / TK);
+    r.kv_lo = rg.x * TK;
+    r.nb = max(rg.y, 1);  // a tile with no visible key still runs one (fully masked) block
+    return r;
+  }
+  r.b = 0;
   r.tok0 = t.x;
   r.L = t.y;
   r.q0 = t.z;
   r.h = w % a.heads;
   int lo = 0, hi = r.L;
-  if (LOCAL) {
+  if (MODE == 1) {
     lo = max(0, r.q0 - a.half_window);
     hi = min(r.L, r.q0 + TQ + a.half_window);
   }
@@ -88,27 +118,59 @@ __device__ __forceinline__ Work decode(const AttnTcArgs& a, int4 t, int w) {
 
 // One role's walk over this CTA's work items (w = blockIdx.x + t * gridDim.x);
 // the tile entry of the following item is loaded one item ahead.
-template <bool LOCAL>
+template <int MODE>
 struct Items {
   int w, t;
   Work cur;
   int4 next;
+  __device__ __forceinline__ int4 tile_of(const AttnTcArgs& a, int wi) const {
+    if constexpr (MODE == 2) return make_int4(0, 0, 0, 0);
+    return a.tiles[wi / a.heads];
+  }
   __device__ __forceinline__ void start(const AttnTcArgs& a) {
     w = blockIdx.x;
     t = 0;
-    if (w < a.nwork) cur = decode<LOCAL>(a, a.tiles[w / a.heads], w);
+    if (w < a.nwork) cur = decode<MODE>(a, tile_of(a, w), w);
     const int wn = w + (int)gridDim.x;
-    if (wn < a.nwork) next = a.tiles[wn / a.heads];
+    if (wn < a.nwork) next = tile_of(a, wn);
   }
   __device__ __forceinline__ bool valid(const AttnTcArgs& a) const { return w < a.nwork; }
   __device__ __forceinline__ void step(const AttnTcArgs& a) {
     w += gridDim.x;
     t++;
-    if (w < a.nwork) cur = decode<LOCAL>(a, next, w);
+    if (w < a.nwork) cur = decode<MODE>(a, next, w);
     const int wn = w + (int)gridDim.x;
-    if (wn < a.nwork) next = a.tiles[wn / a.heads];
+    if (wn < a.nwork) next = tile_of(a, wn);
   }
 };
+
+// Bit i set when byte i of w is nonzero (i < 4).
+__device__ __forceinline__ uint32_t nonzero_bits4(uint32_t w) { return ((__vcmpne4(w, 0u) & 0x01010101u) * 0x10204080u) >> 28; }
+
+// MODE 2: the visible keys of query row qi among keys kbase .. kbase+63 of
+// batch b / head h, as two 32-bit masks (bit i of vis[c] = key kbase + 32c + i).
+__device__ __forceinline__ void mask_bits(const AttnTcArgs& a, int b, int h, int qi, int kbase, uint32_t vis[2]) {
+  vis[0] = vis[1] = 0u;
+  if (qi >= a.Lq) return;
+  const int n = min(TK, a.Lk - kbase);
+  if (!a.mask) {
+    vis[0] = n >= 32 ? 0xffffffffu : (0xffffffffu >> (32 - n));
+    vis[1] = n >= 64 ? 0xffffffffu : (n > 32 ? (0xffffffffu >> (64 - n)) : 0u);
+    return;
+  }
+  const uint8_t* row = a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)qi * a.ms[2] + (int64_t)kbase * a.ms[3];
+  if (a.ms[3] == 1 && n == TK && (((uintptr_t)row) & 15) == 0) {
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      const uint4 u0 = __ldg((const uint4*)row + 2 * c), u1 = __ldg((const uint4*)row + 2 * c + 1);
+      vis[c] = nonzero_bits4(u0.x) | (nonzero_bits4(u0.y) << 4) | (nonzero_bits4(u0.z) << 8) | (nonzero_bits4(u0.w) << 12) |
+               (nonzero_bits4(u1.x) << 16) | (nonzero_bits4(u1.y) << 20) | (nonzero_bits4(u1.z) << 24) | (nonzero_bits4(u1.w) << 28);
+    }
+    return;
+  }
+  for (int i = 0; i < n; i++)
+    if (row[(int64_t)i * a.ms[3]]) vis[i >> 5] |= 1u << (i & 31);
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -131,9 +193,10 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
-template <typename T, bool LOCAL>
+template <typename T, int MODE>
 __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
-                                                    const __grid_constant__ AttnTcArgs a) {
+                                                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnTcArgs a) {
+  constexpr bool LOCAL = MODE == 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem;                 // 2 buffers
@@ -181,6 +244,7 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
   if (warp == 0 && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmQ) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmKV) : "memory");
+    if (MODE == 2) asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmV) : "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -195,13 +259,14 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
       for (int s = 0; s < NST; s++) issued[s] = 0, iph[s] = 0;
       uint32_t kv_it = 0;
       bool ok = true;
-      Items<LOCAL> it;
+      Items<MODE> it;
       for (it.start(a); ok && it.valid(a); it.step(a)) {
         const Work& wk = it.cur;
         const int t = it.t, qb = t & 1;
         if (!mbar_wait(&q_empty[qb], ((t >> 1) & 1) ^ 1, abort, &g_attn_err)) break;
         mbar_arrive_expect_tx(&q_full[qb], TILE_BYTES);
-        tma_load_2d(sQ + qb * TILE_BYTES, &tmQ, &q_full[qb], wk.h * HD, wk.tok0 + wk.q0);
+        if constexpr (MODE == 2) tma_load_4d(sQ + qb * TILE_BYTES, &tmQ, &q_full[qb], 0, wk.q0, wk.h, wk.b);
+        else tma_load_2d(sQ + qb * TILE_BYTES, &tmQ, &q_full[qb], wk.h * HD, wk.tok0 + wk.q0);
         q_issued[qb] = 1;
         q_ph[qb] = (t >> 1) & 1;
         for (int j = 0; j < wk.nb; j++, kv_it++) {
@@ -210,8 +275,13 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
           if (!mbar_wait(&kv_empty[st], ph ^ 1, abort, &g_attn_err)) { ok = false; break; }
           mbar_arrive_expect_tx(&kv_full[st], 2 * KV_BYTES);
           const int row = wk.tok0 + wk.kv_lo + j * TK;
-          tma_load_2d(sK + st * KV_BYTES, &tmKV, &kv_full[st], a.H + wk.h * HD, row);
-          tma_load_2d(sV + st * KV_BYTES, &tmKV, &kv_full[st], 2 * a.H + wk.h * HD, row);
+          if constexpr (MODE == 2) {
+            tma_load_4d(sK + st * KV_BYTES, &tmKV, &kv_full[st], 0, row, wk.h, wk.b);
+            tma_load_4d(sV + st * KV_BYTES, &tmV, &kv_full[st], 0, row, wk.h, wk.b);
+          } else {
+            tma_load_2d(sK + st * KV_BYTES, &tmKV, &kv_full[st], a.H + wk.h * HD, row);
+            tma_load_2d(sV + st * KV_BYTES, &tmKV, &kv_full[st], 2 * a.H + wk.h * HD, row);
+          }
           issued[st] = 1;
           iph[st] = ph;
         }
@@ -240,7 +310,7 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
       const uint64_t dq0 = sdesc_sw128(smem_u32(sQ)), dk0 = sdesc_sw128(smem_u32(sK)), dv0 = sdesc_sw128_mn(smem_u32(sV));
       uint64_t* last_bar = nullptr;  // the barrier of the most recent commit, for the drain
       uint32_t last_ph = 0;
-      Items<LOCAL> si, pi;  // S cursor and P·V cursor
+      Items<MODE> si, pi;  // S cursor and P·V cursor
       si.start(a);
       pi.start(a);
       int sj = 0, pj = 0;
@@ -332,7 +402,7 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
       pend = false;
       return true;
     };
-    Items<LOCAL> it;
+    Items<MODE> it;
     for (it.start(a); ok && it.valid(a); it.step(a)) {
       const Work& wk = it.cur;
       const int qi = wk.q0 + row;
@@ -349,23 +419,32 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
         const int hi = (LOCAL ? min(wk.L - 1, qi + a.half_window) : wk.L - 1) - kbase;
         // per 32-key chunk, warp-uniform: live = some row sees a key of it; full = every row sees all of it
         bool live[TK / 32], full[TK / 32];
-#pragma unroll
-        for (int c = 0; c < TK / 32; c++) {
-          const int c0 = c * 32, c1 = c0 + 31;
-          if (LOCAL) {
-            live[c] = warp_live && __any_sync(0xffffffffu, c1 >= lo && c0 <= hi);
-            full[c] = __all_sync(0xffffffffu, c0 >= lo && c1 <= hi);
-          } else {  // every row sees keys [0, L): lo <= 0 and hi are the same for the whole warp
-            live[c] = warp_live && c0 <= hi;
-            full[c] = c1 <= hi;
-          }
-        }
         // per chunk, this row's visible keys as a bit mask (bit i = key c·32 + i of the block)
         uint32_t vis[TK / 32];
+        if constexpr (MODE == 2) {
+          mask_bits(a, wk.b, wk.h, qi, kbase, vis);
 #pragma unroll
-        for (int c = 0; c < TK / 32; c++) {
-          const int a0 = max(lo - c * 32, 0), a1 = min(hi - c * 32, 31);
-          vis[c] = a0 <= a1 ? ((0xffffffffu >> (31 - a1)) & (0xffffffffu << a0)) : 0u;
+          for (int c = 0; c < TK / 32; c++) {
+            live[c] = warp_live && __any_sync(0xffffffffu, vis[c] != 0u);
+            full[c] = __all_sync(0xffffffffu, vis[c] == 0xffffffffu);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < TK / 32; c++) {
+            const int c0 = c * 32, c1 = c0 + 31;
+            if (LOCAL) {
+              live[c] = warp_live && __any_sync(0xffffffffu, c1 >= lo && c0 <= hi);
+              full[c] = __all_sync(0xffffffffu, c0 >= lo && c1 <= hi);
+            } else {  // every row sees keys [0, L): lo <= 0 and hi are the same for the whole warp
+              live[c] = warp_live && c0 <= hi;
+              full[c] = c1 <= hi;
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < TK / 32; c++) {
+            const int a0 = max(lo - c * 32, 0), a1 = min(hi - c * 32, 31);
+            vis[c] = a0 <= a1 ? ((0xffffffffu >> (31 - a1)) & (0xffffffffu << a0)) : 0u;
+          }
         }
         float s[TK];
         {
@@ -463,8 +542,11 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
       pend = true;
       pend_gl = g + wk.nb - 1;
       pend_ocol = ocol;
-      pend_inv = 1.f / l;
-      pend_out = qi < wk.L ? (T*)a.out + ((int64_t)wk.tok0 + qi) * a.H + wk.h * HD : nullptr;
+      pend_inv = l > 0.f ? 1.f / l : 0.f;  // a row with no visible key (undefined by the contract) gives zeros
+      if constexpr (MODE == 2)
+        pend_out = qi < wk.L ? (T*)a.out + (((int64_t)wk.b * a.Lq + qi) * a.heads + wk.h) * HD : nullptr;
+      else
+        pend_out = qi < wk.L ? (T*)a.out + ((int64_t)wk.tok0 + qi) * a.H + wk.h * HD : nullptr;
       g += wk.nb;
     }
     if (ok && pend) flush();
@@ -477,15 +559,50 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
   }
 }
 
-template <typename T, bool LOCAL>
-void launch_attn(const CUtensorMap& mq, const CUtensorMap& mkv, const AttnTcArgs& a, cudaStream_t st) {
+template <typename T, int MODE>
+void launch_attn(const CUtensorMap& mq, const CUtensorMap& mkv, const CUtensorMap& mv, const AttnTcArgs& a, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    CUDA_OK(cudaFuncSetAttribute(k_attn_tc<T, LOCAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTN_SMEM));
+    CUDA_OK(cudaFuncSetAttribute(k_attn_tc<T, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTN_SMEM));
     attr = true;
   }
   const int grid = std::min(a.nwork, 2 * lc::num_sms());  // persistent: two CTAs per SM
-  lc::launch_chain(k_attn_tc<T, LOCAL>, dim3((unsigned)grid), dim3(192), ATTN_SMEM, st, mq, mkv, a);
+  lc::launch_chain(k_attn_tc<T, MODE>, dim3((unsigned)grid), dim3(192), ATTN_SMEM, st, mq, mkv, mv, a);
+}
+
+// MODE 2 pre-pass: for each (batch, mask head, 128-row query tile) the first
+// key block holding a key visible to some row of the tile and the number of
+// blocks up to the last such block (0 when no row sees any key). One
+// 128-thread block per tile, thread = query row.
+__global__ void __launch_bounds__(TQ) k_mask_ranges(const uint8_t* mask, long long s0, long long s1, long long s2, long long s3, int mheads,
+                                                    int Lq, int Lk, int nqt, int2* ranges) {
+  const int item = blockIdx.x;  // (b * mheads + mh) * nqt + qt
+  const int qt = item % nqt, bm = item / nqt, mh = bm % mheads, b = bm / mheads;
+  const int qi = qt * TQ + (int)threadIdx.x;
+  int first = INT_MAX, last = -1;
+  if (qi < Lq) {
+    const uint8_t* row = mask + (int64_t)b * s0 + (int64_t)mh * s1 + (int64_t)qi * s2;
+    for (int j = 0; j < Lk; j++)
+      if (row[(int64_t)j * s3]) {
+        first = j;
+        break;
+      }
+    for (int j = Lk - 1; j >= first && first != INT_MAX; j--)
+      if (row[(int64_t)j * s3]) {
+        last = j;
+        break;
+      }
+  }
+  __shared__ int lo_s, hi_s;
+  if (threadIdx.x == 0) lo_s = INT_MAX, hi_s = -1;
+  __syncthreads();
+  if (first != INT_MAX) atomicMin(&lo_s, first);
+  if (last >= 0) atomicMax(&hi_s, last);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (hi_s < 0) ranges[item] = make_int2(0, 0);
+    else ranges[item] = make_int2(lo_s / TK, hi_s / TK - lo_s / TK + 1);
+  }
 }
 
 }  // namespace
@@ -514,15 +631,93 @@ void attention_varlen_tc(const void* qkv, void* out, const int4* tiles_dev, int 
   const CUtensorMap& mkv = tensor_map_2d(qkv, T, 3 * (int64_t)H, 3 * (int64_t)H, 64, TK, dtype);
   const int heads = H / HD;
   LC_CHECK((int64_t)ntiles * heads < INT32_MAX, "attention: too many work items");
-  AttnTcArgs a{tiles_dev, out, H, half_window, scale * 1.4426950408889634f, heads, ntiles * heads};
+  AttnTcArgs a{};
+  a.tiles = tiles_dev;
+  a.out = out;
+  a.H = H;
+  a.half_window = half_window;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.heads = heads;
+  a.nwork = ntiles * heads;
   if (dtype == LC_F16) {
-    if (half_window >= 0) launch_attn<__half, true>(mq, mkv, a, st);
-    else launch_attn<__half, false>(mq, mkv, a, st);
+    if (half_window >= 0) launch_attn<__half, 1>(mq, mkv, mkv, a, st);
+    else launch_attn<__half, 0>(mq, mkv, mkv, a, st);
   } else {
-    if (half_window >= 0) launch_attn<__nv_bfloat16, true>(mq, mkv, a, st);
-    else launch_attn<__nv_bfloat16, false>(mq, mkv, a, st);
+    if (half_window >= 0) launch_attn<__nv_bfloat16, 1>(mq, mkv, mkv, a, st);
+    else launch_attn<__nv_bfloat16, 0>(mq, mkv, mkv, a, st);
   }
   LC_LAUNCHED(1);
+}
+
+namespace {
+// 4-D map over a [B, nh, L, 64] view (element strides s[0..2] for B, nh, L;
+// innermost stride 1): dims (64, L, nh, B), box 64 x rows x 1 x 1, 128-byte swizzle.
+bool map_bhld(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t nh, int64_t L, const int64_t* s, int rows) {
+  for (int i = 0; i < 3; i++)
+    if ((s[i] * 2) % 16 || s[i] <= 0 || s[i] * 2 >= ((int64_t)1 << 40)) return false;
+  if (((uintptr_t)ptr) & 15) return false;
+  cuuint64_t dims[4] = {64, (cuuint64_t)L, (cuuint64_t)nh, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(s[2] * 2), (cuuint64_t)(s[1] * 2), (cuuint64_t)(s[0] * 2)};
+  cuuint32_t box[4] = {64, (cuuint32_t)rows, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = tensor_map_encoder()(m, dtype == LC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                                    const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+}  // namespace
+
+bool sdpa_tc(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor** out) {
+  if (!is_half(q->dtype) || k->dtype != q->dtype || v->dtype != q->dtype) return false;
+  const int64_t B = q->shape[0], nh = q->shape[1], Lq = q->shape[2], Lk = k->shape[2];
+  if (q->shape[3] != HD || k->shape[3] != HD || v->shape[3] != HD || Lq < 1 || Lk < 1) return false;
+  if (Lq > INT32_MAX / 2 || Lk > INT32_MAX / 2 || B * nh > INT32_MAX || nh > INT32_MAX) return false;
+  for (const LcTensor* t : {q, k, v})
+    if (t->strides[3] != 1) return false;
+  CUtensorMap mq, mk, mv;
+  if (!map_bhld(&mq, q->data(), q->dtype, B, nh, Lq, q->strides, TQ) || !map_bhld(&mk, k->data(), k->dtype, B, nh, Lk, k->strides, TK) ||
+      !map_bhld(&mv, v->data(), v->dtype, B, nh, Lk, v->strides, TK))
+    return false;
+  const int64_t nqt = (Lq + TQ - 1) / TQ;
+  if (B * nh * nqt >= INT32_MAX) return false;
+  AttnTcArgs a{};
+  a.heads = (int)nh;
+  a.H = (int)(nh * HD);
+  a.half_window = -1;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.Lq = (int)Lq;
+  a.Lk = (int)Lk;
+  a.nqt = (int)nqt;
+  a.nwork = (int)(B * nh * nqt);
+  TV mtv{};
+  int mheads = 1;
+  if (m) {
+    mtv = tv_broadcast(m, {B, nh, Lq, Lk});
+    a.mask = (const uint8_t*)mtv.ptr;
+    for (int i = 0; i < 4; i++) a.ms[i] = mtv.strides[i];
+    mheads = mtv.strides[1] == 0 ? 1 : (int)nh;
+  }
+  a.mheads = mheads;
+  cudaStream_t st = stream();
+  // key-block ranges per (batch, mask head, query tile); without a mask every block
+  const int64_t nranges = B * mheads * nqt;
+  int2* ranges = nullptr;
+  if (m) {
+    ranges = (int2*)dmalloc((size_t)nranges * sizeof(int2));
+    k_mask_ranges<<<(unsigned)nranges, TQ, 0, st>>>(a.mask, a.ms[0], a.ms[1], a.ms[2], a.ms[3], mheads, (int)Lq, (int)Lk, (int)nqt, ranges);
+    LC_LAUNCHED(1);
+  }
+  a.ranges = ranges;
+  // output rows [B, Lq, nh, 64], returned as the [B, nh, Lq, 64] view
+  LcTensor* y = alloc(q->dtype, {B, Lq, nh, HD});
+  a.out = y->data();
+  if (q->dtype == LC_F16) launch_attn<__half, 2>(mq, mk, mv, a, st);
+  else launch_attn<__nv_bfloat16, 2>(mq, mk, mv, a, st);
+  LC_LAUNCHED(1);
+  if (ranges) dfree(ranges);
+  *out = view_of(y, {B, nh, Lq, HD}, {Lq * nh * HD, HD, nh * HD, 1}, 0);
+  release(y);
+  return true;
 }
 
 std::string take_attention_errors() {
@@ -534,3 +729,6 @@ std::string take_attention_errors() {
 }
 
 }  // namespace lc
+
+// Sets this unit's bounded-wait limit (lc_debug_set_wait_limit).
+void lc_internal_wait_limit_attention(unsigned long long ns) { CUDA_OK(cudaMemcpyToSymbol(sm100::g_wait_limit_ns, &ns, sizeof(ns))); }

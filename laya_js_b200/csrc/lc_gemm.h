@@ -1,6 +1,7 @@
 // Tensor-core GEMM (tcgen05 + TMA, sm_100a) and related internal entry points.
 #pragma once
 #include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "lc_common.cuh"
 
@@ -74,6 +75,12 @@ std::string take_device_errors();
 std::string take_attention_errors();
 // Cached 2-D tiled tensor map (128-byte swizzle) over a row-major [rows, cols] matrix with row stride ld.
 const CUtensorMap& tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype);
+// The driver's cuTensorMapEncodeTiled (for maps of other ranks than tensor_map_2d's).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+// The contract's sdpa on the tcgen05 attention kernel (lc_attention_tc.cu) for
+// f16/bf16 head dim 64 with 16-byte strides; *out is a new [B, nh, Lq, 64]
+// view. False, with nothing launched, otherwise.
+bool sdpa_tc(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor** out);
 // tcgen05 varlen attention (lc_attention_tc.cu) and its 128-row tile list.
 std::vector<int4> attention_tiles_tc(const int32_t* cu, int nseq);
 void attention_varlen_tc(const void* qkv, void* out, const int4* tiles_dev, int ntiles, int64_t T, int H, int half_window, float scale,

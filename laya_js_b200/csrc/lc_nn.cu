@@ -845,6 +845,12 @@ int lc_sdpa(lc_tensor* out, lc_tensor qh, lc_tensor kh, lc_tensor vh, lc_tensor 
   if (B * H * Lq && Dv) {
     TV mv{};
     if (m) mv = tv_broadcast(m, {B, H, Lq, Lk});
+    LcTensor* ytc = nullptr;
+    if (odt == q->dtype && lc::sdpa_tc(q, k, v, m, (float)scale, &ytc)) {  // f16/bf16, head dim 64: tcgen05
+      release(y);
+      *out = handle(ytc);
+      return 0;
+    }
     if (lc::sdpa_flash(q, k, v, m, (float)scale, y)) {
       *out = handle(y);
       return 0;

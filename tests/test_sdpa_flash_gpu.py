@@ -1,5 +1,6 @@
 """The contract's sdpa (index.ts:230-237) on its tensor-core path — f16/bf16,
-head dim 64 — against the oracle: no mask, the attentionMasks padding
+head dim 64: the tcgen05 attention kernel (lc_attention_tc.cu, batched mode
+with the bool mask read per key block) — against the oracle: no mask, the attentionMasks padding
 [B,1,1,L] and sliding [B,1,L,L] masks (packages/modernbert/src/index.ts:240-259),
 an arbitrary [B,H,Lq,Lk] mask, Lq != Lk, lengths off the 64-row tiles, and q/k/v
 as the strided views ModernBert.layer makes (reshape -> transpose -> split of the
@@ -76,3 +77,38 @@ def test_sdpa_strided_views_and_unequal_lengths(dt):
     got = to_f32(b.read(b.sdpa(qs, k, v, None, 0.125)))
     want = O.sdpa(r[0][:, :, 10:75], r[1], r[2], None, 0.125)
     assert np.abs(got - want).max() < TOL[dt]
+
+
+def _dense(t) -> bool:
+    import ctypes as C
+    from laya_js_b200 import _lib
+    d = C.c_uint64()
+    _lib.call("lc_tensor_data", C.c_uint64(t.handle), C.byref(d))
+    return d.value != 0
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_sdpa_tcgen05_long_padded_batch(dt):
+    """ModernBERT-base shape (12 heads) at 600 positions with padding: the
+    sliding mask leaves most key blocks of a query tile empty (skipped by the
+    kernel's per-tile key-block ranges); the result is the [B, nh, L, 64]
+    view of [B, L, nh, 64] rows that the tcgen05 path writes."""
+    b = backend()
+    rng = np.random.default_rng(13)
+    B, L, nh = 2, 600, 12
+    qkv, qkvr = _up(b, rng.standard_normal((B, L, 3 * nh * 64)), dt)
+    t = b.transpose(b.reshape(qkv, [B, L, 3, nh, 64]), [2, 0, 3, 1, 4])
+    q, k, v = [b.reshape(x, [B, nh, L, 64]) for x in b.split(t, 3, 0)]
+    valid = np.ones((B, L), bool)
+    valid[1, 451:] = False
+    r = qkvr.reshape(B, L, 3, nh, 64).transpose(2, 0, 3, 1, 4)
+    for mask in M.attention_masks(valid, 128):
+        out = b.sdpa(q, k, v, b.fromHost(HostTensor("bool", mask.shape, mask.astype(np.uint8))), 0.125)
+        assert out.shape == (B, nh, L, 64) and not _dense(out), "expected the tcgen05 path's [B, L, nh, 64] rows"
+        # the layer's transpose + reshape back to [B, L, H] is a view of those rows
+        merged = b.reshape(b.transpose(out, [0, 2, 1, 3]), [B, L, nh * 64])
+        assert _dense(merged)
+        got = to_f32(b.read(out))
+        want = O.sdpa(r[0], r[1], r[2], mask, 0.125)
+        err = np.abs(got - want).max()
+        assert err < TOL[dt], f"{dt}: max err {err}"
