@@ -39,9 +39,12 @@
 // over the [T, 3H] projection. MODE 2: the contract's sdpa
 // (packages/tensor-backend/src/index.ts:230-237) on padded [B, nh, L, 64]
 // q / k / v views of any 16-byte strides, read through 4-D tensor maps, with
-// the bool mask (broadcast to [B, nh, Lq, Lk]) read per row and key block:
-// a pre-pass (k_mask_ranges) gives each (batch, mask head, query tile) the
-// range of key blocks holding a visible key, and only those are visited; the
+// the bool mask (broadcast to [B, nh, Lq, Lk]) packed by a pre-pass
+// (k_mask_pack) into one bit per key — rows [B][mask heads][mask rows][Lk/32]
+// words, 8x fewer bytes than the mask — together with each (batch, mask head,
+// query tile)'s range of key blocks holding a visible key; only those blocks
+// are visited, and each softmax thread loads its row's two words of the next
+// block while it works on the current one; the
 // output is written as [B, Lq, nh, 64] rows, which the caller returns as the
 // transposed [B, nh, Lq, 64] view (ModernBert.layer's transpose + reshape
 // back to [B, L, H] then moves no bytes).
@@ -50,6 +53,7 @@
 #include "lc_sm100.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 __device__ unsigned int g_attn_err;
 
@@ -76,9 +80,10 @@ struct AttnTcArgs {
   int nwork;  // tiles x heads (MODE 2: B x heads x query tiles)
   // MODE 2 only
   int Lq, Lk, nqt, mheads;
-  const uint8_t* mask;  // bool; element strides over [B, nh, Lq, Lk] (0 = broadcast); null = every key visible
-  long long ms[4];
-  const int2* ranges;  // per (b, mask head, query tile): first key block, block count (null: every block)
+  const uint32_t* mbits;  // visible-key bits [B][mheads][mrows][mwords] (bit i of word w = key 32w + i); null = every key visible
+  int mrows, mwords;      // mask rows: Lq, or 1 when the mask is the same for every query
+  const int2* ranges;     // per (b, mask head, query tile, or one per (b, mask head) when mrows == 1): first key block,
+                          // block count (null: every block)
 };
 
 struct Work {
@@ -95,8 +100,8 @@ __device__ __forceinline__ Work decode(const AttnTcArgs& a, int4 t, int w) {
     r.tok0 = 0;
     r.L = a.Lq;
     r.q0 = qt * TQ;
-    const int2 rg = a.ranges ? a.ranges[((int64_t)r.b * a.mheads + (a.mheads > 1 ? r.h : 0)) * a.nqt + qt]
-                             : make_int2(0, (a.Lk + TK - 1) / TK);
+    const int64_t bm = (int64_t)r.b * a.mheads + (a.mheads > 1 ? r.h : 0);
+    const int2 rg = a.ranges ? a.ranges[a.mrows > 1 ? bm * a.nqt + qt : bm] : make_int2(0, (a.Lk + TK - 1) / TK);
     r.kv_lo = rg.x * TK;
     r.nb = max(rg.y, 1);  // a tile with no visible key still runs one (fully masked) block
     return r;
@@ -147,29 +152,17 @@ struct Items {
 // Bit i set when byte i of w is nonzero (i < 4).
 __device__ __forceinline__ uint32_t nonzero_bits4(uint32_t w) { return ((__vcmpne4(w, 0u) & 0x01010101u) * 0x10204080u) >> 28; }
 
-// MODE 2: the visible keys of query row qi among keys kbase .. kbase+63 of
-// batch b / head h, as two 32-bit masks (bit i of vis[c] = key kbase + 32c + i).
-__device__ __forceinline__ void mask_bits(const AttnTcArgs& a, int b, int h, int qi, int kbase, uint32_t vis[2]) {
-  vis[0] = vis[1] = 0u;
-  if (qi >= a.Lq) return;
-  const int n = min(TK, a.Lk - kbase);
-  if (!a.mask) {
-    vis[0] = n >= 32 ? 0xffffffffu : (0xffffffffu >> (32 - n));
-    vis[1] = n >= 64 ? 0xffffffffu : (n > 32 ? (0xffffffffu >> (64 - n)) : 0u);
-    return;
+// MODE 2: the two visibility words of query row qi (batch b, head h) for the
+// key block starting at kbase (bit i of word c = key kbase + 32c + i).
+__device__ __forceinline__ uint2 mask_words(const AttnTcArgs& a, int b, int h, int qi, int kbase) {
+  if (qi >= a.Lq) return make_uint2(0u, 0u);
+  if (!a.mbits) {
+    const int n = min(TK, a.Lk - kbase);
+    return make_uint2(n >= 32 ? 0xffffffffu : (0xffffffffu >> (32 - n)), n >= 64 ? 0xffffffffu : (n > 32 ? (0xffffffffu >> (64 - n)) : 0u));
   }
-  const uint8_t* row = a.mask + (int64_t)b * a.ms[0] + (int64_t)h * a.ms[1] + (int64_t)qi * a.ms[2] + (int64_t)kbase * a.ms[3];
-  if (a.ms[3] == 1 && n == TK && (((uintptr_t)row) & 15) == 0) {
-#pragma unroll
-    for (int c = 0; c < 2; c++) {
-      const uint4 u0 = __ldg((const uint4*)row + 2 * c), u1 = __ldg((const uint4*)row + 2 * c + 1);
-      vis[c] = nonzero_bits4(u0.x) | (nonzero_bits4(u0.y) << 4) | (nonzero_bits4(u0.z) << 8) | (nonzero_bits4(u0.w) << 12) |
-               (nonzero_bits4(u1.x) << 16) | (nonzero_bits4(u1.y) << 20) | (nonzero_bits4(u1.z) << 24) | (nonzero_bits4(u1.w) << 28);
-    }
-    return;
-  }
-  for (int i = 0; i < n; i++)
-    if (row[(int64_t)i * a.ms[3]]) vis[i >> 5] |= 1u << (i & 31);
+  const uint32_t* row = a.mbits + (((int64_t)b * a.mheads + (a.mheads > 1 ? h : 0)) * a.mrows + (a.mrows > 1 ? qi : 0)) * a.mwords;
+  const int w = kbase >> 5;
+  return make_uint2(__ldg(row + w), w + 1 < a.mwords ? __ldg(row + w + 1) : 0u);
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -409,6 +402,8 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
       const uint32_t ocol = O_COL + (it.t & 1) * HD;
       const bool warp_live = wk.q0 + quarter * 32 < wk.L;  // warps wholly past the sequence end skip their exps
       float m = -INFINITY, l = 0.f;
+      uint2 mw_next = make_uint2(0u, 0u);  // MODE 2: this row's visibility words of the next block
+      if constexpr (MODE == 2) mw_next = mask_words(a, wk.b, wk.h, qi, wk.kv_lo);
       for (int j = 0; j < wk.nb; j++) {
         const uint32_t gj = g + j, b = gj % NS;
         if (!mbar_wait(&s_full[b], (gj / NS) & 1, abort, &g_attn_err)) { ok = false; break; }
@@ -422,7 +417,9 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
         // per chunk, this row's visible keys as a bit mask (bit i = key c·32 + i of the block)
         uint32_t vis[TK / 32];
         if constexpr (MODE == 2) {
-          mask_bits(a, wk.b, wk.h, qi, kbase, vis);
+          vis[0] = mw_next.x;
+          vis[1] = mw_next.y;
+          if (j + 1 < wk.nb) mw_next = mask_words(a, wk.b, wk.h, qi, kbase + TK);  // in flight during this block
 #pragma unroll
           for (int c = 0; c < TK / 32; c++) {
             live[c] = warp_live && __any_sync(0xffffffffu, vis[c] != 0u);
@@ -570,28 +567,39 @@ void launch_attn(const CUtensorMap& mq, const CUtensorMap& mkv, const CUtensorMa
   lc::launch_chain(k_attn_tc<T, MODE>, dim3((unsigned)grid), dim3(192), ATTN_SMEM, st, mq, mkv, mv, a);
 }
 
-// MODE 2 pre-pass: for each (batch, mask head, 128-row query tile) the first
-// key block holding a key visible to some row of the tile and the number of
-// blocks up to the last such block (0 when no row sees any key). One
-// 128-thread block per tile, thread = query row.
-__global__ void __launch_bounds__(TQ) k_mask_ranges(const uint8_t* mask, long long s0, long long s1, long long s2, long long s3, int mheads,
-                                                    int Lq, int Lk, int nqt, int2* ranges) {
-  const int item = blockIdx.x;  // (b * mheads + mh) * nqt + qt
-  const int qt = item % nqt, bm = item / nqt, mh = bm % mheads, b = bm / mheads;
-  const int qi = qt * TQ + (int)threadIdx.x;
+// MODE 2 pre-pass: packs the bool mask (element strides s0..s3 over
+// [B, nh, Lq, Lk], 0 where broadcast) into visibility bits [B][mheads][mrows][mwords]
+// and records, for each 128-row group of mask rows (a query tile, or the one
+// row when mrows == 1), the first key block holding a key visible to some row
+// of the group and the number of blocks up to the last such block (0: none).
+// One 128-thread block per (b, mask head, row group), thread = mask row.
+__global__ void __launch_bounds__(TQ) k_mask_pack(const uint8_t* mask, long long s0, long long s1, long long s2, long long s3, int mheads,
+                                                  int mrows, int Lk, int mwords, uint32_t* bits, int2* ranges) {
+  const int ngroups = (mrows + TQ - 1) / TQ;
+  const int gi = blockIdx.x % ngroups, bm = blockIdx.x / ngroups, mh = bm % mheads, b = bm / mheads;
+  const int r = gi * TQ + (int)threadIdx.x;
   int first = INT_MAX, last = -1;
-  if (qi < Lq) {
-    const uint8_t* row = mask + (int64_t)b * s0 + (int64_t)mh * s1 + (int64_t)qi * s2;
-    for (int j = 0; j < Lk; j++)
-      if (row[(int64_t)j * s3]) {
-        first = j;
-        break;
+  if (r < mrows) {
+    const uint8_t* row = mask + (int64_t)b * s0 + (int64_t)mh * s1 + (int64_t)r * s2;
+    uint32_t* out = bits + ((int64_t)bm * mrows + r) * mwords;
+    const bool vec = s3 == 1 && (((uintptr_t)row) & 15) == 0;
+    for (int w = 0; w < mwords; w++) {
+      const int k0 = w * 32;
+      uint32_t v = 0;
+      if (vec && k0 + 32 <= Lk) {
+        const uint4 u0 = __ldg((const uint4*)(row + k0)), u1 = __ldg((const uint4*)(row + k0) + 1);
+        v = nonzero_bits4(u0.x) | (nonzero_bits4(u0.y) << 4) | (nonzero_bits4(u0.z) << 8) | (nonzero_bits4(u0.w) << 12) |
+            (nonzero_bits4(u1.x) << 16) | (nonzero_bits4(u1.y) << 20) | (nonzero_bits4(u1.z) << 24) | (nonzero_bits4(u1.w) << 28);
+      } else {
+        for (int i = 0; i < 32 && k0 + i < Lk; i++)
+          if (row[(int64_t)(k0 + i) * s3]) v |= 1u << i;
       }
-    for (int j = Lk - 1; j >= first && first != INT_MAX; j--)
-      if (row[(int64_t)j * s3]) {
-        last = j;
-        break;
+      out[w] = v;
+      if (v) {
+        if (first == INT_MAX) first = k0 + __ffs(v) - 1;
+        last = k0 + 31 - __clz(v);
       }
+    }
   }
   __shared__ int lo_s, hi_s;
   if (threadIdx.x == 0) lo_s = INT_MAX, hi_s = -1;
@@ -600,8 +608,8 @@ __global__ void __launch_bounds__(TQ) k_mask_ranges(const uint8_t* mask, long lo
   if (last >= 0) atomicMax(&hi_s, last);
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (hi_s < 0) ranges[item] = make_int2(0, 0);
-    else ranges[item] = make_int2(lo_s / TK, hi_s / TK - lo_s / TK + 1);
+    if (hi_s < 0) ranges[blockIdx.x] = make_int2(0, 0);
+    else ranges[blockIdx.x] = make_int2(lo_s / TK, hi_s / TK - lo_s / TK + 1);
   }
 }
 
@@ -667,7 +675,18 @@ bool map_bhld(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t nh,
 }
 }  // namespace
 
+// LAYA_CUDA_SDPA_TC=0 keeps the contract's sdpa on the mma.sync kernel.
+static bool sdpa_tc_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("LAYA_CUDA_SDPA_TC");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 bool sdpa_tc(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTensor* m, float scale, LcTensor** out) {
+  if (!sdpa_tc_enabled()) return false;
   if (!is_half(q->dtype) || k->dtype != q->dtype || v->dtype != q->dtype) return false;
   const int64_t B = q->shape[0], nh = q->shape[1], Lq = q->shape[2], Lk = k->shape[2];
   if (q->shape[3] != HD || k->shape[3] != HD || v->shape[3] != HD || Lq < 1 || Lk < 1) return false;
@@ -689,24 +708,31 @@ bool sdpa_tc(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTe
   a.Lk = (int)Lk;
   a.nqt = (int)nqt;
   a.nwork = (int)(B * nh * nqt);
-  TV mtv{};
-  int mheads = 1;
-  if (m) {
-    mtv = tv_broadcast(m, {B, nh, Lq, Lk});
-    a.mask = (const uint8_t*)mtv.ptr;
-    for (int i = 0; i < 4; i++) a.ms[i] = mtv.strides[i];
-    mheads = mtv.strides[1] == 0 ? 1 : (int)nh;
-  }
-  a.mheads = mheads;
   cudaStream_t st = stream();
-  // key-block ranges per (batch, mask head, query tile); without a mask every block
-  const int64_t nranges = B * mheads * nqt;
+  // visibility bits and key-block ranges per (batch, mask head, query tile);
+  // without a mask every key of every block is visible
+  uint32_t* mbits = nullptr;
   int2* ranges = nullptr;
+  a.mheads = 1;
+  a.mrows = 1;
   if (m) {
-    ranges = (int2*)dmalloc((size_t)nranges * sizeof(int2));
-    k_mask_ranges<<<(unsigned)nranges, TQ, 0, st>>>(a.mask, a.ms[0], a.ms[1], a.ms[2], a.ms[3], mheads, (int)Lq, (int)Lk, (int)nqt, ranges);
+    TV mtv = tv_broadcast(m, {B, nh, Lq, Lk});
+    const int mheads = mtv.strides[1] == 0 ? 1 : (int)nh;
+    const int mrows = mtv.strides[2] == 0 ? 1 : (int)Lq;
+    const int mwords = (int)((Lk + 31) / 32);
+    const int64_t ngroups = (mrows + TQ - 1) / TQ;
+    const int64_t nblocks = B * mheads * ngroups;
+    if (nblocks >= INT32_MAX) return false;
+    mbits = (uint32_t*)dmalloc((size_t)B * mheads * mrows * mwords * sizeof(uint32_t));
+    ranges = (int2*)dmalloc((size_t)nblocks * sizeof(int2));
+    k_mask_pack<<<(unsigned)nblocks, TQ, 0, st>>>((const uint8_t*)mtv.ptr, mtv.strides[0], mtv.strides[1], mtv.strides[2], mtv.strides[3],
+                                                   mheads, mrows, (int)Lk, mwords, mbits, ranges);
     LC_LAUNCHED(1);
+    a.mheads = mheads;
+    a.mrows = mrows;
+    a.mwords = mwords;
   }
+  a.mbits = mbits;
   a.ranges = ranges;
   // output rows [B, Lq, nh, 64], returned as the [B, nh, Lq, 64] view
   LcTensor* y = alloc(q->dtype, {B, Lq, nh, HD});
@@ -715,6 +741,7 @@ bool sdpa_tc(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTe
   else launch_attn<__nv_bfloat16, 2>(mq, mk, mv, a, st);
   LC_LAUNCHED(1);
   if (ranges) dfree(ranges);
+  if (mbits) dfree(mbits);
   *out = view_of(y, {B, nh, Lq, HD}, {Lq * nh * HD, HD, nh * HD, 1}, 0);
   release(y);
   return true;

@@ -8,6 +8,7 @@
 //  * a generic strided kernel over broadcast views for everything else
 //    (any dtype, rank <= 8), computing in f32 / f64 / int64 / uint64.
 #include "lc_api.h"
+#include "lc_gelu.cuh"
 
 #include <cmath>
 #include <type_traits>
@@ -247,8 +248,18 @@ __global__ void __launch_bounds__(256) k_vec_unary(const T* __restrict__ a, T* _
     int64_t i = v * V::N;
     float x[V::N];
     V::load(a + i, x);
+    if constexpr (OP == OP_GELU && sizeof(T) == 2) {
+      // stored in 16 bits: erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7), packed pairs
 #pragma unroll
-    for (int j = 0; j < V::N; j++) x[j] = (OP == OP_SCALE) ? x[j] * s : un_op<float>(OP, x[j], 0.0);
+      for (int j = 0; j < V::N; j += 2) {
+        const float2 g = gelu_as2(make_float2(x[j], x[j + 1]));
+        x[j] = g.x;
+        x[j + 1] = g.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < V::N; j++) x[j] = (OP == OP_SCALE) ? x[j] * s : un_op<float>(OP, x[j], 0.0);
+    }
     V::store(out + i, x);
   }
 }

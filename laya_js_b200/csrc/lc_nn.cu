@@ -3,6 +3,7 @@
 // matmul and the exact-f32 SIMT linear used for f32/f64 and shapes the
 // tcgen05 GEMM does not take (packages/tensor-backend/src/index.ts:208-243).
 #include "lc_api.h"
+#include "lc_gelu.cuh"
 #include "lc_gemm.h"
 
 #include <cmath>
@@ -475,16 +476,29 @@ __global__ void __launch_bounds__(256) k_geglu_vec(const T* __restrict__ x, T* _
     const T* a = (const T*)&ra;
     const T* g = (const T*)&rb;
     T* o = (T*)&ro;
+    if constexpr (sizeof(T) == 4) {
 #pragma unroll
-    for (int j = 0; j < VN; j++) {
-      float av, gv;
-      if constexpr (sizeof(T) == 4) { av = ((const float*)a)[j]; gv = ((const float*)g)[j]; }
-      else if constexpr (std::is_same<T, __half>::value) { av = __half2float(a[j]); gv = __half2float(g[j]); }
-      else { av = __bfloat162float(a[j]); gv = __bfloat162float(g[j]); }
-      float r2 = 0.5f * av * (1.0f + erff(av * 0.7071067811865476f)) * gv;
-      if constexpr (sizeof(T) == 4) ((float*)o)[j] = r2;
-      else if constexpr (std::is_same<T, __half>::value) o[j] = __float2half_rn(r2);
-      else o[j] = __float2bfloat16_rn(r2);
+      for (int j = 0; j < VN; j++) {
+        const float av = ((const float*)a)[j], gv = ((const float*)g)[j];
+        ((float*)o)[j] = 0.5f * av * (1.0f + erff(av * 0.7071067811865476f)) * gv;
+      }
+    } else {
+      // stored in 16 bits: erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7), packed pairs
+#pragma unroll
+      for (int j = 0; j < VN; j += 2) {
+        float2 av, gv;
+        if constexpr (std::is_same<T, __half>::value) {
+          av = __half22float2(*(const __half2*)(a + j));
+          gv = __half22float2(*(const __half2*)(g + j));
+          const float2 r = mul2(gelu_as2(av), gv);
+          *(__half2*)(o + j) = __floats2half2_rn(r.x, r.y);
+        } else {
+          av = __bfloat1622float2(*(const __nv_bfloat162*)(a + j));
+          gv = __bfloat1622float2(*(const __nv_bfloat162*)(g + j));
+          const float2 r = mul2(gelu_as2(av), gv);
+          *(__nv_bfloat162*)(o + j) = __floats2bfloat162_rn(r.x, r.y);
+        }
+      }
     }
     *(uint4*)(y + r * F + c) = ro;
   }

@@ -7,6 +7,7 @@ quick timing. Each case fits in a few GB and ends in seconds.
     python -m laya_js_b200.profile_cases hbm       # the HBM-bound contract ops on ~100-400 MB tensors
     python -m laya_js_b200.profile_cases prompt    # configs[0]: one 128-token prompt, 22 layers, CUDA-graph replays
     python -m laya_js_b200.profile_cases prompt_q4 # the same with 4-bit affine g64 weights (fused-dequant GEMMs)
+    python -m laya_js_b200.profile_cases sdpa      # the contract's sdpa on the padded configs[2] batch (full / sliding masks)
 
 Every case prints one line with its shape and the device time per launch
 (CUDA events on the library stream, after warm-up).
@@ -155,6 +156,29 @@ def case_hbm(b) -> str:
     return "hbm kernels (algorithmic bytes / CUDA-event time):\n  " + "\n  ".join(out)
 
 
+def case_sdpa(b) -> str:
+    """The contract's sdpa as ModernBert.layer calls it on the padded configs[2]
+    batch (256 x 512, 12 heads; q/k dense, v a strided view of the QKV
+    projection) with the full and sliding masks of attentionMasks."""
+    from .modernbert import attentionMasks
+    lens, _, _ = WL.cfg2_prompts()
+    B, L, nh = len(lens), int(lens.max()), 12
+    valid = (np.arange(L)[None, :] < lens[:, None]).astype(np.uint8)
+    full, sliding = attentionMasks(valid, B, L, 128)
+    rng = np.random.default_rng(0)
+    qkv = b.fromHost(HostTensor("f16", (B, L, 3 * nh * 64), rng.standard_normal((B, L, 3 * nh * 64), dtype=np.float32).astype(np.float16)))
+    t = b.transpose(b.reshape(qkv, [B, L, 3, nh, 64]), [2, 0, 3, 1, 4])
+    q, k, v = [b.reshape(x, [B, nh, L, 64]) for x in b.split(t, 3, 0)]
+    q, k = b.cast(q, "f16"), b.cast(k, "f16")  # dense, like rope's outputs
+    out = []
+    for name, m in (("full", full), ("sliding", sliding)):
+        tm = b.fromHost(m)
+        run = lambda: b.dispose(b.sdpa(q, k, v, tm, 0.125))
+        run()
+        out.append(f"{name} {_event_time(b, run, 5) * 1e3:.0f} us")
+    return f"sdpa [{B},{nh},{L},64] padded configs[2] batch: " + ", ".join(out)
+
+
 def _event_time(b, fn, reps: int) -> float:
     """Device ms per call: CUDA events on the library stream around `reps` calls."""
     import torch
@@ -176,7 +200,7 @@ def _event_time(b, fn, reps: int) -> float:
 def main(argv) -> None:
     b = createCudaBackend(0)
     cases = {"encoder": case_encoder, "gemm": case_gemm, "attention": case_attention, "hbm": case_hbm, "prompt": case_prompt,
-             "prompt_q4": case_prompt_q4}
+             "prompt_q4": case_prompt_q4, "sdpa": case_sdpa}
     for name in argv[1:] or list(cases):
         print(cases[name](b), flush=True)
 
