@@ -33,7 +33,9 @@ Keys beyond the driver's contract (extras run on rank 0 of a 1-GPU run):
              load()/predict() run), host buffers in and out: configs[0] p50
              and a padded configs[2] batch;
   p50_latency_ms / p50_latency_graph_ms  configs[0] (batch 1, seq 128,
-             3-way head) end to end, eager and as a captured CUDA graph.
+             3-way head) end to end, eager and as a captured CUDA graph;
+  predict    the DecisionModel forward (predict()'s model call) on one
+             128-token prompt: p50 eager and through Backend.compile.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -390,6 +392,29 @@ def contract_leg(b, ev, enc, thw3, thb3, thw8, thb8) -> dict:
                     "row kernels) + CLS head, host buffers in and out, CUDA events on the library stream"}
 
 
+def predict_leg(b, ev) -> dict:
+    """The predict() path: the Laya DecisionModel (ModernBERT-base fp16 encoder +
+    the two-layer head, scorer and action head, packages/laya/src/model.ts:124-285)
+    through the contract ops on one 128-token prompt with four markers, host
+    batch in and host logits/act out; p50 eager (forwardTensors) and through
+    DecisionModel.compiled() (Backend.compile = one CUDA graph per signature)."""
+    from laya_js_b200 import workloads as WL
+    from laya_js_b200.decision import loadDecisionModel
+    from laya_js_b200.host import HostTensor
+    W = {**{k: v.astype(np.float32) for k, v in WL.base_weights().items()}, **WL.decision_head_weights(WL.BASE)}
+    get = lambda n: HostTensor("f32", W[n].shape, W[n]) if n in W else None
+    model = loadDecisionModel(b, dict(WL.BASE), {"head_layers": 2, "act_costs": {"escalate": 0.5}}, get, "f16")
+    batch = WL.decision_batch(WL.BASE, [128])
+    run = model.compiled()
+    eager = ev.p50(lambda: model.readOutputs(model.forwardTensors(batch)), reps=30)
+    graph = ev.p50(lambda: model.readOutputs(run(batch)), reps=30)
+    del run
+    model.dispose()
+    return {"p50_predict_ms": eager, "p50_predict_compiled_ms": graph,
+            "config": "DecisionModel (ModernBERT-base fp16 + laya head), 1 prompt of 128 tokens, 4 markers; "
+                      "host batch in (ids, masks built on the host), logits + act read back"}
+
+
 def main() -> None:
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -548,6 +573,10 @@ def main() -> None:
     enc.dispose()
     b.dispose(tids)
     if extras:
+        try:
+            line["predict"] = predict_leg(b, ev)
+        except Exception as ex:  # noqa: BLE001
+            line["predict"] = f"failed: {ex}"
         q = {}
         for bits in (4, 8):
             try:

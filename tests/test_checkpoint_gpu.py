@@ -31,7 +31,8 @@ def test_quantized_checkpoint_onto_device(tmp_path, scheme):
     W = WL.random_weights(cfg, seed=6, norm_std=0.05)
     path = str(tmp_path / f"enc.{scheme}.safetensors")
     deq = laya_ckpt.write(path, W, scheme)
-    enc = loadModernBert(b, parseModernBertConfig(cfg), CK.read_weights(path, quantized="device"), "f16")
+    # a consuming getter (each tensor handed out once): the prefix is given, as laya does
+    enc = loadModernBert(b, parseModernBertConfig(cfg), CK.read_weights(path, quantized="device"), "f16", prefix="encoder.")
     for i, L in enumerate(enc.weights.layers):
         for attr, suffix in (("Wqkv", "attn.Wqkv.weight"), ("Wo", "attn.Wo.weight"), ("Wi", "mlp.Wi.weight"), ("WoMlp", "mlp.Wo.weight")):
             m = getattr(L, attr)
