@@ -69,6 +69,11 @@ constexpr int NS = 2;                         // S buffers
 constexpr uint32_t O_COL = NS * TK;           // O of work item t at O_COL + (t & 1) * HD
 constexpr int NST = 4;                        // K/V ring depth
 constexpr size_t ATTN_SMEM = 2 * TILE_BYTES + 2 * NST * KV_BYTES + 1024 + 256;
+#ifndef LC_EXP_FMA_MASK
+#define LC_EXP_FMA_MASK 0x8888u
+#endif
+// pairs i (of 16 per 32-key chunk) whose exponentials run on the FMA pipe
+constexpr uint32_t kExpFmaMask = LC_EXP_FMA_MASK;
 
 struct AttnTcArgs {
   const int4* tiles;  // (first token of the sequence, its length, first query row (multiple of 128), 0)
@@ -169,6 +174,25 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+// 2^x for a pair on the FMA and integer pipes (the exponential unit does one
+// value per lane every 8 cycles per SM sub-partition, the FMA pipe 32 per
+// cycle): x = n + f with n = round(x) (the 1.5·2^23 shift), f in [-1/2, 1/2];
+// 2^f by a cubic fitted here for relative error (|error| < 7.8e-5, below the
+// half-ulp 2^-11 of the f16 P it feeds); 2^n added to the exponent bits.
+// x is clamped to >= -126 (2^-126 rounds to 0 in the 16-bit P).
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 M = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23
+  const float2 t = add2(x, M);
+  const float2 n = add2(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = add2(x, make_float2(-n.x, -n.y));
+  float2 p = fma2(make_float2(0.05508868f, 0.05508868f), f, make_float2(0.24260405f, 0.24260405f));
+  p = fma2(p, f, make_float2(0.6932762f, 0.6932762f));
+  p = fma2(p, f, make_float2(0.99992895f, 0.99992895f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
@@ -487,8 +511,12 @@ __global__ void __launch_bounds__(192, 2) k_attn_tc(const __grid_constant__ CUte
             for (int i = 0; i < 16; i++) {
               const int k = c * 32 + 2 * i;
               float2 x = fma2(make_float2(s[k], s[k + 1]), make_float2(sl, sl), make_float2(nbias, nbias));
-              x.x = ex2(x.x);
-              x.y = ex2(x.y);
+              if (kExpFmaMask & (1u << i)) {  // part of the pairs on the FMA pipe
+                x = exp2_fma2(x);
+              } else {
+                x.x = ex2(x.x);
+                x.y = ex2(x.y);
+              }
               pr[c * 16 + i] = pack2<T>(x.x, x.y);
               acc[i & 3] = add2(acc[i & 3], x);
             }
