@@ -72,6 +72,13 @@ def parse():
     return p.parse_args()
 
 
+def config_of(world: int, tokens_per_gpu: int, tokens_total: int) -> dict:
+    """The workload description both arms report (the reference arm times a
+    stated fixed sample of it per step, see its cpu_baseline.sample)."""
+    return {"workload": WORKLOAD, "global_batch": BATCH * world, "seq_len": f"U[{LO},{HI}]", "tokens_per_gpu_step": tokens_per_gpu,
+            "tokens_per_step": tokens_total, "parallelism": f"dp{world}", "l2": "inputs larger than L2 (activations ~0.5 GB per step)"}
+
+
 def linear_flops_per_token(cfg: dict) -> float:
     H, I, n = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"]
     return 2.0 * (H * 3 * H + H * H + H * 2 * I + I * H) * n
@@ -212,6 +219,14 @@ def cpu_baseline() -> dict:
                       "C++ oracle (f32 storage, f64 accumulation, std::thread workers), same weights and head"}
 
 
+def _batch_tokens(world: int) -> tuple[int, int]:
+    """(tokens of rank 0's shard, tokens of the global batch) of an N-rank run."""
+    from laya_js_b200 import workloads as WL
+    lens, ids, cu = WL.cfg2_prompts(BATCH * world)
+    _, my_ids, _, _ = shard(lens, ids, cu, 0, world)
+    return int(len(my_ids)), int(lens.sum())
+
+
 def run_reference(args, rank: int, world: int) -> None:
     """--impl reference: the reference's CPU path on this box's host cores. The
     reference's own CPU backend (npm @johnhenry/math-plus-tensor-cpu) is not
@@ -227,7 +242,7 @@ def run_reference(args, rank: int, world: int) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init N(0,0.02) weights, uniform token ids)",
-            "config": {"workload": WORKLOAD, "global_batch": BATCH * world, "seq_len": f"U[{LO},{HI}]", "parallelism": f"dp{world}"},
+            "config": config_of(world, *_batch_tokens(world)),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "nproc": os.cpu_count(),
                              "cpu_model": cpu_model(),
                              "sample": f"every 32nd prompt of the configs[2] batch ({r['tokens_per_step']} tokens) per step"},
@@ -532,9 +547,7 @@ def main() -> None:
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16", "data": "synthetic (seeded random-init N(0,0.02) weights, uniform token ids)",
-        "config": {"workload": WORKLOAD, "global_batch": BATCH * world, "seq_len": f"U[{LO},{HI}]", "tokens_per_gpu_step": T,
-                   "tokens_per_step": tok_total, "parallelism": f"dp{world}",
-                   "l2": "inputs larger than L2 (activations ~0.5 GB per step)"},
+        "config": config_of(world, T, tok_total),
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * 4 + (len(mine) + 1) * 4,
                 "d2h_bytes_per_step": len(mine) * CLASSES * 4,
                 "what": "lc_encoder_forward_host per rank (H2D ids + cu_seqlens, D2H probabilities) and the host gather to rank 0"},
