@@ -688,7 +688,12 @@ void attention_varlen_tc(const void* qkv, void* out, const int4* tiles_dev, int 
 namespace {
 // 4-D map over a [B, nh, L, 64] view (element strides s[0..2] for B, nh, L;
 // innermost stride 1): dims (64, L, nh, B), box 64 x rows x 1 x 1, 128-byte swizzle.
-bool map_bhld(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t nh, int64_t L, const int64_t* s, int rows) {
+bool map_bhld(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t nh, int64_t L, const int64_t* s0, int rows) {
+  // a dimension of extent 1 is never stepped: its stride (which a view may
+  // carry as 0 or anything) is replaced by 16 bytes for the map
+  const int64_t ext[3] = {B, nh, L};
+  int64_t s[3];
+  for (int i = 0; i < 3; i++) s[i] = ext[i] == 1 ? 8 : s0[i];
   for (int i = 0; i < 3; i++)
     if ((s[i] * 2) % 16 || s[i] <= 0 || s[i] * 2 >= ((int64_t)1 << 40)) return false;
   if (((uintptr_t)ptr) & 15) return false;

@@ -15,9 +15,23 @@ using namespace lc;
 // ------------------------------------------------------------- layerNorm
 // index.ts:216-217: normalise over the last axis, stats in f32, optional weight/bias.
 
-// Vectorised fast path: dense f16/bf16/f32 rows, N % 8 == 0 (f32: % 4), N <= 256 vectors.
-template <typename T, int MAXV>
-__global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+// Four LayerNorm weights (or biases) as floats: f32, or the rows' own 16-bit type.
+template <typename WT>
+__device__ __forceinline__ float4 ld_w4(const WT* p, int64_t i, float fill) {
+  if (!p) return make_float4(fill, fill, fill, fill);
+  if constexpr (sizeof(WT) == 4) {
+    return __ldg((const float4*)(p + i));
+  } else {
+    const uint2 u = __ldg((const uint2*)(p + i));
+    const WT* h = (const WT*)&u;
+    return make_float4(to_f<WT>(h[0]), to_f<WT>(h[1]), to_f<WT>(h[2]), to_f<WT>(h[3]));
+  }
+}
+
+// Vectorised fast path: dense f16/bf16/f32 rows, N % 8 == 0 (f32: % 4), N <= 256 vectors;
+// weight and bias f32 or of the rows' type (WT).
+template <typename T, int MAXV, typename WT = float>
+__global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, const WT* __restrict__ w, const WT* __restrict__ b,
                                                        T* __restrict__ y, int64_t rows, int N, float eps) {
   pdl_trigger();
   pdl_wait();
@@ -71,8 +85,8 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
         T* e = (T*)&raw;
 #pragma unroll
         for (int j = 0; j < VN; j += 4) {  // weight and bias four at a time (fewer live registers)
-          const float4 a4 = w ? __ldg((const float4*)(w + c * VN + j)) : make_float4(1.f, 1.f, 1.f, 1.f);
-          const float4 b4 = b ? __ldg((const float4*)(b + c * VN + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 a4 = ld_w4<WT>(w, c * VN + j, 1.f);
+          const float4 b4 = ld_w4<WT>(b, c * VN + j, 0.f);
           const float wv[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
           for (int k = 0; k < 4; k++) {
@@ -92,8 +106,8 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
 // taken in turn by the grid), each thread holding up to MAXV 16-byte vectors;
 // the mean and the centred sum of squares go through warp shuffles and the 8
 // warps' partials in shared memory (read by every thread in the same order).
-template <typename T, int MAXV>
-__global__ void __launch_bounds__(256) k_layernorm_blk(const T* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+template <typename T, int MAXV, typename WT = float>
+__global__ void __launch_bounds__(256) k_layernorm_blk(const T* __restrict__ x, const WT* __restrict__ w, const WT* __restrict__ b,
                                                        T* __restrict__ y, int64_t rows, int N, float eps) {
   constexpr int VN = 16 / sizeof(T);
   __shared__ float sm[8];
@@ -144,8 +158,8 @@ __global__ void __launch_bounds__(256) k_layernorm_blk(const T* __restrict__ x, 
         T* e = (T*)&raw;
 #pragma unroll
         for (int j = 0; j < VN; j += 4) {
-          const float4 a4 = w ? __ldg((const float4*)(w + c * VN + j)) : make_float4(1.f, 1.f, 1.f, 1.f);
-          const float4 b4 = b ? __ldg((const float4*)(b + c * VN + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 a4 = ld_w4<WT>(w, c * VN + j, 1.f);
+          const float4 b4 = ld_w4<WT>(b, c * VN + j, 0.f);
           const float wv[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
           for (int k = 0; k < 4; k++) {
@@ -160,33 +174,33 @@ __global__ void __launch_bounds__(256) k_layernorm_blk(const T* __restrict__ x, 
     }
   }
 }
-template <typename T>
-void launch_layernorm_blk(const T* x, const float* w, const float* b, T* y, int64_t rows, int N, float eps, cudaStream_t st) {
+template <typename T, typename WT = float>
+void launch_layernorm_blk(const T* x, const WT* w, const WT* b, T* y, int64_t rows, int N, float eps, cudaStream_t st) {
   constexpr int VN = 16 / sizeof(T);
   const int per = (N / VN + 255) / 256;
   const unsigned blocks = (unsigned)std::min<int64_t>(rows, (int64_t)lc::num_sms() * 8);
   switch (per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8) {
-    case 1: k_layernorm_blk<T, 1><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    case 2: k_layernorm_blk<T, 2><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    case 4: k_layernorm_blk<T, 4><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    default: k_layernorm_blk<T, 8><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 1: k_layernorm_blk<T, 1, WT><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 2: k_layernorm_blk<T, 2, WT><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 4: k_layernorm_blk<T, 4, WT><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    default: k_layernorm_blk<T, 8, WT><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
   }
 }
 
 // The register tile is sized to the row (vectors per lane = ceil(N / VN / 32)) so
 // that short rows (H = 768 -> 3 vectors) keep full occupancy.
-template <typename T>
-void launch_layernorm_vec(const T* x, const float* w, const float* b, T* y, int64_t rows, int N, float eps, cudaStream_t st) {
+template <typename T, typename WT = float>
+void launch_layernorm_vec(const T* x, const WT* w, const WT* b, T* y, int64_t rows, int N, float eps, cudaStream_t st) {
   constexpr int VN = 16 / sizeof(T);
   int per = (N / VN + 31) / 32;
   unsigned blocks = lc::blocks_for(rows * 32, 256);
   switch (per) {
-    case 0: case 1: lc::launch_chain(k_layernorm_vec<T, 1>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
-    case 2: lc::launch_chain(k_layernorm_vec<T, 2>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
-    case 3: lc::launch_chain(k_layernorm_vec<T, 3>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
-    case 4: lc::launch_chain(k_layernorm_vec<T, 4>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
-    case 5: case 6: lc::launch_chain(k_layernorm_vec<T, 6>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
-    default: lc::launch_chain(k_layernorm_vec<T, 8>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 0: case 1: lc::launch_chain(k_layernorm_vec<T, 1, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 2: lc::launch_chain(k_layernorm_vec<T, 2, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 3: lc::launch_chain(k_layernorm_vec<T, 3, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 4: lc::launch_chain(k_layernorm_vec<T, 4, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 5: case 6: lc::launch_chain(k_layernorm_vec<T, 6, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    default: lc::launch_chain(k_layernorm_vec<T, 8, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
   }
 }
 
@@ -665,6 +679,25 @@ __global__ void __launch_bounds__(256) k_matmul(MM p) {
   }
 }
 
+// y[m, n] = x[m, :] · w[n, :] (+ bias[n]) for few rows: one warp per output,
+// lanes striding over K, f32 accumulation (the contract's, index.ts:211-215).
+// The 64 x 64-tile SIMT kernel would put only ceil(N/64) blocks on the GPU.
+__global__ void __launch_bounds__(256) k_linear_rows(const char* x, int xdt, const char* w, int wdt, const char* bias, int bdt, char* y,
+                                                     int ydt, int64_t M, int64_t N, int64_t K) {
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= M * N) return;
+  const int64_t m = warp / N, n = warp % N;
+  float acc = 0.f;
+  for (int64_t k = lane; k < K; k += 32) acc = fmaf(ld_as<float>(x, xdt, m * K + k), ld_as<float>(w, wdt, n * K + k), acc);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) {
+    if (bias) acc += ld_as<float>(bias, bdt, n);
+    st_as<float>(y, ydt, m * N + n, acc);
+  }
+}
+
 namespace {
 
 void launch_mm(const MM& p, int64_t batch, bool dbl) {
@@ -694,7 +727,15 @@ void linear_simt(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, Lc
   p.sam = p.k; p.sak = 1;
   p.sbk = 1; p.sbn = p.k;  // w[n, k]
   p.nb = 0;
-  if (p.m && p.n) launch_mm(p, 1, y->dtype == LC_F64 || x2->dtype == LC_F64);
+  const bool dbl = y->dtype == LC_F64 || x2->dtype == LC_F64 || w->dtype == LC_F64;
+  if (p.m && p.n && p.m <= 16 && !dbl && p.m * p.n < ((int64_t)1 << 26)) {
+    const int64_t threads = p.m * p.n * 32;
+    k_linear_rows<<<(unsigned)((threads + 255) / 256), 256, 0, stream()>>>(p.a, p.adt, p.b, p.bdt, p.bias, p.biasdt, p.c, p.cdt, p.m, p.n,
+                                                                        p.k);
+    LC_LAUNCHED(1);
+    return;
+  }
+  if (p.m && p.n) launch_mm(p, 1, dbl);
 }
 }  // namespace lc
 
@@ -725,8 +766,11 @@ int lc_layer_norm(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh, doub
       return f;
     };
     bool f64 = x->dtype == LC_F64;
-    LcTensor* w = f64 ? w0 : as_f32(w0);
-    LcTensor* b = f64 ? b0 : as_f32(b0);
+    // 16-bit rows with dense weight / bias of the same type are read as they are
+    auto same16 = [&](LcTensor* t) { return !t || (t->dtype == x->dtype && t->contiguous()); };
+    const bool w16 = is_half(x->dtype) && x->dtype == odt && same16(w0) && same16(b0) && (w0 || b0);
+    LcTensor* w = (f64 || w16) ? w0 : as_f32(w0);
+    LcTensor* b = (f64 || w16) ? b0 : as_f32(b0);
     const char* wp = w ? w->data() : nullptr;
     const char* bp = b ? b->data() : nullptr;
     int wdt = w ? w->dtype : 0, bdt = b ? b->dtype : 0;
@@ -738,7 +782,21 @@ int lc_layer_norm(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh, doub
     bool blk = aligned && x->dtype == odt && (odt == LC_F32 || is_half(odt)) && N % vn == 0 && N / vn <= 256 * 8;
     const float* wf = (const float*)wp;
     const float* bf = (const float*)bp;
-    if (vec) {
+    if (w16 && (vec || blk)) {
+      if (odt == LC_F16) {
+        const __half *wh = (const __half*)wp, *bh = (const __half*)bp;
+        if (vec) launch_layernorm_vec<__half, __half>((const __half*)x->data(), wh, bh, (__half*)y->data(), rows, (int)N, (float)eps, st);
+        else launch_layernorm_blk<__half, __half>((const __half*)x->data(), wh, bh, (__half*)y->data(), rows, (int)N, (float)eps, st);
+      } else {
+        const __nv_bfloat16 *wh = (const __nv_bfloat16*)wp, *bh = (const __nv_bfloat16*)bp;
+        if (vec)
+          launch_layernorm_vec<__nv_bfloat16, __nv_bfloat16>((const __nv_bfloat16*)x->data(), wh, bh, (__nv_bfloat16*)y->data(), rows, (int)N,
+                                                             (float)eps, st);
+        else
+          launch_layernorm_blk<__nv_bfloat16, __nv_bfloat16>((const __nv_bfloat16*)x->data(), wh, bh, (__nv_bfloat16*)y->data(), rows, (int)N,
+                                                             (float)eps, st);
+      }
+    } else if (vec) {
       if (odt == LC_F16) launch_layernorm_vec<__half>((const __half*)x->data(), wf, bf, (__half*)y->data(), rows, (int)N, (float)eps, st);
       else if (odt == LC_BF16) launch_layernorm_vec<__nv_bfloat16>((const __nv_bfloat16*)x->data(), wf, bf, (__nv_bfloat16*)y->data(), rows, (int)N, (float)eps, st);
       else launch_layernorm_vec<float>((const float*)x->data(), wf, bf, (float*)y->data(), rows, (int)N, (float)eps, st);

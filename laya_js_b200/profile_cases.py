@@ -8,6 +8,7 @@ quick timing. Each case fits in a few GB and ends in seconds.
     python -m laya_js_b200.profile_cases prompt    # configs[0]: one 128-token prompt, 22 layers, CUDA-graph replays
     python -m laya_js_b200.profile_cases prompt_q4 # the same with 4-bit affine g64 weights (fused-dequant GEMMs)
     python -m laya_js_b200.profile_cases sdpa      # the contract's sdpa on the padded configs[2] batch (full / sliding masks)
+    python -m laya_js_b200.profile_cases predict   # DecisionModel forward, one 128-token prompt, eager and compiled
 
 Every case prints one line with its shape and the device time per launch
 (CUDA events on the library stream, after warm-up).
@@ -179,6 +180,24 @@ def case_sdpa(b) -> str:
     return f"sdpa [{B},{nh},{L},64] padded configs[2] batch: " + ", ".join(out)
 
 
+def case_predict(b) -> str:
+    """The DecisionModel (ModernBERT-base fp16 + laya head) on one 128-token
+    prompt: eager forward and DecisionModel.compiled() replays (CUDA graph)."""
+    from .decision import loadDecisionModel
+    W = {**{k: v.astype(np.float32) for k, v in WL.base_weights().items()}, **WL.decision_head_weights(WL.BASE)}
+    get = lambda n: HostTensor("f32", W[n].shape, W[n]) if n in W else None
+    model = loadDecisionModel(b, dict(WL.BASE), {"head_layers": 2, "act_costs": {"escalate": 0.5}}, get, "f16")
+    batch = WL.decision_batch(WL.BASE, [128])
+    run = model.compiled()
+    eager = _event_time(b, lambda: model.readOutputs(model.forwardTensors(batch)), 5)
+    for _ in range(3):
+        model.readOutputs(run(batch))
+    graph = _event_time(b, lambda: model.readOutputs(run(batch)), 5)
+    del run
+    model.dispose()
+    return f"predict (DecisionModel, 1 x 128 tokens): eager {eager:.3f} ms, compiled {graph:.3f} ms"
+
+
 def _event_time(b, fn, reps: int) -> float:
     """Device ms per call: CUDA events on the library stream around `reps` calls."""
     import torch
@@ -200,7 +219,7 @@ def _event_time(b, fn, reps: int) -> float:
 def main(argv) -> None:
     b = createCudaBackend(0)
     cases = {"encoder": case_encoder, "gemm": case_gemm, "attention": case_attention, "hbm": case_hbm, "prompt": case_prompt,
-             "prompt_q4": case_prompt_q4, "sdpa": case_sdpa}
+             "prompt_q4": case_prompt_q4, "sdpa": case_sdpa, "predict": case_predict}
     for name in argv[1:] or list(cases):
         print(cases[name](b), flush=True)
 

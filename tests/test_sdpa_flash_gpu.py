@@ -112,3 +112,21 @@ def test_sdpa_tcgen05_long_padded_batch(dt):
         want = O.sdpa(r[0], r[1], r[2], mask, 0.125)
         err = np.abs(got - want).max()
         assert err < TOL[dt], f"{dt}: max err {err}"
+
+
+def test_sdpa_tcgen05_batch_of_one():
+    """B = 1 (one prompt, the predict() case): the batch dimension's stride of
+    a view is arbitrary and must not keep the call off the tcgen05 path."""
+    b = backend()
+    rng = np.random.default_rng(14)
+    L, nh = 128, 12
+    qkv, qkvr = _up(b, rng.standard_normal((1, L, 3 * nh * 64)), "f16")
+    t = b.transpose(b.reshape(qkv, [1, L, 3, nh, 64]), [2, 0, 3, 1, 4])
+    q, k, v = [b.reshape(x, [1, nh, L, 64]) for x in b.split(t, 3, 0)]
+    r = qkvr.reshape(1, L, 3, nh, 64).transpose(2, 0, 3, 1, 4)
+    mask = np.ones((1, 1, 1, L), bool)
+    mask[0, 0, 0, 100:] = False
+    out = b.sdpa(q, k, v, b.fromHost(HostTensor("bool", mask.shape, mask.astype(np.uint8))), 0.125)
+    assert not _dense(out), "expected the tcgen05 path"
+    err = np.abs(to_f32(b.read(out)) - O.sdpa(r[0], r[1], r[2], mask, 0.125)).max()
+    assert err < TOL["f16"], f"max err {err}"
