@@ -209,9 +209,9 @@ namespace lc {
 void layernorm_raw(const void* x, const float* w, void* y, int64_t rows, int N, float eps, int dtype, cudaStream_t st) {
   LC_CHECK(N % 8 == 0 && N <= 2048, "layernorm_raw: row length must be a multiple of 8, at most 2048");
   if (dtype == LC_F16)
-    launch_layernorm_vec<__half>((const __half*)x, w, nullptr, (__half*)y, rows, N, eps, st);
+    launch_layernorm_vec<__half, float>((const __half*)x, w, nullptr, (__half*)y, rows, N, eps, st);
   else
-    launch_layernorm_vec<__nv_bfloat16>((const __nv_bfloat16*)x, w, nullptr, (__nv_bfloat16*)y, rows, N, eps, st);
+    launch_layernorm_vec<__nv_bfloat16, float>((const __nv_bfloat16*)x, w, nullptr, (__nv_bfloat16*)y, rows, N, eps, st);
   LC_LAUNCHED(1);
 }
 }  // namespace lc
