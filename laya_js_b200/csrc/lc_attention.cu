@@ -435,7 +435,9 @@ bool sdpa_flash(const LcTensor* q, const LcTensor* k, const LcTensor* v, const L
   const int64_t B = q->shape[0], H = q->shape[1], Lq = q->shape[2], Lk = k->shape[2];
   if (q->shape[3] != HD || v->shape[3] != HD || Lq < 1 || Lk < 1 || B * H > 65535 || Lq > INT32_MAX || Lk > INT32_MAX) return false;
   for (const LcTensor* t : {q, k, v}) {
-    if (t->strides[3] != 1 || (t->strides[0] % 8) || (t->strides[1] % 8) || (t->strides[2] % 8) || ((uintptr_t)t->data() & 15)) return false;
+    if (t->strides[3] != 1 || ((uintptr_t)t->data() & 15)) return false;
+    for (int d = 0; d < 3; d++)
+      if (t->shape[d] > 1 && t->strides[d] % 8) return false;  // a size-1 axis's stride is never used
   }
   SdpaArgs a{};
   a.q = q->data();

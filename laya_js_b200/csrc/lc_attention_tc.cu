@@ -603,6 +603,8 @@ void launch_attn(const CUtensorMap& mq, const CUtensorMap& mkv, const CUtensorMa
 // One 128-thread block per (b, mask head, row group), thread = mask row.
 __global__ void __launch_bounds__(TQ) k_mask_pack(const uint8_t* mask, long long s0, long long s1, long long s2, long long s3, int mheads,
                                                   int mrows, int Lk, int mwords, uint32_t* bits, int2* ranges) {
+  pdl_trigger();
+  pdl_wait();
   const int ngroups = (mrows + TQ - 1) / TQ;
   const int gi = blockIdx.x % ngroups, bm = blockIdx.x / ngroups, mh = bm % mheads, b = bm / mheads;
   const int r = gi * TQ + (int)threadIdx.x;
@@ -708,6 +710,52 @@ bool map_bhld(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t nh,
 }
 }  // namespace
 
+// Packed masks are kept per mask view: a model passes the same mask tensor to
+// every layer of a forward (ModernBert.encode hands each layer kind's mask to
+// all its layers), so the bits and key-block ranges are built once. The key is
+// the storage (unique id and write version) and the broadcast view; an entry
+// goes when its storage is released. Entries made while a CUDA graph is being
+// captured live only inside that capture (their buffers are the graph's own
+// allocations, freed inside it at the end) and entries made outside it are
+// not used by it, so a recording never holds a pointer the cache may free.
+namespace {
+struct PackedMask {
+  uint64_t sid;
+  uint32_t ver;
+  const void* ptr;
+  int64_t strides[4];
+  int64_t dims[4];
+  int mheads, mrows, mwords;
+  uint32_t* bits;
+  int2* ranges;
+  bool in_capture;
+};
+std::vector<PackedMask>& mask_cache() {
+  static std::vector<PackedMask> v;
+  return v;
+}
+constexpr size_t kMaskCacheEntries = 8;
+void drop_mask(size_t i, bool free_buffers) {
+  auto& c = mask_cache();
+  if (free_buffers) {
+    dfree(c[i].bits);
+    dfree(c[i].ranges);
+  }
+  c.erase(c.begin() + (std::ptrdiff_t)i);
+}
+}  // namespace
+
+void storage_released(uint64_t id) {
+  auto& c = mask_cache();
+  for (size_t i = c.size(); i-- > 0;)
+    if (c[i].sid == id) drop_mask(i, true);
+}
+void capture_ending(bool aborted) {
+  auto& c = mask_cache();
+  for (size_t i = c.size(); i-- > 0;)
+    if (c[i].in_capture) drop_mask(i, !aborted);
+}
+
 // LAYA_CUDA_SDPA_TC=0 keeps the contract's sdpa on the mma.sync kernel.
 static bool sdpa_tc_enabled() {
   static int on = -1;
@@ -746,6 +794,7 @@ bool sdpa_tc(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTe
   // without a mask every key of every block is visible
   uint32_t* mbits = nullptr;
   int2* ranges = nullptr;
+  bool cached = false;
   a.mheads = 1;
   a.mrows = 1;
   if (m) {
@@ -756,11 +805,38 @@ bool sdpa_tc(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTe
     const int64_t ngroups = (mrows + TQ - 1) / TQ;
     const int64_t nblocks = B * mheads * ngroups;
     if (nblocks >= INT32_MAX) return false;
-    mbits = (uint32_t*)dmalloc((size_t)B * mheads * mrows * mwords * sizeof(uint32_t));
-    ranges = (int2*)dmalloc((size_t)nblocks * sizeof(int2));
-    k_mask_pack<<<(unsigned)nblocks, TQ, 0, st>>>((const uint8_t*)mtv.ptr, mtv.strides[0], mtv.strides[1], mtv.strides[2], mtv.strides[3],
-                                                   mheads, mrows, (int)Lk, mwords, mbits, ranges);
-    LC_LAUNCHED(1);
+    const bool capturing = lc::capturing();
+    const bool cacheable = !m->st->external && m->st->id != 0;
+    const int64_t dims[4] = {B, nh, Lq, Lk};
+    auto& c = mask_cache();
+    for (const PackedMask& e : c)
+      if (cacheable && e.sid == m->st->id && e.ver == m->st->version && e.ptr == mtv.ptr && e.in_capture == capturing &&
+          std::equal(e.strides, e.strides + 4, mtv.strides) && std::equal(e.dims, e.dims + 4, dims)) {
+        mbits = e.bits;
+        ranges = e.ranges;
+        cached = true;
+        break;
+      }
+    if (!cached) {
+      mbits = (uint32_t*)dmalloc((size_t)B * mheads * mrows * mwords * sizeof(uint32_t));
+      ranges = (int2*)dmalloc((size_t)nblocks * sizeof(int2));
+      lc::launch_chain(k_mask_pack, dim3((unsigned)nblocks), dim3(TQ), 0, st, (const uint8_t*)mtv.ptr, mtv.strides[0], mtv.strides[1],
+                       mtv.strides[2], mtv.strides[3], mheads, mrows, (int)Lk, mwords, mbits, ranges);
+      LC_LAUNCHED(1);
+      if (cacheable) {
+        if (!capturing && c.size() >= kMaskCacheEntries)
+          for (size_t i = 0; i < c.size(); i++)
+            if (!c[i].in_capture) {
+              drop_mask(i, true);
+              break;
+            }
+        PackedMask e{m->st->id, m->st->version, mtv.ptr, {}, {}, mheads, mrows, mwords, mbits, ranges, capturing};
+        std::copy(mtv.strides, mtv.strides + 4, e.strides);
+        std::copy(dims, dims + 4, e.dims);
+        c.push_back(e);
+        cached = true;
+      }
+    }
     a.mheads = mheads;
     a.mrows = mrows;
     a.mwords = mwords;
@@ -773,8 +849,10 @@ bool sdpa_tc(const LcTensor* q, const LcTensor* k, const LcTensor* v, const LcTe
   if (q->dtype == LC_F16) launch_attn<__half, 2>(mq, mk, mv, a, st);
   else launch_attn<__nv_bfloat16, 2>(mq, mk, mv, a, st);
   LC_LAUNCHED(1);
-  if (ranges) dfree(ranges);
-  if (mbits) dfree(mbits);
+  if (!cached) {
+    if (ranges) dfree(ranges);
+    if (mbits) dfree(mbits);
+  }
   *out = view_of(y, {B, nh, Lq, HD}, {Lq * nh * HD, HD, nh * HD, 1}, 0);
   release(y);
   return true;

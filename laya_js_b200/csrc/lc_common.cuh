@@ -42,6 +42,11 @@ struct LcStorage {
   size_t bytes = 0;
   int refs = 1;
   bool external = false;  // not owned (never freed by the library)
+  // The launch count when lc_from_host filled it, -1 once lc_copy_into has
+  // written it (or for memory it did not upload): a weight no kernel writes.
+  int64_t upload_mark = -1;
+  uint64_t id = 0;       // unique per storage for the process's lifetime
+  uint32_t version = 0;  // bumped whenever lc_copy_into writes it
 };
 
 struct LcTensor {
@@ -124,6 +129,18 @@ inline unsigned blocks_for(int64_t n, int threads) {
 // Only kernels that call pdl_wait() in every CTA before touching memory an
 // earlier kernel wrote (and before exiting) may be launched this way.
 bool& pdl_flag();
+// The storage was filled by a host upload, no kernel has written it since,
+// and a kernel has been launched after the upload (so the copy has landed
+// before any later kernel starts): a GEMM may read it before pdl_wait().
+bool upload_settled(const LcStorage* st);
+// Called once a storage's memory is released: drops derived data cached for
+// it (the packed attention masks).
+void storage_released(uint64_t id);
+// Called while a capture ends (aborted: after the capture, whose allocations
+// no longer exist): releases data cached during the capture.
+void capture_ending(bool aborted);
+// A CUDA graph capture (lc_graph_capture_begin) is in progress.
+bool capturing();
 struct PdlScope {
   bool prev;
   PdlScope() : prev(pdl_flag()) { pdl_flag() = true; }

@@ -34,6 +34,7 @@ struct State {
   bool capturing = false;
   std::unordered_set<void*> cap_allocs;
   std::vector<void*> cap_deferred;
+  uint64_t next_storage_id = 0;
 };
 State& S() {
   static State s;
@@ -66,8 +67,18 @@ cudaStream_t stream() { return S().cur; }
 int device() { return S().device; }
 int num_sms() { return S().sms; }
 void count_launch(int n) { S().launches += n; }
+bool capturing() { return S().capturing; }
+bool upload_settled(const LcStorage* st) { return st->upload_mark >= 0 && S().launches > st->upload_mark; }
+// On by default: every kernel launched through launch_chain waits for its
+// predecessor before touching memory, so each launch of the contract's ops
+// may start (and run its prologue) while the previous kernel finishes.
+// LAYA_CUDA_PDL=0 launches them fully serialised instead (both are tested).
 bool& pdl_flag() {
-  static thread_local bool on = false;
+  static const bool dflt = [] {
+    const char* v = getenv("LAYA_CUDA_PDL");
+    return !(v && v[0] == '0');
+  }();
+  static thread_local bool on = dflt;
   return on;
 }
 
@@ -131,6 +142,7 @@ LcTensor* alloc(int dtype, const std::vector<int64_t>& shape) {
     fail("out of device memory allocating " + std::to_string(bytes) + " bytes (the allocation cap of " +
          std::to_string(S().alloc_cap) + " bytes would be exceeded)");
   LcStorage* st = new LcStorage();
+  st->id = ++S().next_storage_id;
   st->bytes = bytes;
   st->ptr = dmalloc(st->bytes);
   S().live_bytes += (int64_t)st->bytes;
@@ -150,6 +162,7 @@ void release(LcTensor* t) {
   S().live.erase(t);
   t->magic = 0;
   if (--t->st->refs == 0) {
+    storage_released(t->st->id);
     if (!t->st->external) {
       dfree(t->st->ptr);
       S().live_bytes -= (int64_t)t->st->bytes;
@@ -254,12 +267,16 @@ int norm_axis(int axis, int ndim) {
 
 template <typename CT>
 __global__ void k_copy_convert(TV src, char* dst, int dst_dtype, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   LC_GRID_STRIDE(i, n) { st_as<CT>(dst, dst_dtype, i, ld_as<CT>(src.ptr, src.dtype, tv_offset(src, i))); }
 }
 
 // Same-dtype strided gather in 1/2/4/8-byte units (no conversion).
 template <typename U>
 __global__ void k_copy_raw(TV src, U* dst, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   LC_GRID_STRIDE(i, n) { dst[i] = ((const U*)src.ptr)[tv_offset(src, i)]; }
 }
 
@@ -267,6 +284,8 @@ __global__ void k_copy_raw(TV src, U* dst, int64_t n) {
 // 16-byte vectors (every row start 16-byte aligned): one 16-byte load and
 // store per thread step, the row offset computed once per vector.
 __global__ void k_copy_vec16(TV src, uint4* __restrict__ dst, int64_t nvec, int vpr, int epv) {
+  pdl_trigger();
+  pdl_wait();
   LC_GRID_STRIDE(i, nvec) {
     int64_t row = i / vpr, off = 0;
     const int c = (int)(i % vpr);
@@ -307,24 +326,24 @@ void copy_into(const LcTensor* src, LcTensor* dst) {
     if (vec) {
       const int vpr = (int)(src->shape[src->ndim - 1] / epv);
       const int64_t nvec = n / epv;
-      k_copy_vec16<<<blocks_for(nvec, threads), threads, 0, st>>>(s, (uint4*)dst->data(), nvec, vpr, epv);
+      lc::launch_chain(k_copy_vec16, dim3(blocks_for(nvec, threads)), dim3(threads), 0, st, s, (uint4*)dst->data(), nvec, vpr, epv);
       LC_LAUNCHED(1);
       return;
     }
     switch (dtype_size(src->dtype)) {
-      case 1: k_copy_raw<uint8_t><<<blocks, threads, 0, st>>>(s, (uint8_t*)dst->data(), n); break;
-      case 2: k_copy_raw<uint16_t><<<blocks, threads, 0, st>>>(s, (uint16_t*)dst->data(), n); break;
-      case 4: k_copy_raw<uint32_t><<<blocks, threads, 0, st>>>(s, (uint32_t*)dst->data(), n); break;
-      default: k_copy_raw<uint64_t><<<blocks, threads, 0, st>>>(s, (uint64_t*)dst->data(), n); break;
+      case 1: lc::launch_chain(k_copy_raw<uint8_t>, dim3(blocks), dim3(threads), 0, st, s, (uint8_t*)dst->data(), n); break;
+      case 2: lc::launch_chain(k_copy_raw<uint16_t>, dim3(blocks), dim3(threads), 0, st, s, (uint16_t*)dst->data(), n); break;
+      case 4: lc::launch_chain(k_copy_raw<uint32_t>, dim3(blocks), dim3(threads), 0, st, s, (uint32_t*)dst->data(), n); break;
+      default: lc::launch_chain(k_copy_raw<uint64_t>, dim3(blocks), dim3(threads), 0, st, s, (uint64_t*)dst->data(), n); break;
     }
   } else {
     // float -> int truncates toward zero; int -> float rounds to nearest.
     int ct = ct_for(src->dtype, dst->dtype);
     switch (ct) {
-      case 0: k_copy_convert<float><<<blocks, threads, 0, st>>>(s, dst->data(), dst->dtype, n); break;
-      case 1: k_copy_convert<int64_t><<<blocks, threads, 0, st>>>(s, dst->data(), dst->dtype, n); break;
-      case 2: k_copy_convert<double><<<blocks, threads, 0, st>>>(s, dst->data(), dst->dtype, n); break;
-      default: k_copy_convert<uint64_t><<<blocks, threads, 0, st>>>(s, dst->data(), dst->dtype, n); break;
+      case 0: lc::launch_chain(k_copy_convert<float>, dim3(blocks), dim3(threads), 0, st, s, dst->data(), dst->dtype, n); break;
+      case 1: lc::launch_chain(k_copy_convert<int64_t>, dim3(blocks), dim3(threads), 0, st, s, dst->data(), dst->dtype, n); break;
+      case 2: lc::launch_chain(k_copy_convert<double>, dim3(blocks), dim3(threads), 0, st, s, dst->data(), dst->dtype, n); break;
+      default: lc::launch_chain(k_copy_convert<uint64_t>, dim3(blocks), dim3(threads), 0, st, s, dst->data(), dst->dtype, n); break;
     }
   }
   count_launch(1);
@@ -425,6 +444,7 @@ int lc_from_host(lc_tensor* out, int dtype, const int64_t* shape, int ndim, cons
     // so the caller may reuse `data` at once (index.ts:146-154).
     CUDA_OK(cudaMemcpyAsync(t->data(), data, nbytes, cudaMemcpyHostToDevice, stream()));
   }
+  t->st->upload_mark = S().launches;
   *out = handle(t);
   LC_API_END
 }
@@ -714,6 +734,7 @@ int lc_graph_capture_end(uint64_t* out) {
   ensure_init();
   State& s = S();
   LC_CHECK(s.capturing, "graph capture: no capture in progress");
+  capture_ending(false);
   cudaGraph_t graph = nullptr;
   cudaError_t e = cudaStreamEndCapture(s.cur, &graph);
   const size_t unfreed = s.cap_allocs.size();
@@ -751,6 +772,7 @@ int lc_graph_capture_abort(void) {
   cudaStreamEndCapture(s.cur, &graph);
   cudaGetLastError();
   if (graph) cudaGraphDestroy(graph);
+  capture_ending(true);
   end_capture_state(nullptr);
   LC_API_END
 }
@@ -787,6 +809,8 @@ int lc_copy_into(lc_tensor dsth, lc_tensor srch) {
            "copyInto: dst " + std::string(dtype_name(dst->dtype)) + shape_str(dst->dims()) + " vs src " + dtype_name(src->dtype) +
                shape_str(src->dims()));
   LC_CHECK(dst->contiguous(), "copyInto: the destination must be dense");
+  dst->st->upload_mark = -1;
+  dst->st->version++;
   copy_into(src, dst);
   LC_API_END
 }

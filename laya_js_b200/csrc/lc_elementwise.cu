@@ -144,6 +144,8 @@ __device__ __forceinline__ double un_op<double>(int op, double x, double s) {
 
 template <typename CT>
 __global__ void k_binary(TV a, TV b, char* out, int out_dtype, int op, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   LC_GRID_STRIDE(i, n) {
     CT x = ld_as<CT>(a.ptr, a.dtype, tv_offset(a, i));
     CT y = ld_as<CT>(b.ptr, b.dtype, tv_offset(b, i));
@@ -153,11 +155,15 @@ __global__ void k_binary(TV a, TV b, char* out, int out_dtype, int op, int64_t n
 
 template <typename CT>
 __global__ void k_unary(TV a, char* out, int out_dtype, int op, double s, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   LC_GRID_STRIDE(i, n) { st_as<CT>(out, out_dtype, i, un_op<CT>(op, ld_as<CT>(a.ptr, a.dtype, tv_offset(a, i)), s)); }
 }
 
 template <typename CT>
 __global__ void k_where(TV c, TV a, TV b, char* out, int out_dtype, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   LC_GRID_STRIDE(i, n) {
     bool cv = ld_as<int64_t>(c.ptr, c.dtype, tv_offset(c, i)) != 0;
     if (c.dtype == LC_F32 || c.dtype == LC_F16 || c.dtype == LC_BF16 || c.dtype == LC_F64)
@@ -227,6 +233,8 @@ template <> struct Vec<__nv_bfloat16> {
 // bn == N (row length) for a row-broadcast operand. n and bn are multiples of V::N.
 template <typename T, int OP>
 __global__ void __launch_bounds__(256) k_vec_binary(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ out, int64_t n, int64_t bn) {
+  pdl_trigger();
+  pdl_wait();
   using V = Vec<T>;
   const int64_t nv = n / V::N;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
@@ -242,6 +250,8 @@ __global__ void __launch_bounds__(256) k_vec_binary(const T* __restrict__ a, con
 
 template <typename T, int OP>
 __global__ void __launch_bounds__(256) k_vec_unary(const T* __restrict__ a, T* __restrict__ out, int64_t n, float s) {
+  pdl_trigger();
+  pdl_wait();
   using V = Vec<T>;
   const int64_t nv = n / V::N;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
@@ -288,11 +298,11 @@ bool try_vec_binary(int op, LcTensor* a, LcTensor* b, LcTensor* y) {
   T* po = (T*)y->data();
   cudaStream_t st = stream();
   switch (op) {
-    case OP_ADD: k_vec_binary<T, OP_ADD><<<blocks, 256, 0, st>>>(pa, pb, po, n, bn); break;
-    case OP_SUB: k_vec_binary<T, OP_SUB><<<blocks, 256, 0, st>>>(pa, pb, po, n, bn); break;
-    case OP_MUL: k_vec_binary<T, OP_MUL><<<blocks, 256, 0, st>>>(pa, pb, po, n, bn); break;
-    case OP_DIV: k_vec_binary<T, OP_DIV><<<blocks, 256, 0, st>>>(pa, pb, po, n, bn); break;
-    case OP_MAX: k_vec_binary<T, OP_MAX><<<blocks, 256, 0, st>>>(pa, pb, po, n, bn); break;
+    case OP_ADD: lc::launch_chain(k_vec_binary<T, OP_ADD>, dim3(blocks), dim3(256), 0, st, pa, pb, po, n, bn); break;
+    case OP_SUB: lc::launch_chain(k_vec_binary<T, OP_SUB>, dim3(blocks), dim3(256), 0, st, pa, pb, po, n, bn); break;
+    case OP_MUL: lc::launch_chain(k_vec_binary<T, OP_MUL>, dim3(blocks), dim3(256), 0, st, pa, pb, po, n, bn); break;
+    case OP_DIV: lc::launch_chain(k_vec_binary<T, OP_DIV>, dim3(blocks), dim3(256), 0, st, pa, pb, po, n, bn); break;
+    case OP_MAX: lc::launch_chain(k_vec_binary<T, OP_MAX>, dim3(blocks), dim3(256), 0, st, pa, pb, po, n, bn); break;
     default: return false;
   }
   LC_LAUNCHED(1);
@@ -309,12 +319,12 @@ bool try_vec_unary(int op, LcTensor* a, LcTensor* y, double s) {
   T* po = (T*)y->data();
   cudaStream_t st = stream();
   switch (op) {
-    case OP_EXP: k_vec_unary<T, OP_EXP><<<blocks, 256, 0, st>>>(pa, po, n, 0.f); break;
-    case OP_RELU: k_vec_unary<T, OP_RELU><<<blocks, 256, 0, st>>>(pa, po, n, 0.f); break;
-    case OP_GELU: k_vec_unary<T, OP_GELU><<<blocks, 256, 0, st>>>(pa, po, n, 0.f); break;
+    case OP_EXP: lc::launch_chain(k_vec_unary<T, OP_EXP>, dim3(blocks), dim3(256), 0, st, pa, po, n, 0.f); break;
+    case OP_RELU: lc::launch_chain(k_vec_unary<T, OP_RELU>, dim3(blocks), dim3(256), 0, st, pa, po, n, 0.f); break;
+    case OP_GELU: lc::launch_chain(k_vec_unary<T, OP_GELU>, dim3(blocks), dim3(256), 0, st, pa, po, n, 0.f); break;
     case OP_SCALE:
       if (std::is_same<T, float>::value) return false;  // f32 scale keeps double math in the generic path
-      k_vec_unary<T, OP_SCALE><<<blocks, 256, 0, st>>>(pa, po, n, (float)s); break;
+      lc::launch_chain(k_vec_unary<T, OP_SCALE>, dim3(blocks), dim3(256), 0, st, pa, po, n, (float)s); break;
     default: return false;
   }
   LC_LAUNCHED(1);
@@ -363,10 +373,10 @@ LcTensor* binary(int op, uint64_t ah, uint64_t bh, const char* name) {
   unsigned blocks = blocks_for(n, 256);
   cudaStream_t st = stream();
   switch (ct) {
-    case 0: k_binary<float><<<blocks, 256, 0, st>>>(va, vb, y->data(), odt, op, n); break;
-    case 1: k_binary<int64_t><<<blocks, 256, 0, st>>>(va, vb, y->data(), odt, op, n); break;
-    case 2: k_binary<double><<<blocks, 256, 0, st>>>(va, vb, y->data(), odt, op, n); break;
-    default: k_binary<uint64_t><<<blocks, 256, 0, st>>>(va, vb, y->data(), odt, op, n); break;
+    case 0: lc::launch_chain(k_binary<float>, dim3(blocks), dim3(256), 0, st, va, vb, y->data(), odt, op, n); break;
+    case 1: lc::launch_chain(k_binary<int64_t>, dim3(blocks), dim3(256), 0, st, va, vb, y->data(), odt, op, n); break;
+    case 2: lc::launch_chain(k_binary<double>, dim3(blocks), dim3(256), 0, st, va, vb, y->data(), odt, op, n); break;
+    default: lc::launch_chain(k_binary<uint64_t>, dim3(blocks), dim3(256), 0, st, va, vb, y->data(), odt, op, n); break;
   }
   LC_LAUNCHED(1);
   return y;
@@ -405,10 +415,10 @@ LcTensor* unary(int op, uint64_t xh, const char* name, double s = 0.0) {
   unsigned blocks = blocks_for(n, 256);
   cudaStream_t st = stream();
   switch (ct) {
-    case 0: k_unary<float><<<blocks, 256, 0, st>>>(vx, y->data(), odt, op, s, n); break;
-    case 1: k_unary<int64_t><<<blocks, 256, 0, st>>>(vx, y->data(), odt, op, s, n); break;
-    case 2: k_unary<double><<<blocks, 256, 0, st>>>(vx, y->data(), odt, op, s, n); break;
-    default: k_unary<uint64_t><<<blocks, 256, 0, st>>>(vx, y->data(), odt, op, s, n); break;
+    case 0: lc::launch_chain(k_unary<float>, dim3(blocks), dim3(256), 0, st, vx, y->data(), odt, op, s, n); break;
+    case 1: lc::launch_chain(k_unary<int64_t>, dim3(blocks), dim3(256), 0, st, vx, y->data(), odt, op, s, n); break;
+    case 2: lc::launch_chain(k_unary<double>, dim3(blocks), dim3(256), 0, st, vx, y->data(), odt, op, s, n); break;
+    default: lc::launch_chain(k_unary<uint64_t>, dim3(blocks), dim3(256), 0, st, vx, y->data(), odt, op, s, n); break;
   }
   LC_LAUNCHED(1);
   return y;
@@ -419,6 +429,8 @@ LcTensor* unary(int op, uint64_t xh, const char* name, double s = 0.0) {
 // Converting copy into a strided destination (used by concat).
 template <typename CT>
 __global__ void k_copy_to_strided(TV src, TV dst, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   LC_GRID_STRIDE(i, n) { st_as<CT>(dst.ptr, dst.dtype, tv_offset(dst, i), ld_as<CT>(src.ptr, src.dtype, tv_offset(src, i))); }
 }
 
@@ -431,10 +443,10 @@ void lc_internal_copy_strided(const LcTensor* src, LcTensor* dst) {
   if (src->dtype == LC_U64 || dst->dtype == LC_U64) ct = 3;
   if (is_float(src->dtype) && !is_float(dst->dtype)) ct = 2;
   switch (ct) {
-    case 0: k_copy_to_strided<float><<<blocks, 256, 0, stream()>>>(s, d, n); break;
-    case 1: k_copy_to_strided<int64_t><<<blocks, 256, 0, stream()>>>(s, d, n); break;
-    case 2: k_copy_to_strided<double><<<blocks, 256, 0, stream()>>>(s, d, n); break;
-    default: k_copy_to_strided<uint64_t><<<blocks, 256, 0, stream()>>>(s, d, n); break;
+    case 0: lc::launch_chain(k_copy_to_strided<float>, dim3(blocks), dim3(256), 0, stream(), s, d, n); break;
+    case 1: lc::launch_chain(k_copy_to_strided<int64_t>, dim3(blocks), dim3(256), 0, stream(), s, d, n); break;
+    case 2: lc::launch_chain(k_copy_to_strided<double>, dim3(blocks), dim3(256), 0, stream(), s, d, n); break;
+    default: lc::launch_chain(k_copy_to_strided<uint64_t>, dim3(blocks), dim3(256), 0, stream(), s, d, n); break;
   }
   LC_LAUNCHED(1);
 }
@@ -498,10 +510,10 @@ int lc_where(lc_tensor* out, lc_tensor ch, lc_tensor ah, lc_tensor bh) {
     int ct = ctype_of(a->dtype, b->dtype);
     if (odt == LC_U64) ct = 3;
     switch (ct) {
-      case 0: k_where<float><<<blocks, 256, 0, stream()>>>(vc, va, vb, y->data(), odt, n); break;
-      case 1: k_where<int64_t><<<blocks, 256, 0, stream()>>>(vc, va, vb, y->data(), odt, n); break;
-      case 2: k_where<double><<<blocks, 256, 0, stream()>>>(vc, va, vb, y->data(), odt, n); break;
-      default: k_where<uint64_t><<<blocks, 256, 0, stream()>>>(vc, va, vb, y->data(), odt, n); break;
+      case 0: lc::launch_chain(k_where<float>, dim3(blocks), dim3(256), 0, stream(), vc, va, vb, y->data(), odt, n); break;
+      case 1: lc::launch_chain(k_where<int64_t>, dim3(blocks), dim3(256), 0, stream(), vc, va, vb, y->data(), odt, n); break;
+      case 2: lc::launch_chain(k_where<double>, dim3(blocks), dim3(256), 0, stream(), vc, va, vb, y->data(), odt, n); break;
+      default: lc::launch_chain(k_where<uint64_t>, dim3(blocks), dim3(256), 0, stream(), vc, va, vb, y->data(), odt, n); break;
     }
     LC_LAUNCHED(1);
   }

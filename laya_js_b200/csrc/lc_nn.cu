@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
 template <typename T, int MAXV, typename WT = float>
 __global__ void __launch_bounds__(256) k_layernorm_blk(const T* __restrict__ x, const WT* __restrict__ w, const WT* __restrict__ b,
                                                        T* __restrict__ y, int64_t rows, int N, float eps) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int VN = 16 / sizeof(T);
   __shared__ float sm[8];
   const int nv = N / VN;
@@ -180,10 +182,10 @@ void launch_layernorm_blk(const T* x, const WT* w, const WT* b, T* y, int64_t ro
   const int per = (N / VN + 255) / 256;
   const unsigned blocks = (unsigned)std::min<int64_t>(rows, (int64_t)lc::num_sms() * 8);
   switch (per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8) {
-    case 1: k_layernorm_blk<T, 1, WT><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    case 2: k_layernorm_blk<T, 2, WT><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    case 4: k_layernorm_blk<T, 4, WT><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
-    default: k_layernorm_blk<T, 8, WT><<<blocks, 256, 0, st>>>(x, w, b, y, rows, N, eps); break;
+    case 1: lc::launch_chain(k_layernorm_blk<T, 1, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 2: lc::launch_chain(k_layernorm_blk<T, 2, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 4: lc::launch_chain(k_layernorm_blk<T, 4, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    default: lc::launch_chain(k_layernorm_blk<T, 8, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
   }
 }
 
@@ -250,6 +252,8 @@ __global__ void k_layernorm_generic(const char* x, int xdt, const char* w, int w
 // out row r = table[ids[r]] (zeros for an out-of-range id)
 __global__ void k_gather_rows(const char* table, int64_t V, int64_t rowbytes, const char* ids, int iddt, char* out, int64_t n,
                               int64_t group, const int64_t group_rows) {
+  pdl_trigger();
+  pdl_wait();
   // group/group_rows: for gatherRows, row r reads from batch r / group, offset batch*group_rows
   int lane = threadIdx.x & 31;
   int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -302,6 +306,8 @@ __global__ void k_rope(TV x, const float* __restrict__ cs, int64_t rows, int64_t
 // cos / sin quads of the position, two 4-element stores; 32-bit index math.
 template <typename T>
 __global__ void __launch_bounds__(256) k_rope_vec(TV x, const float* __restrict__ cs, int rows, int L, int half, int cap, T* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int qpr = half / 4;
   const int64_t n = (int64_t)rows * qpr;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
@@ -347,6 +353,51 @@ __global__ void __launch_bounds__(256) k_rope_vec(TV x, const float* __restrict_
   }
 }
 
+// 16-bit rows with half % 8 == 0, rows 8-element strided and 16-byte aligned:
+// one thread per 8 pairs, 16-byte loads and stores of x and y, the position's
+// cos / sin as four float4 loads. The row offset is split into the row's
+// position l (fastest) and the rows above it, whose offsets a table of the
+// leading dims' strides gives with at most two divisions.
+template <typename T>
+__global__ void __launch_bounds__(256) k_rope_vec8(TV x, const float* __restrict__ cs, int rows, int L, int half, int cap, T* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int qpr = half / 8;
+  const int64_t n = (int64_t)rows * qpr;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(t / qpr), i = (int)(t % qpr) * 8;
+    const int l = r % L;
+    int64_t off = (int64_t)l * x.strides[x.ndim - 2];
+    int rr = r / L;
+    for (int d = x.ndim - 3; d >= 0; d--) {
+      const int sh = (int)x.shape[d];
+      off += (int64_t)(rr % sh) * x.strides[d];
+      rr /= sh;
+    }
+    const T* p = (const T*)x.ptr + off + i;
+    const uint4 ua = *(const uint4*)p, ub = *(const uint4*)(p + half);
+    const T* ha = (const T*)&ua;
+    const T* hb = (const T*)&ub;
+    const float4* cp = (const float4*)(cs + (int64_t)l * half + i);
+    const float4* sp = (const float4*)(cs + (int64_t)cap * half + (int64_t)l * half + i);
+    const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+    const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    uint4 ra, rb;
+    T* ya = (T*)&ra;
+    T* yb = (T*)&rb;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float a = to_f(ha[j]), b = to_f(hb[j]);
+      ya[j] = from_f<T>(a * cc[j] - b * ss[j]);
+      yb[j] = from_f<T>(b * cc[j] + a * ss[j]);
+    }
+    T* o = out + (int64_t)r * 2 * half + i;
+    *(uint4*)o = ra;
+    *(uint4*)(o + half) = rb;
+  }
+}
+
 namespace {
 struct RopeTable {
   float* d = nullptr;
@@ -355,6 +406,12 @@ struct RopeTable {
 std::map<std::tuple<int, double, bool>, RopeTable>& rope_cache() {
   static std::map<std::tuple<int, double, bool>, RopeTable> m;
   return m;
+}
+// Outgrown tables stay allocated until the caches are destroyed: a recorded
+// CUDA graph (Backend.compile) keeps the pointer it was captured with.
+std::vector<float*>& rope_retired() {
+  static std::vector<float*> v;
+  return v;
 }
 }  // namespace
 
@@ -388,7 +445,7 @@ const float* rope_table(int D, double base, int L, int* cap_out, bool position_m
         }
       }
     }
-    if (t.d) CUDA_OK(cudaFree(t.d));
+    if (t.d) rope_retired().push_back(t.d);
     CUDA_OK(cudaMalloc(&t.d, h.size() * sizeof(float)));
     CUDA_OK(cudaMemcpy(t.d, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
     t.cap = cap;
@@ -402,6 +459,8 @@ void lc_internal_destroy_caches() {
   for (auto& kv : rope_cache())
     if (kv.second.d) cudaFree(kv.second.d);
   rope_cache().clear();
+  for (float* d : rope_retired()) cudaFree(d);
+  rope_retired().clear();
   lc_gemm_destroy_caches();
 }
 
@@ -480,6 +539,8 @@ __global__ void __launch_bounds__(128) k_sdpa_generic(TV q, TV k, TV v, TV m, in
 
 template <typename T>
 __global__ void __launch_bounds__(256) k_geglu_vec(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int64_t F) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int VN = 16 / sizeof(T);
   int64_t nv = F / VN;
   LC_GRID_STRIDE(t, rows * nv) {
@@ -684,6 +745,8 @@ __global__ void __launch_bounds__(256) k_matmul(MM p) {
 // The 64 x 64-tile SIMT kernel would put only ceil(N/64) blocks on the GPU.
 __global__ void __launch_bounds__(256) k_linear_rows(const char* x, int xdt, const char* w, int wdt, const char* bias, int bdt, char* y,
                                                      int ydt, int64_t M, int64_t N, int64_t K) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= M * N) return;
@@ -695,6 +758,37 @@ __global__ void __launch_bounds__(256) k_linear_rows(const char* x, int xdt, con
   if (lane == 0) {
     if (bias) acc += ld_as<float>(bias, bdt, n);
     st_as<float>(y, ydt, m * N + n, acc);
+  }
+}
+
+// The same for dense 16-bit x and w rows with K % 8 == 0 and 16-byte aligned
+// rows: 16-byte loads, the whole K range of a lane in flight at once.
+template <typename T>
+__global__ void __launch_bounds__(256) k_linear_rows16(const T* __restrict__ x, const T* __restrict__ w, const char* bias, int bdt, char* y,
+                                                       int ydt, int M, int N, int K) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= (int64_t)M * N) return;
+  const int m = (int)(warp / N), n = (int)(warp % N);
+  const uint4* xr = (const uint4*)(x + (int64_t)m * K);
+  const uint4* wr = (const uint4*)(w + (int64_t)n * K);
+  const int nv = K / 8;
+  float acc = 0.f;
+#pragma unroll 4
+  for (int v = lane; v < nv; v += 32) {
+    const uint4 a = __ldg(xr + v), b = __ldg(wr + v);
+    const T* ae = (const T*)&a;
+    const T* be = (const T*)&b;
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc = fmaf(to_f<T>(ae[j]), to_f<T>(be[j]), acc);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) {
+    if (bias) acc += ld_as<float>(bias, bdt, n);
+    st_as<float>(y, ydt, (int64_t)m * N + n, acc);
   }
 }
 
@@ -729,9 +823,18 @@ void linear_simt(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, Lc
   p.nb = 0;
   const bool dbl = y->dtype == LC_F64 || x2->dtype == LC_F64 || w->dtype == LC_F64;
   if (p.m && p.n && p.m <= 16 && !dbl && p.m * p.n < ((int64_t)1 << 26)) {
-    const int64_t threads = p.m * p.n * 32;
-    k_linear_rows<<<(unsigned)((threads + 255) / 256), 256, 0, stream()>>>(p.a, p.adt, p.b, p.bdt, p.bias, p.biasdt, p.c, p.cdt, p.m, p.n,
-                                                                        p.k);
+    const unsigned blocks = (unsigned)((p.m * p.n * 32 + 255) / 256);
+    const bool v16 = is_half(x2->dtype) && w->dtype == x2->dtype && p.k % 8 == 0 && p.k < INT32_MAX &&
+                     (((uintptr_t)p.a | (uintptr_t)p.b) & 15) == 0;
+    if (v16 && x2->dtype == LC_F16)
+      lc::launch_chain(k_linear_rows16<__half>, dim3(blocks), dim3(256), 0, stream(), (const __half*)p.a, (const __half*)p.b, p.bias,
+                       p.biasdt, p.c, p.cdt, (int)p.m, (int)p.n, (int)p.k);
+    else if (v16)
+      lc::launch_chain(k_linear_rows16<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream(), (const __nv_bfloat16*)p.a,
+                       (const __nv_bfloat16*)p.b, p.bias, p.biasdt, p.c, p.cdt, (int)p.m, (int)p.n, (int)p.k);
+    else
+      lc::launch_chain(k_linear_rows, dim3(blocks), dim3(256), 0, stream(), p.a, p.adt, p.b, p.bdt, p.bias, p.biasdt, p.c, p.cdt, p.m,
+                       p.n, p.k);
     LC_LAUNCHED(1);
     return;
   }
@@ -831,7 +934,7 @@ int lc_embedding(lc_tensor* out, lc_tensor th, lc_tensor ih) {
   if (n && t0->shape[1]) {
     LcTensor* t = contiguous(t0);
     LcTensor* ids = contiguous(i0);
-    k_gather_rows<<<blocks_for(n * 32, 256), 256, 0, stream()>>>(t->data(), t->shape[0], t->shape[1] * dtype_size(t->dtype),
+    lc::launch_chain(k_gather_rows, dim3(blocks_for(n * 32, 256)), dim3(256), 0, stream(), t->data(), t->shape[0], t->shape[1] * dtype_size(t->dtype),
                                                                  ids->data(), ids->dtype, y->data(), n, 0, 0);
     LC_LAUNCHED(1);
     if (t != t0) release(t);
@@ -851,7 +954,7 @@ int lc_gather_rows(lc_tensor* out, lc_tensor xh, lc_tensor ih) {
   if (B * M && D) {
     LcTensor* x = contiguous(x0);
     LcTensor* ids = contiguous(i0);
-    k_gather_rows<<<blocks_for(B * M * 32, 256), 256, 0, stream()>>>(x->data(), L, D * dtype_size(x->dtype), ids->data(), ids->dtype,
+    lc::launch_chain(k_gather_rows, dim3(blocks_for(B * M * 32, 256)), dim3(256), 0, stream(), x->data(), L, D * dtype_size(x->dtype), ids->data(), ids->dtype,
                                                                      y->data(), B * M, M, L);
     LC_LAUNCHED(1);
     if (x != x0) release(x);
@@ -884,13 +987,23 @@ int lc_rope(lc_tensor* out, lc_tensor xh, double base) {
                (odt == LC_F32 || odt == LC_F16 || odt == LC_BF16) && ((uintptr_t)x->data() % (4 * dtype_size(odt))) == 0 &&
                [&] {
                  for (int d = 0; d < x->ndim - 1; d++)
-                   if (x->strides[d] % 4 || x->shape[d] >= INT32_MAX) return false;
+                   if ((x->shape[d] > 1 && x->strides[d] % 4) || x->shape[d] >= INT32_MAX) return false;  // a size-1 axis's stride is never used
                  return true;
                }()) {
-      const unsigned blocks = blocks_for(rows * (D / 8), 256);
-      if (odt == LC_F32) k_rope_vec<float><<<blocks, 256, 0, stream()>>>(v, cs, (int)rows, (int)L, (int)(D / 2), cap, (float*)y->data());
-      else if (odt == LC_F16) k_rope_vec<__half><<<blocks, 256, 0, stream()>>>(v, cs, (int)rows, (int)L, (int)(D / 2), cap, (__half*)y->data());
-      else k_rope_vec<__nv_bfloat16><<<blocks, 256, 0, stream()>>>(v, cs, (int)rows, (int)L, (int)(D / 2), cap, (__nv_bfloat16*)y->data());
+      const bool v8 = odt != LC_F32 && (D / 2) % 8 == 0 && ((uintptr_t)x->data() % 16) == 0 && [&] {
+        for (int d = 0; d < x->ndim - 1; d++)
+          if (x->shape[d] > 1 && x->strides[d] % 8) return false;
+        return true;
+      }();
+      const unsigned blocks = blocks_for(rows * (D / (v8 ? 16 : 8)), 256);
+      if (v8 && odt == LC_F16)
+        lc::launch_chain(k_rope_vec8<__half>, dim3(blocks), dim3(256), 0, stream(), v, cs, (int)rows, (int)L, (int)(D / 2), cap, (__half*)y->data());
+      else if (v8)
+        lc::launch_chain(k_rope_vec8<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream(), v, cs, (int)rows, (int)L, (int)(D / 2), cap,
+                         (__nv_bfloat16*)y->data());
+      else if (odt == LC_F32) lc::launch_chain(k_rope_vec<float>, dim3(blocks), dim3(256), 0, stream(), v, cs, (int)rows, (int)L, (int)(D / 2), cap, (float*)y->data());
+      else if (odt == LC_F16) lc::launch_chain(k_rope_vec<__half>, dim3(blocks), dim3(256), 0, stream(), v, cs, (int)rows, (int)L, (int)(D / 2), cap, (__half*)y->data());
+      else lc::launch_chain(k_rope_vec<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream(), v, cs, (int)rows, (int)L, (int)(D / 2), cap, (__nv_bfloat16*)y->data());
     } else {
       k_rope<<<blocks_for(rows * (D / 2), 256), 256, 0, stream()>>>(v, cs, rows, L, (int)(D / 2), cap, y->data());
     }
@@ -955,9 +1068,9 @@ int lc_geglu(lc_tensor* out, lc_tensor xh) {
     cudaStream_t st = stream();
     if (vec) {
       unsigned blocks = blocks_for(rows * F / vn, 256);
-      if (odt == LC_F16) k_geglu_vec<__half><<<blocks, 256, 0, st>>>((const __half*)x->data(), (__half*)y->data(), rows, F);
-      else if (odt == LC_BF16) k_geglu_vec<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)x->data(), (__nv_bfloat16*)y->data(), rows, F);
-      else k_geglu_vec<float><<<blocks, 256, 0, st>>>((const float*)x->data(), (float*)y->data(), rows, F);
+      if (odt == LC_F16) lc::launch_chain(k_geglu_vec<__half>, dim3(blocks), dim3(256), 0, st, (const __half*)x->data(), (__half*)y->data(), rows, F);
+      else if (odt == LC_BF16) lc::launch_chain(k_geglu_vec<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, (const __nv_bfloat16*)x->data(), (__nv_bfloat16*)y->data(), rows, F);
+      else lc::launch_chain(k_geglu_vec<float>, dim3(blocks), dim3(256), 0, st, (const float*)x->data(), (float*)y->data(), rows, F);
     } else if (x->dtype == LC_F64) {
       k_geglu_generic<double><<<blocks_for(rows * F, 256), 256, 0, st>>>(x->data(), x->dtype, y->data(), odt, rows, F);
     } else {
@@ -1060,8 +1173,15 @@ int lc_linear(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh) {
     LcTensor* b = b0 ? contiguous(b0) : nullptr;
     LcTensor* x2 = view_of(x, {M, K}, {K, 1}, x->offset);
     bool done = false;
-    if (is_half(odt) && x->dtype == odt && w->dtype == odt && (!b || is_float(b->dtype)))
-      done = gemm_linear(x2, w, b, y, GemmEpilogue{});
+    // Few rows of a small product (a head over a handful of marker rows, a
+    // one-row projection): a warp per output finishes before the tensor-core
+    // GEMM's pipeline fills.
+    const bool few = M <= 16 && M * N * K <= ((int64_t)1 << 23);
+    if (!few && is_half(odt) && x->dtype == odt && w->dtype == odt && (!b || is_float(b->dtype))) {
+      GemmEpilogue ep{};
+      ep.w_static = w == w0 && upload_settled(w->st);  // weight blocks requested before the dependency wait
+      done = gemm_linear(x2, w, b, y, ep);
+    }
     if (!done) {
       LcTensor* y2 = view_of(y, {M, N}, {N, 1}, 0);
       linear_simt(x2, w, b, y2);

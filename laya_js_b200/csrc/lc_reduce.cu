@@ -121,6 +121,8 @@ __global__ void k_softmax_cols(const char* x, int dtype, char* out, int out_dtyp
 // n <= 32 * (16 / sizeof(T)) * MAXV.
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int n) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int VEC = 16 / sizeof(T);
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -219,6 +221,8 @@ struct VecPick<float, OP> {
 // is a template parameter so the per-element loop carries no branch on it
 template <typename T, int MAXV, int OP>
 __global__ void __launch_bounds__(256) k_reduce_rows_vec(const T* __restrict__ x, char* out, int out_dtype, int64_t rows, int n) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int VEC = 16 / sizeof(T);
   constexpr int op = OP;
   const int lane = threadIdx.x & 31;
@@ -509,10 +513,10 @@ int row_vec_maxv(int dtype, int64_t n) {
 template <typename T, int MAXV>
 void launch_reduce_vec_op(unsigned blocks, int op, const T* x, char* out, int odt, int64_t rows, int n) {
   switch (op) {
-    case R_SUM: k_reduce_rows_vec<T, MAXV, R_SUM><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
-    case R_MEAN: k_reduce_rows_vec<T, MAXV, R_MEAN><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
-    case R_MAX: k_reduce_rows_vec<T, MAXV, R_MAX><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
-    default: k_reduce_rows_vec<T, MAXV, R_MIN><<<blocks, 256, 0, stream()>>>(x, out, odt, rows, n); break;
+    case R_SUM: lc::launch_chain(k_reduce_rows_vec<T, MAXV, R_SUM>, dim3(blocks), dim3(256), 0, stream(), x, out, odt, rows, n); break;
+    case R_MEAN: lc::launch_chain(k_reduce_rows_vec<T, MAXV, R_MEAN>, dim3(blocks), dim3(256), 0, stream(), x, out, odt, rows, n); break;
+    case R_MAX: lc::launch_chain(k_reduce_rows_vec<T, MAXV, R_MAX>, dim3(blocks), dim3(256), 0, stream(), x, out, odt, rows, n); break;
+    default: lc::launch_chain(k_reduce_rows_vec<T, MAXV, R_MIN>, dim3(blocks), dim3(256), 0, stream(), x, out, odt, rows, n); break;
   }
 }
 template <typename T, int MAXV>

@@ -135,3 +135,21 @@ def test_decision_model_base_shape_compiled_equals_eager():
         assert np.array_equal(got["logits"], want["logits"]) and np.array_equal(got["act"], want["act"])
     del run
     model.dispose()
+
+
+def test_recorded_rope_survives_a_longer_sequence():
+    """A recording keeps the cos/sin table it was captured with: a later eager
+    rope over more positions (a larger table for the same head dim and base)
+    must not free it under the graph."""
+    b = backend()
+    base = 12345.0  # a base no other test uses: the table starts at this test's length
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((1, 2, 40, 64)).astype(np.float32)
+    cf = b.compile(lambda t: b.rope(t, base))
+    tx = _f32(b, x.shape, x)
+    want = b.read(b.rope(tx, base)).data.copy()
+    cf(tx)
+    assert np.array_equal(b.read(cf(tx)).data, want)
+    long = rng.standard_normal((1, 1, 3000, 64)).astype(np.float32)
+    b.read(b.rope(_f32(b, long.shape, long), base))  # grows the table past 40 positions
+    assert np.array_equal(b.read(cf(tx)).data, want)

@@ -92,3 +92,33 @@ def test_mean_pool_masks(dt):
     assert got.shape == (B, D)
     assert np.abs(got - ref).max() < 1e-5
     assert np.all(got[2] == 0)
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("D", [64, 48, 40, 6])
+def test_rope_paths_against_f64(dt, D):
+    """rope (index.ts:225-229) on every kernel: 8 pairs per thread with 16-byte
+    loads (16-bit, half % 8 == 0), 4 pairs (half % 4 == 0), the generic one;
+    dense rows, the strided q/k views ModernBert.layer makes (reshape ->
+    transpose -> split of the QKV projection), and a batch of one (whose
+    size-1 axis carries an arbitrary stride)."""
+    from oracle import ops as O
+    b = backend()
+    rng = np.random.default_rng(D)
+    B, H, L = 2, 3, 37
+    x = rng.standard_normal((B, H, L, D)).astype(np.float32)
+    hx = _host(dt, x)
+    ref = O.rope(to_f32(hx), 10000.0)
+    got = to_f32(b.read(b.rope(b.fromHost(hx), 10000.0)))
+    tol = {"f32": 1e-5, "f16": 2e-3, "bf16": 1.6e-2}[dt] * (1 + np.abs(ref))
+    assert np.all(np.abs(got - ref) <= tol)
+    for Bv in (B, 1):
+        qkv = rng.standard_normal((Bv, L, 3, H, D)).astype(np.float32)
+        hq = _host(dt, qkv)
+        t = b.transpose(b.fromHost(hq), [2, 0, 3, 1, 4])
+        q, k, _ = [b.reshape(s, [Bv, H, L, D]) for s in b.split(t, 3, 0)]
+        vals = to_f32(hq).transpose(2, 0, 3, 1, 4)
+        for view, i in ((q, 0), (k, 1)):
+            ref = O.rope(vals[i], 10000.0)
+            got = to_f32(b.read(b.rope(view, 10000.0)))
+            assert np.all(np.abs(got - ref) <= {"f32": 1e-5, "f16": 2e-3, "bf16": 1.6e-2}[dt] * (1 + np.abs(ref)))

@@ -130,3 +130,81 @@ def test_sdpa_tcgen05_batch_of_one():
     assert not _dense(out), "expected the tcgen05 path"
     err = np.abs(to_f32(b.read(out)) - O.sdpa(r[0], r[1], r[2], mask, 0.125)).max()
     assert err < TOL["f16"], f"max err {err}"
+
+
+def _stats(b):
+    import ctypes as C
+    from laya_js_b200 import _lib
+    lt, lb, ln = C.c_int64(), C.c_int64(), C.c_int64()
+    _lib.call("lc_stats", C.byref(lt), C.byref(lb), C.byref(ln))
+    return lt.value, lb.value, ln.value
+
+
+def test_sdpa_packed_mask_reused_and_invalidated():
+    """One mask tensor across calls (a forward's layers) is packed once; a
+    write into it (lc_copy_into, what a compiled replay does to its inputs)
+    is packed again; no tensor outlives the calls."""
+    import ctypes as C
+    from laya_js_b200 import _lib
+    b = backend()
+    rng = np.random.default_rng(21)
+    B, H, L = 2, 3, 200
+    q, qr = _up(b, rng.standard_normal((B, H, L, 64)), "f16")
+    k, kr = _up(b, rng.standard_normal((B, H, L, 64)), "f16")
+    v, vr = _up(b, rng.standard_normal((B, H, L, 64)), "f16")
+    valid = np.ones((B, L), bool)
+    valid[1, 150:] = False
+    m1 = M.attention_masks(valid, 128)[1]
+    valid[0, 60:] = False
+    m2 = M.attention_masks(valid, 128)[1]
+
+    def run(tm):
+        n0 = _stats(b)[2]
+        t = b.sdpa(q, k, v, tm, 0.125)
+        n = _stats(b)[2] - n0
+        y = to_f32(b.read(t))
+        b.dispose(t)
+        return y, n
+    b.flush()
+    bytes0 = _stats(b)[1]
+    tm = b.fromHost(HostTensor("bool", m1.shape, m1.astype(np.uint8)))
+    mask_bytes = _stats(b)[1] - bytes0
+    ys = [run(tm) for _ in range(3)]
+    assert [n for _, n in ys] == [2, 1, 1], f"mask packed once, then attention alone: {[n for _, n in ys]}"
+    assert np.array_equal(ys[0][0], ys[1][0]) and np.array_equal(ys[0][0], ys[2][0])
+    assert np.abs(ys[0][0] - O.sdpa(qr, kr, vr, m1, 0.125)).max() < TOL["f16"]
+    src = b.fromHost(HostTensor("bool", m2.shape, m2.astype(np.uint8)))
+    _lib.call("lc_copy_into", C.c_uint64(tm.handle), C.c_uint64(src.handle))
+    b.dispose(src)
+    y2, n = run(tm)
+    assert n == 2, "a written mask is packed again"
+    assert np.abs(y2 - O.sdpa(qr, kr, vr, m2, 0.125)).max() < TOL["f16"]
+    b.flush()
+    assert _stats(b)[1] == bytes0 + mask_bytes
+    b.dispose(tm)
+    b.flush()
+    assert _stats(b)[1] == bytes0
+
+
+def test_sdpa_packed_mask_inside_a_recording():
+    """Backend.compile over two sdpa calls sharing a mask: the replay packs the
+    replayed mask (not one cached before the recording) and matches eager."""
+    b = backend()
+    rng = np.random.default_rng(22)
+    B, H, L = 2, 2, 160
+    q, _ = _up(b, rng.standard_normal((B, H, L, 64)), "f16")
+    k, _ = _up(b, rng.standard_normal((B, H, L, 64)), "f16")
+    v, _ = _up(b, rng.standard_normal((B, H, L, 64)), "f16")
+
+    def fn(q, k, v, m):
+        return b.add(b.sdpa(q, k, v, m, 0.125), b.sdpa(v, k, q, m, 0.125))
+    cf = b.compile(fn)
+    masks = []
+    for cut in (160, 90, 33, 120):
+        valid = np.ones((B, L), bool)
+        valid[1, cut:] = False
+        masks.append(b.fromHost(HostTensor("bool", (B, 1, L, L), M.attention_masks(valid, 128)[1].astype(np.uint8))))
+    for tm in masks:
+        want = to_f32(b.read(fn(q, k, v, tm)))
+        got = to_f32(b.read(cf(q, k, v, tm)))
+        assert np.array_equal(got, want)
