@@ -62,11 +62,13 @@ def attentionMasks(attention_mask: np.ndarray, B: int, L: int, window: int):
     m = np.asarray(attention_mask).reshape(B, L).astype(bool)
     half = window // 2
     full = m.astype(np.uint8).reshape(B, 1, 1, L)
-    i = np.arange(L)[:, None]
-    j = np.arange(L)[None, :]
-    near = np.abs(i - j) <= half
-    sliding = (m[:, None, :] & ((~m)[:, :, None] | near[None])).astype(np.uint8).reshape(B, 1, L, L)
-    return HostTensor("bool", (B, 1, 1, L), full), HostTensor("bool", (B, 1, L, L), sliding)
+    i = np.arange(L)
+    near = np.abs(i[:, None] - i[None, :]) <= half
+    # two in-place passes over the [B, L, L] result (no temporaries of that size)
+    sliding = np.empty((B, L, L), bool)
+    np.logical_or((~m)[:, :, None], near[None], out=sliding)
+    np.logical_and(sliding, m[:, None, :], out=sliding)
+    return HostTensor("bool", (B, 1, 1, L), full), HostTensor("bool", (B, 1, L, L), sliding.view(np.uint8).reshape(B, 1, L, L))
 
 
 def is_host_quantized(h) -> bool:
