@@ -29,74 +29,95 @@ __device__ __forceinline__ float4 ld_w4(const WT* p, int64_t i, float fill) {
 }
 
 // Vectorised fast path: dense f16/bf16/f32 rows, N % 8 == 0 (f32: % 4), N <= 256 vectors;
-// weight and bias f32 or of the rows' type (WT).
+// weight and bias f32 or of the rows' type (WT). A warp takes R rows at a time
+// (R = 2 for short rows: both rows' loads in flight together, their
+// reductions interleaved).
 template <typename T, int MAXV, typename WT = float>
 __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, const WT* __restrict__ w, const WT* __restrict__ b,
                                                        T* __restrict__ y, int64_t rows, int N, float eps) {
   pdl_trigger();
   pdl_wait();
   constexpr int VN = 16 / sizeof(T);
+  constexpr int R = MAXV <= 4 ? 2 : 1;
   int lane = threadIdx.x & 31;
   int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   int nv = N / VN;
-  for (int64_t r = warp; r < rows; r += nwarps) {
-    float v[MAXV][VN];
-    float s = 0.f;
+  for (int64_t r0 = warp * R; r0 < rows; r0 += nwarps * R) {
+    float v[R][MAXV][VN];
+    float s[R], q[R], mu[R], rs[R];
 #pragma unroll
-    for (int t = 0; t < MAXV; t++) {
-      int c = t * 32 + lane;
-      if (c < nv) {
-        uint4 raw = *(const uint4*)(x + r * N + (int64_t)c * VN);
-        const T* e = (const T*)&raw;
+    for (int k = 0; k < R; k++) {
+      s[k] = 0.f;
+      const int64_t r = r0 + k;
 #pragma unroll
-        for (int j = 0; j < VN; j++) {
-          float f;
-          if constexpr (sizeof(T) == 4) f = ((const float*)e)[j];
-          else if constexpr (std::is_same<T, __half>::value) f = __half2float(e[j]);
-          else f = __bfloat162float(e[j]);
-          v[t][j] = f;
-          s += f;
+      for (int t = 0; t < MAXV; t++) {
+        int c = t * 32 + lane;
+        if (c < nv && r < rows) {
+          uint4 raw = *(const uint4*)(x + r * N + (int64_t)c * VN);
+          const T* e = (const T*)&raw;
+#pragma unroll
+          for (int j = 0; j < VN; j++) {
+            float f;
+            if constexpr (sizeof(T) == 4) f = ((const float*)e)[j];
+            else if constexpr (std::is_same<T, __half>::value) f = __half2float(e[j]);
+            else f = __bfloat162float(e[j]);
+            v[k][t][j] = f;
+            s[k] += f;
+          }
         }
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    float mu = s / N;
-    float q = 0.f;
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-    for (int t = 0; t < MAXV; t++) {
-      if (t * 32 + lane < nv) {
+      for (int k = 0; k < R; k++) s[k] += __shfl_xor_sync(0xffffffffu, s[k], o);
 #pragma unroll
-        for (int j = 0; j < VN; j++) {
-          float d = v[t][j] - mu;
-          q += d * d;
+    for (int k = 0; k < R; k++) {
+      mu[k] = s[k] / N;
+      q[k] = 0.f;
+#pragma unroll
+      for (int t = 0; t < MAXV; t++) {
+        if (t * 32 + lane < nv) {
+#pragma unroll
+          for (int j = 0; j < VN; j++) {
+            float d = v[k][t][j] - mu[k];
+            q[k] += d * d;
+          }
         }
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-    float rs = rsqrtf(q / N + eps);
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int k = 0; k < R; k++) q[k] += __shfl_xor_sync(0xffffffffu, q[k], o);
+#pragma unroll
+    for (int k = 0; k < R; k++) rs[k] = rsqrtf(q[k] / N + eps);
 #pragma unroll
     for (int t = 0; t < MAXV; t++) {
       int c = t * 32 + lane;
       if (c < nv) {
-        uint4 raw;
-        T* e = (T*)&raw;
+        uint4 raw[R];
 #pragma unroll
         for (int j = 0; j < VN; j += 4) {  // weight and bias four at a time (fewer live registers)
           const float4 a4 = ld_w4<WT>(w, c * VN + j, 1.f);
           const float4 b4 = ld_w4<WT>(b, c * VN + j, 0.f);
           const float wv[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const float o = (v[t][j + k] - mu) * rs * wv[k] + bv[k];
-            if constexpr (sizeof(T) == 4) ((float*)e)[j + k] = o;
-            else if constexpr (std::is_same<T, __half>::value) e[j + k] = __float2half_rn(o);
-            else e[j + k] = __float2bfloat16_rn(o);
+          for (int k = 0; k < R; k++) {
+            T* e = (T*)&raw[k];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              const float o = (v[k][t][j + i] - mu[k]) * rs[k] * wv[i] + bv[i];
+              if constexpr (sizeof(T) == 4) ((float*)e)[j + i] = o;
+              else if constexpr (std::is_same<T, __half>::value) e[j + i] = __float2half_rn(o);
+              else e[j + i] = __float2bfloat16_rn(o);
+            }
           }
         }
-        *(uint4*)(y + r * N + (int64_t)c * VN) = raw;
+#pragma unroll
+        for (int k = 0; k < R; k++)
+          if (r0 + k < rows) *(uint4*)(y + (r0 + k) * N + (int64_t)c * VN) = raw[k];
       }
     }
   }
@@ -195,7 +216,7 @@ template <typename T, typename WT = float>
 void launch_layernorm_vec(const T* x, const WT* w, const WT* b, T* y, int64_t rows, int N, float eps, cudaStream_t st) {
   constexpr int VN = 16 / sizeof(T);
   int per = (N / VN + 31) / 32;
-  unsigned blocks = lc::blocks_for(rows * 32, 256);
+  unsigned blocks = lc::blocks_for((per <= 4 ? (rows + 1) / 2 : rows) * 32, 256);  // two rows per warp for short rows
   switch (per) {
     case 0: case 1: lc::launch_chain(k_layernorm_vec<T, 1, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
     case 2: lc::launch_chain(k_layernorm_vec<T, 2, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
@@ -591,12 +612,15 @@ __global__ void k_geglu_generic(const char* x, int xdt, char* y, int ydt, int64_
 // Dense f16 / bf16 / f32 x with D % (16 / sizeof(T)) == 0: block (b, 32*VEC-column
 // chunk); its 8 warps take 32-row chunks of the L positions in turn. A warp
 // reads the 32 mask entries of a chunk at once (one per lane, a ballot gives
-// the kept rows), then each lane sums VEC columns of the kept rows from
-// 16-byte loads, eight rows in flight; the warps' partial sums and counts
-// combine in shared memory.
+// the kept rows; the next chunk's entries are loaded while this one is
+// summed), then each lane sums VEC columns of the kept rows from 16-byte
+// loads, eight rows in flight; the warps' partial sums and counts combine in
+// shared memory.
 template <typename T>
 __global__ void __launch_bounds__(256) k_mean_pool_vec(const T* __restrict__ x, const char* mask, int mdt, float* __restrict__ out,
                                                        int64_t L, int64_t D) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int VEC = 16 / sizeof(T);
   constexpr int UNR = 8;
   __shared__ float part[8][32 * VEC];
@@ -609,9 +633,11 @@ __global__ void __launch_bounds__(256) k_mean_pool_vec(const T* __restrict__ x, 
 #pragma unroll
   for (int j = 0; j < VEC; j++) acc[j] = 0.f;
   float n = 0.f;
+  bool keep_next = (int64_t)warp * 32 + lane < L && ld_as<int64_t>(mask, mdt, b * L + (int64_t)warp * 32 + lane) != 0;
   for (int64_t l0 = (int64_t)warp * 32; l0 < L; l0 += 8 * 32) {
-    const int64_t lr = l0 + lane;
-    const bool keep = lr < L && ld_as<int64_t>(mask, mdt, b * L + lr) != 0;
+    const bool keep = keep_next;
+    const int64_t ln = l0 + 8 * 32 + lane;
+    if (l0 + 8 * 32 < L) keep_next = ln < L && ld_as<int64_t>(mask, mdt, b * L + ln) != 0;
     const uint32_t bits = __ballot_sync(0xffffffffu, keep);
     n += (float)__popc(bits);
     if (!on) continue;
@@ -1098,10 +1124,15 @@ int lc_mean_pool(lc_tensor* out, lc_tensor xh, lc_tensor mh) {
     const int vec = d == LC_F32 ? 4 : 8;
     if ((d == LC_F16 || d == LC_BF16 || d == LC_F32) && D % vec == 0 && B <= 65535) {
       dim3 grid((unsigned)((D + 32 * vec - 1) / (32 * vec)), (unsigned)B);
-      if (d == LC_F16) k_mean_pool_vec<__half><<<grid, 256, 0, stream()>>>((const __half*)x->data(), m->data(), m->dtype, (float*)y->data(), L, D);
+      if (d == LC_F16)
+        lc::launch_chain(k_mean_pool_vec<__half>, grid, dim3(256), 0, stream(), (const __half*)x->data(), (const char*)m->data(), (int)m->dtype,
+                         (float*)y->data(), L, D);
       else if (d == LC_BF16)
-        k_mean_pool_vec<__nv_bfloat16><<<grid, 256, 0, stream()>>>((const __nv_bfloat16*)x->data(), m->data(), m->dtype, (float*)y->data(), L, D);
-      else k_mean_pool_vec<float><<<grid, 256, 0, stream()>>>((const float*)x->data(), m->data(), m->dtype, (float*)y->data(), L, D);
+        lc::launch_chain(k_mean_pool_vec<__nv_bfloat16>, grid, dim3(256), 0, stream(), (const __nv_bfloat16*)x->data(), (const char*)m->data(),
+                         (int)m->dtype, (float*)y->data(), L, D);
+      else
+        lc::launch_chain(k_mean_pool_vec<float>, grid, dim3(256), 0, stream(), (const float*)x->data(), (const char*)m->data(), (int)m->dtype,
+                         (float*)y->data(), L, D);
     } else {
       k_mean_pool<<<blocks_for(B * D, 256), 256, 0, stream()>>>(x->data(), x->dtype, m->data(), m->dtype, (float*)y->data(), B, L, D);
     }
