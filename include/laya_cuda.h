@@ -58,7 +58,8 @@ int lc_read(lc_tensor t, void* dst, size_t nbytes);
 int lc_tensor_free(lc_tensor t);
 /* Shape and dtype of a handle (Tensor.shape / Tensor.dtype, index.ts:75-78). */
 int lc_tensor_info(lc_tensor t, int* dtype, int* ndim, int64_t* shape /* [8] */);
-/* Device pointer of a dense tensor (0 when it is a strided view). */
+/* Device pointer of a dense tensor (0 when it is a strided view). Read-only:
+   the library treats tensors as immutable (only lc_copy_into writes one). */
 int lc_tensor_data(lc_tensor t, uint64_t* dptr);
 /* index.ts:163-164 flush: waits for queued work. */
 int lc_flush(void);
