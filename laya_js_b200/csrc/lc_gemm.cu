@@ -165,6 +165,31 @@ __device__ __forceinline__ float2 stats_unit(float* a, float* b) {
   return make_float2(mu, (q[0] + q[1]) + (q[2] + q[3]));
 }
 
+// stats_unit on packed pairs (a[j] = columns col+2j, col+2j+1; b the same
+// 32 columns on): the chains and their order are stats_unit's, so are the
+// bits; half the instructions.
+template <typename T>
+__device__ __forceinline__ float2 stats_unit2(float2* a, float2* b) {
+  float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    a[j] = round_pair<T>(a[j].x, a[j].y);
+    b[j] = round_pair<T>(b[j].x, b[j].y);
+    sa = add2(sa, a[j]);
+    sb = add2(sb, b[j]);
+  }
+  const float mu = ((sa.x + sa.y) + (sb.x + sb.y)) * (1.f / 64.f);
+  const float2 nmu = make_float2(-mu, -mu);
+  float2 qa = make_float2(0.f, 0.f), qb = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    const float2 da = add2(a[j], nmu), db = add2(b[j], nmu);
+    qa = fma2(da, da, qa);
+    qb = fma2(db, db, qb);
+  }
+  return make_float2(mu, (qa.x + qa.y) + (qb.x + qb.y));
+}
+
 // store 32 consecutive values v[0..31] at columns [col, col+32) of row `row`, valid columns < ncols
 template <typename T>
 __device__ __forceinline__ void store32(T* rowp, int col, int ncols, const float* v, bool vec) {
@@ -591,7 +616,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
 #pragma unroll
             for (int j = 0; j < 4; j++) dst[j] = add2(dst[j], unpack_pair<T>(hw[j]));
           }
-          if (ep.stats_out && live) ep.stats_out[(int64_t)row * nparts + col / 64] = stats_unit<T>((float*)a, (float*)b);
+          if (ep.stats_out && live) ep.stats_out[(int64_t)row * nparts + col / 64] = stats_unit2<T>(a, b);
         }
       }
       if (first && !resid) {  // the store that last used this buffer has read it
