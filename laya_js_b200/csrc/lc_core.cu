@@ -9,10 +9,13 @@
 #include "lc_gemm.h"
 
 #include <algorithm>
+#include <cstring>
 #include <memory>
 #include <mutex>
 #include <unordered_map>
 #include <unordered_set>
+#include <thread>
+#include <vector>
 
 static const uint64_t kMagic = 0x4c41594143554441ull;  // "LAYACUDA"
 
@@ -392,6 +395,8 @@ int lc_init(int device) {
   LC_API_END
 }
 
+static void destroy_upload_stage();  // the pinned staging of large uploads (lc_from_host)
+
 int lc_destroy(void) {
   LC_API_BEGIN
   State& s = S();
@@ -399,6 +404,7 @@ int lc_destroy(void) {
   std::vector<LcTensor*> all(s.live.begin(), s.live.end());
   for (auto* t : all) release(t);
   lc_internal_destroy_caches();
+  destroy_upload_stage();
   CUDA_OK(cudaStreamSynchronize(s.cur));
   LC_API_END
 }
@@ -429,6 +435,68 @@ int lc_stats(int64_t* live_tensors, int64_t* live_bytes, int64_t* launches) {
   return 0;
 }
 
+namespace {
+// Large uploads go through two pinned staging buffers: the host copies chunk
+// i + 1 into one while the DMA engine moves chunk i out of the other (a
+// pageable cudaMemcpyAsync runs at a few GB/s; the pinned DMA at tens). Each
+// chunk's host copy is split over a few threads. The caller's memory is
+// fully read when lc_from_host returns, as fromHost requires; the staging
+// buffers are reused only after their DMA has completed (an event per buffer).
+constexpr size_t kStageChunk = (size_t)8 << 20;
+constexpr size_t kStageMin = (size_t)4 << 20;  // smaller uploads: one pageable copy
+struct UploadStage {
+  void* buf[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+};
+UploadStage& upload_stage() {
+  static UploadStage u;
+  return u;
+}
+void host_copy_parallel(void* dst, const void* src, size_t n) {
+  const size_t kPart = (size_t)1 << 20;
+  const int parts = (int)std::min<size_t>(4, (n + kPart - 1) / kPart);
+  if (parts <= 1) {
+    std::memcpy(dst, src, n);
+    return;
+  }
+  const size_t per = (n + parts - 1) / parts;
+  std::vector<std::thread> ts;
+  for (int i = 1; i < parts; i++) {
+    const size_t o = per * i, len = std::min(per, n - o);
+    ts.emplace_back([=] { std::memcpy((char*)dst + o, (const char*)src + o, len); });
+  }
+  std::memcpy(dst, src, std::min(per, n));
+  for (auto& t : ts) t.join();
+}
+void upload_staged(void* dev, const void* host, size_t nbytes, cudaStream_t st) {
+  UploadStage& u = upload_stage();
+  for (int i = 0; i < 2; i++)
+    if (!u.buf[i]) {
+      CUDA_OK(cudaHostAlloc(&u.buf[i], kStageChunk, cudaHostAllocDefault));
+      CUDA_OK(cudaEventCreateWithFlags(&u.done[i], cudaEventDisableTiming));
+      CUDA_OK(cudaEventRecord(u.done[i], st));
+    }
+  int k = 0;
+  for (size_t o = 0; o < nbytes; o += kStageChunk, k ^= 1) {
+    const size_t len = std::min(kStageChunk, nbytes - o);
+    CUDA_OK(cudaEventSynchronize(u.done[k]));  // the previous DMA out of this buffer has finished
+    host_copy_parallel(u.buf[k], (const char*)host + o, len);
+    CUDA_OK(cudaMemcpyAsync((char*)dev + o, u.buf[k], len, cudaMemcpyHostToDevice, st));
+    CUDA_OK(cudaEventRecord(u.done[k], st));
+  }
+}
+}  // namespace
+
+static void destroy_upload_stage() {
+  UploadStage& u = upload_stage();
+  for (int i = 0; i < 2; i++) {
+    if (u.done[i]) cudaEventSynchronize(u.done[i]), cudaEventDestroy(u.done[i]);
+    if (u.buf[i]) cudaFreeHost(u.buf[i]);
+    u.buf[i] = nullptr;
+    u.done[i] = nullptr;
+  }
+}
+
 int lc_from_host(lc_tensor* out, int dtype, const int64_t* shape, int ndim, const void* data, size_t nbytes) {
   LC_API_BEGIN
   LC_CHECK(dtype >= 0 && dtype < LC_NUM_DTYPES, "fromHost: unknown dtype");
@@ -441,8 +509,10 @@ int lc_from_host(lc_tensor* out, int dtype, const int64_t* shape, int ndim, cons
   LcTensor* t = alloc(dtype, sh);
   if (nbytes) {
     // pageable source: the copy is complete (staged) when cudaMemcpyAsync returns,
-    // so the caller may reuse `data` at once (index.ts:146-154).
-    CUDA_OK(cudaMemcpyAsync(t->data(), data, nbytes, cudaMemcpyHostToDevice, stream()));
+    // so the caller may reuse `data` at once (index.ts:146-154). While a graph is
+    // captured the copy is the capture's (no host-side staging).
+    if (nbytes >= kStageMin && !S().capturing) upload_staged(t->data(), data, nbytes, stream());
+    else CUDA_OK(cudaMemcpyAsync(t->data(), data, nbytes, cudaMemcpyHostToDevice, stream()));
   }
   t->st->upload_mark = S().launches;
   *out = handle(t);

@@ -123,3 +123,26 @@ def test_sort_long_rows_and_nan_last():
     assert np.array_equal(np.isnan(got), np.isnan(np.sort(x, -1)))
     ok = ~np.isnan(got)
     assert np.array_equal(got[ok], np.sort(x, -1)[ok])
+
+
+def test_large_uploads_through_the_staging_buffers():
+    """fromHost copies before it returns (index.ts:146-154) also for uploads
+    that go through the pinned double buffer: ragged chunk counts, the caller
+    overwriting its array right after the call, back-to-back uploads."""
+    b = backend()
+    rng = np.random.default_rng(5)
+    for n in ((8 << 20) * 2 + 12345, (4 << 20), (8 << 20) * 5 - 7):
+        a = rng.integers(0, 256, size=n, dtype=np.uint8)
+        want = a.copy()
+        t1 = b.fromHost(HostTensor("u8", (n,), a))
+        a[:] = 0  # the caller reuses its buffer at once
+        c = rng.integers(0, 256, size=n, dtype=np.uint8)
+        t2 = b.fromHost(HostTensor("u8", (n,), c))
+        assert np.array_equal(b.read(t1).data, want)
+        assert np.array_equal(b.read(t2).data, c)
+        b.dispose(t1)
+        b.dispose(t2)
+    x = rng.standard_normal((4096, 2048)).astype(np.float16)
+    t = b.fromHost(HostTensor("f16", x.shape, x))
+    assert np.array_equal(b.read(t).data, x)
+    b.dispose(t)
