@@ -546,8 +546,18 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
     ep.ln_cols = H;
     ep.ln_eps = (float)c.norm_eps;
   };
+  // Few rows: each GEMM brings the next projection's weight into L2 (the
+  // chain is latency-bound there and the weights of all layers exceed L2).
+  const bool l2_chain = T <= 4096;
+  auto next_weight = [&](GemmEpilogue& ep, const Mat* m) {
+    if (!l2_chain || !m) return;
+    const LcTensor* t = m->dense ? m->dense : m->q;
+    ep.l2_next = t->data();
+    ep.l2_next_bytes = (size_t)t->numel() * dtype_size(t->dtype);
+  };
   for (size_t li = 0; li < e->layers.size(); li++) {
     const Layer& L = e->layers[li];
+    const Layer* Ln = li + 1 < e->layers.size() ? &e->layers[li + 1] : nullptr;
     const void* hin = x;
     GemmEpilogue eq;
     eq.kind = EPI_ROPE_QKV;
@@ -562,6 +572,7 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
       layernorm_raw(x, (const float*)L.attn_norm->data(), h, T, H, (float)c.norm_eps, c.dtype, st);
       hin = h;
     }
+    next_weight(eq, &L.Wo);
     run_gemm(e, L.Wqkv, hin, T, qkv, 3 * H, eq, 3 * H, 0);
     // attention -> h (h is free again once the Wqkv GEMM has read it)
     {
@@ -573,11 +584,15 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
     er.resid = x;
     er.ldr = H;
     er.stats_out = stats;
-    run_gemm(e, L.Wo, h, T, x, H, er, H, 4);
+    GemmEpilogue ero = er;
+    next_weight(ero, &L.Wi);
+    run_gemm(e, L.Wo, h, T, x, H, ero, H, 4);
     GemmEpilogue eg;
     eg.kind = EPI_GEGLU;
     folded(eg, L.Wi);
+    next_weight(eg, &L.WoMlp);
     run_gemm(e, L.Wi, x, T, qkv, I, eg, I, 5);
+    next_weight(er, Ln ? &Ln->Wqkv : nullptr);
     run_gemm(e, L.WoMlp, qkv, T, x, H, er, H, 6);
   }
   void* fin = hidden_out ? hidden_out : h;

@@ -773,6 +773,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       }
     }
   }
+  if (warp == 0 && lane == 0 && args.ep.l2_next) {  // this CTA's slice of the next projection's weight
+    const size_t total = args.ep.l2_next_bytes & ~(size_t)15;
+    const size_t per = ((total + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+    const size_t lo = per * blockIdx.x, hi = lo + per < total ? lo + per : total;
+    for (size_t o = lo; o < hi; o += 65536) bulk_prefetch_l2((const char*)args.ep.l2_next + o, (uint32_t)(hi - o < 65536 ? hi - o : 65536));
+  }
   if (!QB) pdl_wait();  // the kernel that wrote the activations has completed
 
   if (warp == 0) {

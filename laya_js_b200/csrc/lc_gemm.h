@@ -34,6 +34,11 @@ struct GemmEpilogue {
   // resident dense weight, not a dequantisation scratch): the kernel may
   // request it before waiting for its predecessor.
   bool w_static = false;
+  // The weight of the next projection of the chain (or null): the CTAs bring
+  // it into L2 while this one runs, so the next GEMM's weight blocks come from
+  // L2 rather than HBM (few rows: the chain is latency-bound). 16-byte aligned.
+  const void* l2_next = nullptr;
+  size_t l2_next_bytes = 0;
 };
 
 // A weight in the native packed 4/8-bit layout (packages/tensor-backend/src/index.ts:98-108)

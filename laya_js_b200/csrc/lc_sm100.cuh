@@ -75,6 +75,10 @@ static __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap*
       : "memory");
 }
 // Pull a tile of a tensor map into L2 (no shared-memory destination).
+// Brings [p, p + bytes) into L2 (p and bytes multiples of 16).
+static __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)p), "r"(bytes) : "memory");
+}
 static __device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, int y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"((uint64_t)map), "r"(x), "r"(y) : "memory");
 }
