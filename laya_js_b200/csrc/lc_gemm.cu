@@ -657,6 +657,197 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
   __syncwarp();
 }
 
+// Split K (KS with args.ksplit = S > 1; one tile per cluster). The partial
+// tiles meet in the owners' shared memory as in epilogue_tma — the warp
+// holding a lane quarter's rows sends them with one bulk copy to the CTA that
+// reduces that quarter — but the owner's rows (128/S of them) are then
+// finished by all EW epilogue warps together instead of one warp per lane
+// quarter: a warp takes R rows at a time (R = 4 for 64-column tiles, 2 for
+// GeGLU's 128), lane = (row, 8-column chunk), sums the S slots of its chunk
+// in the order 0..S-1, applies the epilogue to its 8 values (the RoPE / GeGLU
+// partner half of the 64-column unit is four lanes away), stages the R rows
+// and stores them with one TMA store (the y map's box is 64 columns x R rows).
+// The row statistics of a residual epilogue reduce over the unit's 8 lanes.
+template <typename T, int BN, int EW>
+__device__ __forceinline__ void epilogue_split(const GemmArgs& args, const CUtensorMap* tmYp, uint8_t* sE, uint64_t* tfull,
+                                               uint64_t* tempty, volatile int* abort, uint32_t tmem, int warp, int lane, float* sP,
+                                               float* sSend, uint64_t* pbar) {
+  const GemmEpilogue& ep = args.ep;
+  const int S = args.ksplit, rank = (int)cluster_rank(), orows = BM / S;
+  const int quarter = warp & 3, sub = (warp - 2) >> 2;
+  constexpr int U = BN / 64;
+  const bool geglu = ep.kind == EPI_GEGLU, resid = ep.kind == EPI_RESIDUAL;
+  const int t = blockIdx.x / S;  // the cluster's tile
+  const int m0 = (t / args.ntile_n) * BM, n0 = (t % args.ntile_n) * BN;
+  bool ok = mbar_wait(&tfull[0], 0, abort, &g_gemm_err);
+  if (ok) {
+    tc_fence_after();
+    if (sub == 0) {  // this quarter's 32 rows of the partial tile -> the owner's slot for this CTA
+      const int owner = (quarter * S) / 4, lrow0 = (quarter - owner * (4 / S)) * 32;
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16);
+      float* srow = sSend + (quarter * 32 + lane) * (BN + 4);
+#pragma unroll 1
+      for (int u = 0; u < U; u++) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tbase + u * 64, ra);
+        tmem_ld32(tbase + u * 64 + 32, rb);
+        tmem_wait_ld();
+        float4* p4 = (float4*)(srow + u * 64);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          p4[j] = make_float4(__uint_as_float(ra[4 * j]), __uint_as_float(ra[4 * j + 1]), __uint_as_float(ra[4 * j + 2]),
+                              __uint_as_float(ra[4 * j + 3]));
+          p4[8 + j] = make_float4(__uint_as_float(rb[4 * j]), __uint_as_float(rb[4 * j + 1]), __uint_as_float(rb[4 * j + 2]),
+                                  __uint_as_float(rb[4 * j + 3]));
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0)
+        bulk_copy_to_cluster(mapa_rank(smem_u32(sP + (rank * orows + lrow0) * (BN + 4)), (uint32_t)owner),
+                             smem_u32(sSend + quarter * 32 * (BN + 4)), 32u * (BN + 4) * 4u, mapa_rank(smem_u32(&pbar[0]), (uint32_t)owner));
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&tempty[0]);  // the accumulator has been read (one tile per CTA)
+  constexpr int CPR = BN / 8;    // 8-column chunks per row of the tile
+  constexpr int R = 32 / CPR;    // rows per warp pass
+  const int k = lane % CPR, rl = lane / CPR;
+  const int col = k * 8, unit = col / 64, uc = col % 64;  // tile column, its 64-column unit and place in it
+  const int gc = n0 + col;                                // accumulator column
+  const bool rope = ep.kind == EPI_ROPE_QKV && n0 + unit * 64 < ep.rope_cols;
+  const int nparts = args.N / 64;
+  float wsum[8];
+  if (ep.ln_stats) {
+    const float4 w0 = __ldg((const float4*)(ep.ln_wsum + gc)), w1 = __ldg((const float4*)(ep.ln_wsum + gc) + 1);
+    wsum[0] = w0.x, wsum[1] = w0.y, wsum[2] = w0.z, wsum[3] = w0.w, wsum[4] = w1.x, wsum[5] = w1.y, wsum[6] = w1.z, wsum[7] = w1.w;
+  }
+  float bias[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+    bias[i] = (args.bias && !geglu && gc + i < args.N) ? ld_as<float>((const char*)args.bias, args.bias_dtype, gc + i) : 0.f;
+  uint8_t* stg0 = sE + (warp - 2) * 4096;  // this warp's 4 KB of staging: two 1024-aligned buffers of R rows
+  int npass = 0;
+  bool waited = false;
+#pragma unroll 1
+  for (int r0 = (warp - 2) * R; r0 < orows; r0 += EW * R, npass++) {
+    const int lr = r0 + rl, row = m0 + rank * orows + lr;
+    const bool live = row < args.M;
+    float mu = 0.f, rr = 1.f;
+    if (ep.ln_stats) ln_row(ep, row, args.M, mu, rr);
+    float res[8];
+    if (resid) {
+      uint4 rv = make_uint4(0u, 0u, 0u, 0u);
+      if (live && gc < args.N) rv = __ldg((const uint4*)((const T*)ep.resid + (int64_t)row * ep.ldr + gc));
+      const uint32_t* hw = (const uint32_t*)&rv;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float2 f = unpack_pair<T>(hw[j]);
+        res[2 * j] = f.x;
+        res[2 * j + 1] = f.y;
+      }
+    }
+    float4 cs[4];
+    if (rope) {
+      const float4* rq = (const float4*)ep.rope_cs + (live ? ep.pos[row] : 0);
+#pragma unroll
+      for (int j = 0; j < 4; j++) cs[j] = __ldg(rq + (int64_t)(((uc % 32) >> 1) + j) * ep.rope_cap);
+    }
+    if (!waited) {
+      ok = ok && mbar_wait(&pbar[0], 0, abort, &g_gemm_err);
+      waited = true;
+    }
+    // the S slots of this chunk, added in the order 0..S-1
+    float v[8];
+    {
+      const float4* src = (const float4*)(sP + lr * (BN + 4) + col);
+      float4 x0 = src[0], x1 = src[1];
+      for (int c = 1; c < S; c++) {
+        const float4* sc = src + c * orows * (BN + 4) / 4;
+        const float4 y0 = sc[0], y1 = sc[1];
+        x0.x += y0.x, x0.y += y0.y, x0.z += y0.z, x0.w += y0.w;
+        x1.x += y1.x, x1.y += y1.y, x1.z += y1.z, x1.w += y1.w;
+      }
+      v[0] = x0.x, v[1] = x0.y, v[2] = x0.z, v[3] = x0.w, v[4] = x1.x, v[5] = x1.y, v[6] = x1.z, v[7] = x1.w;
+    }
+    if (ep.ln_stats)
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = rr * fmaf(-mu, wsum[i], v[i]);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) o[i] = __shfl_xor_sync(0xffffffffu, v[i], 4);  // the other half of the unit
+    const bool lo_half = uc < 32;
+    uint4 packed;
+    uint32_t* pk = (uint32_t*)&packed;
+    if (geglu) {  // lanes of the gate half: gelu(gate) * up
+#pragma unroll
+      for (int j = 0; j < 4; j++) pk[j] = pack_pair<T>(mul2(gelu_as2(make_float2(v[2 * j], v[2 * j + 1])), make_float2(o[2 * j], o[2 * j + 1])));
+    } else {
+      if (rope) {  // (x1, x2) -> (x1 cos - x2 sin, x2 cos + x1 sin)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float4 q = cs[j];
+          if (lo_half) {
+            v[2 * j] = fmaf(o[2 * j], -q.z, v[2 * j] * q.x);
+            v[2 * j + 1] = fmaf(o[2 * j + 1], -q.w, v[2 * j + 1] * q.y);
+          } else {
+            v[2 * j] = fmaf(o[2 * j], q.z, v[2 * j] * q.x);
+            v[2 * j + 1] = fmaf(o[2 * j + 1], q.w, v[2 * j + 1] * q.y);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] += bias[i];
+      if (resid)
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] += res[i];
+#pragma unroll
+      for (int j = 0; j < 4; j++) pk[j] = pack_pair<T>(make_float2(v[2 * j], v[2 * j + 1]));
+      if (resid && ep.stats_out) {  // (mean, M2) of the stored unit: this lane's 8 values, then the unit's 8 lanes
+        float f[8], sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float2 g = unpack_pair<T>(pk[j]);
+          f[2 * j] = g.x;
+          f[2 * j + 1] = g.y;
+          sum += g.x + g.y;
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        const float m = sum * (1.f / 64.f);
+        float q2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) q2 = fmaf(f[i] - m, f[i] - m, q2);
+        q2 += __shfl_xor_sync(0xffffffffu, q2, 1);
+        q2 += __shfl_xor_sync(0xffffffffu, q2, 2);
+        q2 += __shfl_xor_sync(0xffffffffu, q2, 4);
+        if (uc == 0 && live) ep.stats_out[(int64_t)row * nparts + gc / 64] = make_float2(m, q2);
+      }
+    }
+    // stage the R rows (128-byte swizzle) and store them
+    uint8_t* stg = stg0 + (npass & 1) * 2048;
+    if (lane == 0) bulk_wait_read1();  // the store that last read this buffer is done with it
+    __syncwarp();
+    if (!geglu) *(uint4*)(stg + rl * 128 + ((k ^ (rl & 7)) << 4)) = packed;
+    else if (lo_half) {
+      const int oc = unit * 4 + uc / 8;  // output chunk: units 0 / 1 fill columns [0, 32) / [32, 64)
+      *(uint4*)(stg + rl * 128 + ((oc ^ (rl & 7)) << 4)) = packed;
+    }
+    fence_async_smem();
+    __syncwarp();
+    const int srow = m0 + rank * orows + r0;
+    if (lane == 0 && ok && srow < args.M) {
+      tma_store_2d(tmYp, stg, geglu ? n0 / 2 : n0, srow);
+      bulk_commit();
+    }
+  }
+  if (!waited) mbar_wait(&pbar[0], 0, abort, &g_gemm_err);  // every partial sent here has landed before the CTA exits
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
 // KS: split K over the CTAs of a cluster of args.ksplit (launched with that
 // cluster size, one K slice per CTA rank): the unit of work is (tile, slice),
 // CTA rank r takes K blocks [r·KB/S, (r+1)·KB/S) of its cluster's tiles and
@@ -890,8 +1081,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(const __grid_consta
       }
       pdl_wait();  // the kernel that wrote the activations and the residual has completed
     }
-    epilogue_tma<T, BN, false, EPI_WARPS, 1, KS>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x / S,
-                                                 gridDim.x / S, BM, 0, sP, (float*)sA, pbar);
+    if (KS && S > 1)
+      epilogue_split<T, BN, EPI_WARPS>(args, &tmY, sE, tfull, tempty, abort, tmem, warp, lane, sP, (float*)sA, pbar);
+    else
+      epilogue_tma<T, BN, false, EPI_WARPS, 1, KS>(args, &tmY, &tmR, sE, rbar, tfull, tempty, abort, tmem, warp, lane, blockIdx.x / S,
+                                                   gridDim.x / S, BM, 0, sP, (float*)sA, pbar);
   } else {
     // ---------------- epilogue (warps 2..9 -> TMEM lane quarter warp % 4, half of the units each)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
@@ -1158,7 +1352,8 @@ std::map<MapKey, CUtensorMap>& map_cache() {
 // Row-major [rows, K] matrix, boxes of box_rows x 64, 128-byte swizzle.
 // Row-major [rows, cols] matrix with row stride ld (elements), boxes of
 // box_rows x box_cols (box_cols * 2 bytes = 128: one swizzle row).
-const CUtensorMap& tensor_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype) {
+// Returned by value: a later call may clear the cache.
+CUtensorMap tensor_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype) {
   MapKey key{(uintptr_t)ptr, rows, cols, ld, box_cols * 1024 + box_rows, dtype};
   auto& c = map_cache();
   auto it = c.find(key);
@@ -1177,7 +1372,7 @@ const CUtensorMap& tensor_map(const void* ptr, int64_t rows, int64_t cols, int64
 }
 // Bytes of a row-major [rows, cols] byte matrix (the packed weights), boxes of
 // box_rows x box_cols bytes, no swizzle.
-const CUtensorMap& tensor_map_u8(const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+CUtensorMap tensor_map_u8(const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows) {
   MapKey key{(uintptr_t)ptr, rows, cols, cols, box_cols * 1024 + box_rows, -1};
   auto& c = map_cache();
   auto it = c.find(key);
@@ -1376,7 +1571,8 @@ bool gemm_raw(const void* x, int64_t M, int64_t K, const void* w, int64_t N, con
     as.ntiles = (int)(mt * nt);
     as.ksplit = S;
     const CUtensorMap& mbs = tensor_map(w, Nacc, K, K, BK, BNs, dtype);
-    const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
+    // split: the owner's warps store R rows at a time (epilogue_split)
+    const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, S > 1 ? (BNs == 128 ? 2 : 4) : 32, dtype);
     const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
     if (dtype == LC_F16) {
       if (BNs == 64) launch_gemm_split<__half, 64, 4>(ma, mbs, my, mr, as, st);
@@ -1478,7 +1674,7 @@ bool gemm_raw_q(const void* x, int64_t M, int64_t K, const GemmQuantB& q, int64_
   a.q = q;
   const CUtensorMap& ma = tensor_map(x, M, K, K, BK, BM, dtype);
   const CUtensorMap& mb = tensor_map_u8(q.w, Nacc, rowb, BK * q.bits / 8, BNs);
-  const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, 32, dtype);
+  const CUtensorMap& my = tensor_map(y, M, N, ldy, 64, S > 1 ? (BNs == 128 ? 2 : 4) : 32, dtype);
   const CUtensorMap& mr = ep.kind == EPI_RESIDUAL ? tensor_map(ep.resid, M, N, ep.ldr, 64, 32, dtype) : my;
   if (dtype == LC_F16) {
     if (BNs == 64) launch_gemm_split<__half, 64, 4, true>(ma, mb, my, mr, a, st);
@@ -1521,7 +1717,7 @@ std::string take_device_errors() {
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
 
-const CUtensorMap& tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype) {
+CUtensorMap tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype) {
   return tensor_map(ptr, rows, cols, ld, box_cols, box_rows, dtype);
 }
 

@@ -79,7 +79,7 @@ bool sdpa_flash(const LcTensor* q, const LcTensor* k, const LcTensor* v, const L
 std::string take_device_errors();
 std::string take_attention_errors();
 // Cached 2-D tiled tensor map (128-byte swizzle) over a row-major [rows, cols] matrix with row stride ld.
-const CUtensorMap& tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype);
+CUtensorMap tensor_map_2d(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, int dtype);
 // The driver's cuTensorMapEncodeTiled (for maps of other ranks than tensor_map_2d's).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 // The contract's sdpa on the tcgen05 attention kernel (lc_attention_tc.cu) for
