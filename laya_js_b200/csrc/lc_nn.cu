@@ -787,28 +787,30 @@ __global__ void __launch_bounds__(256) k_linear_rows(const char* x, int xdt, con
   }
 }
 
-// The same for dense 16-bit x and w rows with K % 8 == 0 and 16-byte aligned
-// rows: 16-byte loads, the whole K range of a lane in flight at once.
-template <typename T>
+// The same for dense 16-bit x and w rows with K % VW == 0 and rows aligned to
+// VW elements (VW = 8: 16-byte loads; 4: 8-byte loads, e.g. K = 772), the
+// whole K range of a lane in flight at once.
+template <typename T, int VW>
 __global__ void __launch_bounds__(256) k_linear_rows16(const T* __restrict__ x, const T* __restrict__ w, const char* bias, int bdt, char* y,
                                                        int ydt, int M, int N, int K) {
   pdl_trigger();
   pdl_wait();
+  using V = typename std::conditional<VW == 8, uint4, uint2>::type;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= (int64_t)M * N) return;
   const int m = (int)(warp / N), n = (int)(warp % N);
-  const uint4* xr = (const uint4*)(x + (int64_t)m * K);
-  const uint4* wr = (const uint4*)(w + (int64_t)n * K);
-  const int nv = K / 8;
+  const V* xr = (const V*)(x + (int64_t)m * K);
+  const V* wr = (const V*)(w + (int64_t)n * K);
+  const int nv = K / VW;
   float acc = 0.f;
 #pragma unroll 4
   for (int v = lane; v < nv; v += 32) {
-    const uint4 a = __ldg(xr + v), b = __ldg(wr + v);
+    const V a = __ldg(xr + v), b = __ldg(wr + v);
     const T* ae = (const T*)&a;
     const T* be = (const T*)&b;
 #pragma unroll
-    for (int j = 0; j < 8; j++) acc = fmaf(to_f<T>(ae[j]), to_f<T>(be[j]), acc);
+    for (int j = 0; j < VW; j++) acc = fmaf(to_f<T>(ae[j]), to_f<T>(be[j]), acc);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -850,14 +852,17 @@ void linear_simt(const LcTensor* x2, const LcTensor* w, const LcTensor* bias, Lc
   const bool dbl = y->dtype == LC_F64 || x2->dtype == LC_F64 || w->dtype == LC_F64;
   if (p.m && p.n && p.m <= 16 && !dbl && p.m * p.n < ((int64_t)1 << 26)) {
     const unsigned blocks = (unsigned)((p.m * p.n * 32 + 255) / 256);
-    const bool v16 = is_half(x2->dtype) && w->dtype == x2->dtype && p.k % 8 == 0 && p.k < INT32_MAX &&
-                     (((uintptr_t)p.a | (uintptr_t)p.b) & 15) == 0;
-    if (v16 && x2->dtype == LC_F16)
-      lc::launch_chain(k_linear_rows16<__half>, dim3(blocks), dim3(256), 0, stream(), (const __half*)p.a, (const __half*)p.b, p.bias,
-                       p.biasdt, p.c, p.cdt, (int)p.m, (int)p.n, (int)p.k);
-    else if (v16)
-      lc::launch_chain(k_linear_rows16<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream(), (const __nv_bfloat16*)p.a,
-                       (const __nv_bfloat16*)p.b, p.bias, p.biasdt, p.c, p.cdt, (int)p.m, (int)p.n, (int)p.k);
+    const bool h16 = is_half(x2->dtype) && w->dtype == x2->dtype && p.k < INT32_MAX;
+    const int vw = !h16 ? 0 : (p.k % 8 == 0 && (((uintptr_t)p.a | (uintptr_t)p.b) & 15) == 0) ? 8
+                            : (p.k % 4 == 0 && (((uintptr_t)p.a | (uintptr_t)p.b) & 7) == 0) ? 4 : 0;
+#define LC_ROWS16(T, VW)                                                                                                               \
+  lc::launch_chain(k_linear_rows16<T, VW>, dim3(blocks), dim3(256), 0, stream(), (const T*)p.a, (const T*)p.b, p.bias, p.biasdt, p.c, \
+                   p.cdt, (int)p.m, (int)p.n, (int)p.k)
+    if (vw == 8 && x2->dtype == LC_F16) LC_ROWS16(__half, 8);
+    else if (vw == 8) LC_ROWS16(__nv_bfloat16, 8);
+    else if (vw == 4 && x2->dtype == LC_F16) LC_ROWS16(__half, 4);
+    else if (vw == 4) LC_ROWS16(__nv_bfloat16, 4);
+#undef LC_ROWS16
     else
       lc::launch_chain(k_linear_rows, dim3(blocks), dim3(256), 0, stream(), p.a, p.adt, p.b, p.bdt, p.bias, p.biasdt, p.c, p.cdt, p.m,
                        p.n, p.k);

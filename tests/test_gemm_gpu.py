@@ -2,7 +2,8 @@
 every tile path (BN 128 / 256, the split-K clusters for few rows), M and N
 tails, K not a multiple of 64; and the warp-per-output kernel that takes few
 rows of a small product (M <= 16, M*N*K <= 2^23: the (1, 2304, 768),
-(4, 768, 768) and (3, 2, 256) cases)."""
+(4, 768, 768) and (3, 2, 256) cases with 16-byte loads, (1, 256, 772) and
+(2, 40, 68) with 8-byte loads)."""
 from __future__ import annotations
 
 import numpy as np
@@ -16,7 +17,7 @@ pytestmark = pytest.mark.gpu
 SHAPES = [(1, 40, 64), (127, 128, 64), (128, 256, 768), (300, 768, 768), (1000, 2304, 768), (4096, 768, 1152),
           (513, 5248, 1024), (77, 1024, 2624), (2048, 3072, 1024), (130, 24, 128), (64, 200, 200),
           (5, 44, 64), (300, 129, 128), (1, 2304, 768), (4, 768, 768), (3, 2, 256),
-          (16, 2304, 768), (12, 768, 1152)]
+          (16, 2304, 768), (12, 768, 1152), (1, 256, 772), (2, 40, 68)]
 
 
 def _mk(dtype, a):
