@@ -35,7 +35,9 @@ Keys beyond the driver's contract (extras run on rank 0 of a 1-GPU run):
   p50_latency_ms / p50_latency_graph_ms  configs[0] (batch 1, seq 128,
              3-way head) end to end, eager and as a captured CUDA graph;
   predict    the DecisionModel forward (predict()'s model call) on one
-             128-token prompt: p50 eager and through Backend.compile.
+             128-token prompt: p50 eager and through Backend.compile;
+  microbench configs[1]: the row and elementwise contract ops over [M, N]
+             (f16 / f32), GB/s against the measured copy bandwidth.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -407,6 +409,55 @@ def contract_leg(b, ev, enc, thw3, thb3, thw8, thb8) -> dict:
                     "row kernels) + CLS head, host buffers in and out, CUDA events on the library stream"}
 
 
+def microbench_leg(b, ev, hbm_peak: float) -> dict:
+    """the tensor-backend op microbench — add, mul, GELU, row
+    broadcast add, row sum / max, softmax and LayerNorm over [M, N] in f16 and
+    f32, M in {1024, 16384, 262144}, N in {768, 1152, 2304}, values N(0, 1)
+    from one seeded buffer (the second operand of add / mul is its negation,
+    in its own memory). GB/s = algorithmic bytes (inputs read once, output
+    written once) / CUDA-event time per launch; only M = 262144 exceeds L2 at
+    every N."""
+    from laya_js_b200.host import HostTensor
+    Ms, Ns = (1024, 16384, 262144), (768, 1152, 2304)
+    rng = np.random.default_rng(20261201 + 30)
+    nmax = Ms[-1] * Ns[-1]
+    flat32 = b.fromHost(HostTensor("f32", (nmax,), rng.standard_normal(nmax, dtype=np.float32)))
+    flat16 = b.cast(flat32, "f16")
+    out: dict = {}
+    fracs = []
+    for dt, flat, e in (("f16", flat16, 2), ("f32", flat32, 4)):
+        for N in Ns:
+            g = b.fromHost(HostTensor(dt, (N,), np.ones(N, np.float16 if dt == "f16" else np.float32)))
+            for M in Ms:
+                x = b.reshape(b.slice(flat, [0], [M * N]), [M, N])
+                y = b.neg(x)  # a second operand in its own memory (N(0, 1) as well)
+                cases = (("add", lambda: b.add(x, y), 3 * M * N * e), ("mul", lambda: b.mul(x, y), 3 * M * N * e),
+                         ("gelu", lambda: b.gelu(x), 2 * M * N * e), ("add_row", lambda: b.add(x, g), 2 * M * N * e + N * e),
+                         ("sum", lambda: b.sum(x, -1), M * N * e + M * e), ("max", lambda: b.max(x, -1), M * N * e + M * e),
+                         ("softmax", lambda: b.softmax(x, -1), 2 * M * N * e),
+                         ("layerNorm", lambda: b.layerNorm(x, g, None, 1e-5), 2 * M * N * e + N * e))
+                for name, fn, nbytes in cases:
+                    run = lambda: b.dispose(fn())
+                    run()
+                    reps = 5
+                    gbs = nbytes / (ev.time(run, reps) / reps * 1e-3) / 1e9
+                    out.setdefault(f"{name}/{dt}", {}).setdefault(str(N), []).append(round(gbs, 1))
+                    if M == Ms[-1]:
+                        fracs.append(gbs / hbm_peak)
+                b.dispose(x)
+                b.dispose(y)
+            b.dispose(g)
+    b.dispose(flat16)
+    b.dispose(flat32)
+    return {"config": "configs[1]: add/mul/GELU/row-broadcast add/row sum/row max/softmax/LayerNorm, [M, N], "
+                      "M in (1024, 16384, 262144), N in (768, 1152, 2304), f16 and f32, N(0, 1) seeded",
+            "unit": "GB/s", "layout": "results[op/dtype][N] = GB/s at M = 1024, 16384, 262144",
+            "peak_gbs": hbm_peak, "peak_src": "measured copy bandwidth (MEASURED_PEAKS.json)",
+            "frac_of_peak_at_M262144": {"median": round(statistics.median(fracs), 3), "min": round(min(fracs), 3),
+                                        "max": round(max(fracs), 3)},
+            "results": out}
+
+
 def predict_leg(b, ev) -> dict:
     """The predict() path: the Laya DecisionModel (ModernBERT-base fp16 encoder +
     the two-layer head, scorer and action head, packages/laya/src/model.ts:124-285)
@@ -601,6 +652,10 @@ def main() -> None:
             line["large_bf16"] = large_leg(b, ev, min(args.steps, 3))
         except Exception as ex:  # noqa: BLE001
             line["large_bf16"] = f"failed: {ex}"
+        try:
+            line["microbench"] = microbench_leg(b, ev, peaks["hbm"])
+        except Exception as ex:  # noqa: BLE001
+            line["microbench"] = f"failed: {ex}"
         try:
             line["cpu_baseline"] = cpu_baseline()
         except Exception as ex:  # noqa: BLE001

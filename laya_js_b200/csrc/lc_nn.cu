@@ -223,7 +223,8 @@ void launch_layernorm_vec(const T* x, const WT* w, const WT* b, T* y, int64_t ro
     case 3: lc::launch_chain(k_layernorm_vec<T, 3, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
     case 4: lc::launch_chain(k_layernorm_vec<T, 4, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
     case 5: case 6: lc::launch_chain(k_layernorm_vec<T, 6, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
-    default: lc::launch_chain(k_layernorm_vec<T, 8, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    case 7: case 8: lc::launch_chain(k_layernorm_vec<T, 8, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
+    default: lc::launch_chain(k_layernorm_vec<T, 12, WT>, dim3(blocks), dim3(256), 0, st, x, w, b, y, rows, N, eps); break;
   }
 }
 
@@ -912,7 +913,7 @@ int lc_layer_norm(lc_tensor* out, lc_tensor xh, lc_tensor wh, lc_tensor bh, doub
     cudaStream_t st = stream();
     bool aligned = (((uintptr_t)x->data() | (uintptr_t)y->data() | (uintptr_t)wp | (uintptr_t)bp) & 15) == 0;
     int vn = x->dtype == LC_F32 ? 4 : 8;
-    bool vec = aligned && x->dtype == odt && (odt == LC_F32 || is_half(odt)) && N % vn == 0 && N / vn <= 32 * 8;
+    bool vec = aligned && x->dtype == odt && (odt == LC_F32 || is_half(odt)) && N % vn == 0 && N / vn <= 32 * 12;
     bool blk = aligned && x->dtype == odt && (odt == LC_F32 || is_half(odt)) && N % vn == 0 && N / vn <= 256 * 8;
     const float* wf = (const float*)wp;
     const float* bf = (const float*)bp;

@@ -478,10 +478,12 @@ std::vector<int64_t> reduced_shape(const LcTensor* x, int a, bool keep) {
 
 // Fast-path dispatch: dense f16 / bf16 / f32 rows of at most 32 * VEC * 8
 // elements, n a multiple of the vector width. Returns false when it does not apply.
-bool row_vec_ok(int dtype, int64_t n, int64_t rows) {
+// `maxv` vectors per lane at most (softmax keeps them in registers: 12; the
+// reductions only stream them: 16).
+bool row_vec_ok(int dtype, int64_t n, int64_t rows, int maxv) {
   if (!(dtype == LC_F16 || dtype == LC_BF16 || dtype == LC_F32) || rows <= 0) return false;
   const int vec = dtype == LC_F32 ? 4 : 8;
-  return n > 0 && n % vec == 0 && n <= 32 * vec * 8 && n < INT32_MAX;
+  return n > 0 && n % vec == 0 && n <= (int64_t)32 * vec * maxv && n < INT32_MAX;
 }
 // Block-per-row path: dense f16 / bf16 / f32 rows longer than the warp path
 // takes, up to 256 threads x 8 vectors, 16-byte aligned.
@@ -499,7 +501,7 @@ unsigned row_blk_grid(int64_t rows) { return (unsigned)std::min<int64_t>(rows, (
 int row_vec_maxv(int dtype, int64_t n) {
   const int vec = dtype == LC_F32 ? 4 : 8;
   const int per = (int)((n / vec + 31) / 32);
-  return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8;
+  return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : per <= 12 ? 12 : 16;
 }
 
 #define LC_ROWVEC_DISPATCH(KERNEL, T, MAXV_RT, BLOCKS, ...)                     \
@@ -543,7 +545,9 @@ void launch_reduce_vec(unsigned blocks, int maxv, int op, const T* x, char* out,
     case 1: launch_reduce_vec_op<T, 1>(blocks, op, x, out, odt, rows, n); break;
     case 2: launch_reduce_vec_op<T, 2>(blocks, op, x, out, odt, rows, n); break;
     case 4: launch_reduce_vec_op<T, 4>(blocks, op, x, out, odt, rows, n); break;
-    default: launch_reduce_vec_op<T, 8>(blocks, op, x, out, odt, rows, n); break;
+    case 8: launch_reduce_vec_op<T, 8>(blocks, op, x, out, odt, rows, n); break;
+    case 12: launch_reduce_vec_op<T, 12>(blocks, op, x, out, odt, rows, n); break;
+    default: launch_reduce_vec_op<T, 16>(blocks, op, x, out, odt, rows, n); break;
   }
 }
 
@@ -554,7 +558,8 @@ void launch_reduce_vec(unsigned blocks, int maxv, int op, const T* x, char* out,
     case 3: KERNEL<T, 3><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
     case 4: KERNEL<T, 4><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
     case 6: KERNEL<T, 6><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
-    default: KERNEL<T, 8><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;   \
+    case 8: KERNEL<T, 8><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;    \
+    default: KERNEL<T, 12><<<BLOCKS, 256, 0, stream()>>>(__VA_ARGS__); break;  \
   }
 
 #define LC_ROWBLK_DISPATCH(KERNEL, T, MAXV_RT, BLOCKS, ...)                     \
@@ -595,7 +600,7 @@ LcTensor* reduce(int op, uint64_t xh, int axis, bool keep, const char* name) {
   if (y->numel() == 0) return y;
   LcTensor* c = contiguous(x);
   int d = x->dtype;
-  if (s.inner == 1 && op != R_ARGMAX && op != R_ARGMIN && row_vec_ok(d, s.n, s.outer) && ((uintptr_t)c->data() & 15) == 0) {
+  if (s.inner == 1 && op != R_ARGMAX && op != R_ARGMIN && row_vec_ok(d, s.n, s.outer, 16) && ((uintptr_t)c->data() & 15) == 0) {
     const unsigned blocks = blocks_for(s.outer * 32, 256);
     const int mv = row_vec_maxv(d, s.n);
     const int n = (int)s.n;
@@ -656,12 +661,12 @@ int lc_softmax(lc_tensor* out, lc_tensor xh, int axis) {
     LcTensor* c = contiguous(x);
     cudaStream_t st = stream();
     bool dbl = x->dtype == LC_F64;
-    if (s.inner == 1 && odt == x->dtype && row_vec_ok(x->dtype, s.n, s.outer) && (((uintptr_t)c->data() | (uintptr_t)y->data()) & 15) == 0) {
+    if (s.inner == 1 && odt == x->dtype && row_vec_ok(x->dtype, s.n, s.outer, 12) && (((uintptr_t)c->data() | (uintptr_t)y->data()) & 15) == 0) {
       const unsigned blocks = blocks_for(s.outer * 32, 256);
       // the register tile holds the whole row: sized to it (3 vectors per lane
       // for 768 16-bit values) so short rows keep more warps resident
       const int per = (int)((s.n / (x->dtype == LC_F32 ? 4 : 8) + 31) / 32);
-      const int mv = per <= 4 ? per : per <= 6 ? 6 : 8;
+      const int mv = per <= 4 ? per : per <= 6 ? 6 : per <= 8 ? 8 : 12;
       const int n = (int)s.n;
       if (x->dtype == LC_F16) { LC_ROWVEC_DISPATCH6(k_softmax_rows_vec, __half, mv, blocks, (const __half*)c->data(), (__half*)y->data(), s.outer, n) }
       else if (x->dtype == LC_BF16) { LC_ROWVEC_DISPATCH6(k_softmax_rows_vec, __nv_bfloat16, mv, blocks, (const __nv_bfloat16*)c->data(), (__nv_bfloat16*)y->data(), s.outer, n) }
