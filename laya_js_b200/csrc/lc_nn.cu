@@ -44,7 +44,9 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   int nv = N / VN;
   for (int64_t r0 = warp * R; r0 < rows; r0 += nwarps * R) {
-    float v[R][MAXV][VN];
+    // the rows stay in registers in their stored form (4 registers per 16-byte
+    // vector); each pass converts what it reads
+    uint4 raw[R][MAXV];
     float s[R], q[R], mu[R], rs[R];
 #pragma unroll
     for (int k = 0; k < R; k++) {
@@ -54,17 +56,12 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
       for (int t = 0; t < MAXV; t++) {
         int c = t * 32 + lane;
         if (c < nv && r < rows) {
-          uint4 raw = *(const uint4*)(x + r * N + (int64_t)c * VN);
-          const T* e = (const T*)&raw;
+          raw[k][t] = *(const uint4*)(x + r * N + (int64_t)c * VN);
+          const T* e = (const T*)&raw[k][t];
 #pragma unroll
-          for (int j = 0; j < VN; j++) {
-            float f;
-            if constexpr (sizeof(T) == 4) f = ((const float*)e)[j];
-            else if constexpr (std::is_same<T, __half>::value) f = __half2float(e[j]);
-            else f = __bfloat162float(e[j]);
-            v[k][t][j] = f;
-            s[k] += f;
-          }
+          for (int j = 0; j < VN; j++) s[k] += to_f<T>(e[j]);
+        } else {
+          raw[k][t] = make_uint4(0u, 0u, 0u, 0u);
         }
       }
     }
@@ -79,9 +76,10 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
 #pragma unroll
       for (int t = 0; t < MAXV; t++) {
         if (t * 32 + lane < nv) {
+          const T* e = (const T*)&raw[k][t];
 #pragma unroll
           for (int j = 0; j < VN; j++) {
-            float d = v[k][t][j] - mu[k];
+            float d = to_f<T>(e[j]) - mu[k];
             q[k] += d * d;
           }
         }
@@ -97,7 +95,7 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
     for (int t = 0; t < MAXV; t++) {
       int c = t * 32 + lane;
       if (c < nv) {
-        uint4 raw[R];
+        uint4 out[R];
 #pragma unroll
         for (int j = 0; j < VN; j += 4) {  // weight and bias four at a time (fewer live registers)
           const float4 a4 = ld_w4<WT>(w, c * VN + j, 1.f);
@@ -105,19 +103,20 @@ __global__ void __launch_bounds__(256) k_layernorm_vec(const T* __restrict__ x, 
           const float wv[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
           for (int k = 0; k < R; k++) {
-            T* e = (T*)&raw[k];
+            const T* e = (const T*)&raw[k][t];
+            T* f = (T*)&out[k];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-              const float o = (v[k][t][j + i] - mu[k]) * rs[k] * wv[i] + bv[i];
-              if constexpr (sizeof(T) == 4) ((float*)e)[j + i] = o;
-              else if constexpr (std::is_same<T, __half>::value) e[j + i] = __float2half_rn(o);
-              else e[j + i] = __float2bfloat16_rn(o);
+              const float o = (to_f<T>(e[j + i]) - mu[k]) * rs[k] * wv[i] + bv[i];
+              if constexpr (sizeof(T) == 4) ((float*)f)[j + i] = o;
+              else if constexpr (std::is_same<T, __half>::value) f[j + i] = __float2half_rn(o);
+              else f[j + i] = __float2bfloat16_rn(o);
             }
           }
         }
 #pragma unroll
         for (int k = 0; k < R; k++)
-          if (r0 + k < rows) *(uint4*)(y + (r0 + k) * N + (int64_t)c * VN) = raw[k];
+          if (r0 + k < rows) *(uint4*)(y + (r0 + k) * N + (int64_t)c * VN) = out[k];
       }
     }
   }
@@ -610,38 +609,35 @@ __global__ void k_geglu_generic(const char* x, int xdt, char* y, int ydt, int64_
   }
 }
 
-// Dense f16 / bf16 / f32 x with D % (16 / sizeof(T)) == 0: block (b, 32*VEC-column
-// chunk); its 8 warps take 32-row chunks of the L positions in turn. A warp
-// reads the 32 mask entries of a chunk at once (one per lane, a ballot gives
-// the kept rows; the next chunk's entries are loaded while this one is
-// summed), then each lane sums VEC columns of the kept rows from 16-byte
-// loads, eight rows in flight; the warps' partial sums and counts combine in
-// shared memory.
+// Dense f16 / bf16 / f32 x with D % (16 / sizeof(T)) == 0: block (32*VEC-column
+// chunk, b, slice of 256 positions); each of its 8 warps takes one 32-row
+// chunk of the slice: it reads the chunk's 32 mask entries at once (one per
+// lane, a ballot gives the kept rows), then each lane sums VEC columns of the
+// kept rows from 16-byte loads, eight rows in flight; the warps' partial sums
+// and counts combine in shared memory. With one slice (L <= 256) the block
+// writes the mean; otherwise it writes its slice's sums and count and
+// k_mean_pool_fin adds the slices in order.
 template <typename T>
 __global__ void __launch_bounds__(256) k_mean_pool_vec(const T* __restrict__ x, const char* mask, int mdt, float* __restrict__ out,
-                                                       int64_t L, int64_t D) {
+                                                       float* __restrict__ part, float* __restrict__ pcnt, int64_t L, int64_t D) {
   pdl_trigger();
   pdl_wait();
   constexpr int VEC = 16 / sizeof(T);
   constexpr int UNR = 8;
-  __shared__ float part[8][32 * VEC];
+  __shared__ float sp[8][32 * VEC];
   __shared__ float cnt[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t b = blockIdx.y;
+  const int64_t b = blockIdx.y, B = gridDim.y, z = blockIdx.z;
   const int64_t c0 = (int64_t)blockIdx.x * 32 * VEC + lane * VEC;
   const bool on = c0 < D;
   float acc[VEC];
 #pragma unroll
   for (int j = 0; j < VEC; j++) acc[j] = 0.f;
-  float n = 0.f;
-  bool keep_next = (int64_t)warp * 32 + lane < L && ld_as<int64_t>(mask, mdt, b * L + (int64_t)warp * 32 + lane) != 0;
-  for (int64_t l0 = (int64_t)warp * 32; l0 < L; l0 += 8 * 32) {
-    const bool keep = keep_next;
-    const int64_t ln = l0 + 8 * 32 + lane;
-    if (l0 + 8 * 32 < L) keep_next = ln < L && ld_as<int64_t>(mask, mdt, b * L + ln) != 0;
-    const uint32_t bits = __ballot_sync(0xffffffffu, keep);
-    n += (float)__popc(bits);
-    if (!on) continue;
+  const int64_t l0 = z * 256 + (int64_t)warp * 32;
+  const bool keep = l0 + lane < L && ld_as<int64_t>(mask, mdt, b * L + l0 + lane) != 0;
+  const uint32_t bits = __ballot_sync(0xffffffffu, keep);
+  const float n = (float)__popc(bits);
+  if (on) {
 #pragma unroll 1
     for (int i0 = 0; i0 < 32; i0 += UNR) {
       if (((bits >> i0) & ((1u << UNR) - 1u)) == 0u) continue;  // warp-uniform
@@ -658,7 +654,7 @@ __global__ void __launch_bounds__(256) k_mean_pool_vec(const T* __restrict__ x, 
     }
   }
 #pragma unroll
-  for (int j = 0; j < VEC; j++) part[warp][lane * VEC + j] = acc[j];
+  for (int j = 0; j < VEC; j++) sp[warp][lane * VEC + j] = acc[j];
   if (lane == 0) cnt[warp] = n;
   __syncthreads();
   if (warp == 0) {
@@ -671,9 +667,27 @@ __global__ void __launch_bounds__(256) k_mean_pool_vec(const T* __restrict__ x, 
       for (int j = 0; j < VEC; j++) {
         float s = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; w++) s += part[w][lane * VEC + j];
-        out[b * D + c0 + j] = s * inv;
+        for (int w = 0; w < 8; w++) s += sp[w][lane * VEC + j];
+        if (gridDim.z == 1) out[b * D + c0 + j] = s * inv;
+        else part[(z * B + b) * D + c0 + j] = s;
       }
+    if (gridDim.z > 1 && blockIdx.x == 0 && lane == 0) pcnt[z * B + b] = tot;
+  }
+}
+
+// The slices' sums of k_mean_pool_vec added in slice order, divided by the count.
+__global__ void __launch_bounds__(256) k_mean_pool_fin(const float* __restrict__ part, const float* __restrict__ pcnt, float* __restrict__ out,
+                                                       int64_t B, int64_t D, int LS) {
+  pdl_trigger();
+  pdl_wait();
+  LC_GRID_STRIDE(t, B * D) {
+    const int64_t b = t / D, d = t % D;
+    float s = 0.f, n = 0.f;
+    for (int z = 0; z < LS; z++) {
+      s += part[(z * B + b) * D + d];
+      n += pcnt[z * B + b];
+    }
+    out[t] = s / fmaxf(n, 1.f);
   }
 }
 
@@ -1128,17 +1142,26 @@ int lc_mean_pool(lc_tensor* out, lc_tensor xh, lc_tensor mh) {
     LcTensor* m = contiguous(m0);
     const int d = x->dtype;
     const int vec = d == LC_F32 ? 4 : 8;
-    if ((d == LC_F16 || d == LC_BF16 || d == LC_F32) && D % vec == 0 && B <= 65535) {
-      dim3 grid((unsigned)((D + 32 * vec - 1) / (32 * vec)), (unsigned)B);
+    const int64_t LS = (L + 255) / 256;
+    if ((d == LC_F16 || d == LC_BF16 || d == LC_F32) && D % vec == 0 && B <= 65535 && LS <= 65535) {
+      dim3 grid((unsigned)((D + 32 * vec - 1) / (32 * vec)), (unsigned)B, (unsigned)std::max<int64_t>(LS, 1));
+      float* part = LS > 1 ? (float*)dmalloc((size_t)(LS * B * D + LS * B) * sizeof(float)) : nullptr;
+      float* pcnt = part ? part + LS * B * D : nullptr;
       if (d == LC_F16)
         lc::launch_chain(k_mean_pool_vec<__half>, grid, dim3(256), 0, stream(), (const __half*)x->data(), (const char*)m->data(), (int)m->dtype,
-                         (float*)y->data(), L, D);
+                         (float*)y->data(), part, pcnt, L, D);
       else if (d == LC_BF16)
         lc::launch_chain(k_mean_pool_vec<__nv_bfloat16>, grid, dim3(256), 0, stream(), (const __nv_bfloat16*)x->data(), (const char*)m->data(),
-                         (int)m->dtype, (float*)y->data(), L, D);
+                         (int)m->dtype, (float*)y->data(), part, pcnt, L, D);
       else
         lc::launch_chain(k_mean_pool_vec<float>, grid, dim3(256), 0, stream(), (const float*)x->data(), (const char*)m->data(), (int)m->dtype,
-                         (float*)y->data(), L, D);
+                         (float*)y->data(), part, pcnt, L, D);
+      if (part) {
+        LC_LAUNCHED(1);
+        lc::launch_chain(k_mean_pool_fin, dim3(blocks_for(B * D, 256)), dim3(256), 0, stream(), (const float*)part, (const float*)pcnt,
+                         (float*)y->data(), B, D, (int)LS);
+        dfree(part);
+      }
     } else {
       k_mean_pool<<<blocks_for(B * D, 256), 256, 0, stream()>>>(x->data(), x->dtype, m->data(), m->dtype, (float*)y->data(), B, L, D);
     }

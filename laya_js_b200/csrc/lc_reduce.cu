@@ -128,20 +128,23 @@ __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ 
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int nv = n / VEC;
+  // 16-bit outputs: the hardware exp2 (relative error ~2^-22, far below the
+  // output's 2^-11 rounding); f32 outputs keep the full expf
+  auto ex = [](float v) { if constexpr (sizeof(T) == 2) return __expf(v); else return expf(v); };
   for (int64_t r = warp; r < rows; r += nwarps) {
-    float v[MAXV][VEC];
+    // the row stays in registers in its stored form (4 registers per 16-byte
+    // vector, whatever T is); each pass converts what it reads, and the
+    // exponentials are recomputed for the output (same values, same order)
+    uint4 raw[MAXV];
     float m = -INFINITY;
 #pragma unroll
     for (int t = 0; t < MAXV; t++) {
       const int c = t * 32 + lane;
       if (c < nv) {
-        const uint4 raw = *(const uint4*)(x + r * n + (int64_t)c * VEC);
-        const T* e = (const T*)&raw;
+        raw[t] = *(const uint4*)(x + r * n + (int64_t)c * VEC);
+        const T* e = (const T*)&raw[t];
 #pragma unroll
-        for (int j = 0; j < VEC; j++) {
-          v[t][j] = to_f<T>(e[j]);
-          m = fmaxf(m, v[t][j]);
-        }
+        for (int j = 0; j < VEC; j++) m = fmaxf(m, to_f<T>(e[j]));
       }
     }
 #pragma unroll
@@ -149,15 +152,11 @@ __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ 
     float s = 0.f;
 #pragma unroll
     for (int t = 0; t < MAXV; t++)
-      if (t * 32 + lane < nv)
+      if (t * 32 + lane < nv) {
+        const T* e = (const T*)&raw[t];
 #pragma unroll
-        for (int j = 0; j < VEC; j++) {
-          // 16-bit outputs: the hardware exp2 (relative error ~2^-22, far below
-          // the output's 2^-11 rounding); f32 outputs keep the full expf
-          if constexpr (sizeof(T) == 2) v[t][j] = __expf(v[t][j] - m);
-          else v[t][j] = expf(v[t][j] - m);
-          s += v[t][j];
-        }
+        for (int j = 0; j < VEC; j++) s += ex(to_f<T>(e[j]) - m);
+      }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float inv = 1.f / s;
@@ -165,11 +164,12 @@ __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ 
     for (int t = 0; t < MAXV; t++) {
       const int c = t * 32 + lane;
       if (c < nv) {
-        uint4 raw;
-        T* e = (T*)&raw;
+        const T* e = (const T*)&raw[t];
+        uint4 o4;
+        T* q = (T*)&o4;
 #pragma unroll
-        for (int j = 0; j < VEC; j++) e[j] = from_f<T>(v[t][j] * inv);
-        *(uint4*)(y + r * n + (int64_t)c * VEC) = raw;
+        for (int j = 0; j < VEC; j++) q[j] = from_f<T>(ex(to_f<T>(e[j]) - m) * inv);
+        *(uint4*)(y + r * n + (int64_t)c * VEC) = o4;
       }
     }
   }

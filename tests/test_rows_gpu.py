@@ -79,10 +79,13 @@ def test_layer_norm_over_rows(dt):
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
-def test_mean_pool_masks(dt):
+@pytest.mark.parametrize("L", [77, 600])
+def test_mean_pool_masks(dt, L):
+    """meanPool over one slice of 256 positions (the block writes the mean)
+    and over three (slice sums added in order by a second kernel)."""
     b = backend()
     rng = np.random.default_rng(3)
-    B, L, D = 5, 77, 768
+    B, D = 5, 768
     a = rng.standard_normal((B, L, D)).astype(np.float32)
     h = _host(dt, a)
     x = to_f32(h).astype(np.float64)
