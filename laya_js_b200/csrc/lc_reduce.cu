@@ -124,6 +124,11 @@ __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ 
   pdl_trigger();
   pdl_wait();
   constexpr int VEC = 16 / sizeof(T);
+  // short rows (up to 4 vectors per lane) keep the values and then the
+  // exponentials as floats; longer rows stay in registers in their stored
+  // form (4 registers per 16-byte vector), each pass converts what it reads
+  // and the exponentials are recomputed for the output (same values, same order)
+  constexpr bool KEEP_F = MAXV <= 4;
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -132,19 +137,22 @@ __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ 
   // output's 2^-11 rounding); f32 outputs keep the full expf
   auto ex = [](float v) { if constexpr (sizeof(T) == 2) return __expf(v); else return expf(v); };
   for (int64_t r = warp; r < rows; r += nwarps) {
-    // the row stays in registers in its stored form (4 registers per 16-byte
-    // vector, whatever T is); each pass converts what it reads, and the
-    // exponentials are recomputed for the output (same values, same order)
-    uint4 raw[MAXV];
+    uint4 raw[KEEP_F ? 1 : MAXV];
+    float v[KEEP_F ? MAXV : 1][VEC];
     float m = -INFINITY;
 #pragma unroll
     for (int t = 0; t < MAXV; t++) {
       const int c = t * 32 + lane;
       if (c < nv) {
-        raw[t] = *(const uint4*)(x + r * n + (int64_t)c * VEC);
-        const T* e = (const T*)&raw[t];
+        const uint4 ld = *(const uint4*)(x + r * n + (int64_t)c * VEC);
+        const T* e = (const T*)&ld;
+        if constexpr (!KEEP_F) raw[t] = ld;
 #pragma unroll
-        for (int j = 0; j < VEC; j++) m = fmaxf(m, to_f<T>(e[j]));
+        for (int j = 0; j < VEC; j++) {
+          const float f = to_f<T>(e[j]);
+          if constexpr (KEEP_F) v[t][j] = f;
+          m = fmaxf(m, f);
+        }
       }
     }
 #pragma unroll
@@ -153,9 +161,15 @@ __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ 
 #pragma unroll
     for (int t = 0; t < MAXV; t++)
       if (t * 32 + lane < nv) {
-        const T* e = (const T*)&raw[t];
 #pragma unroll
-        for (int j = 0; j < VEC; j++) s += ex(to_f<T>(e[j]) - m);
+        for (int j = 0; j < VEC; j++) {
+          if constexpr (KEEP_F) {
+            v[t][j] = ex(v[t][j] - m);
+            s += v[t][j];
+          } else {
+            s += ex(to_f<T>(((const T*)&raw[t])[j]) - m);
+          }
+        }
       }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -164,11 +178,13 @@ __global__ void __launch_bounds__(256) k_softmax_rows_vec(const T* __restrict__ 
     for (int t = 0; t < MAXV; t++) {
       const int c = t * 32 + lane;
       if (c < nv) {
-        const T* e = (const T*)&raw[t];
         uint4 o4;
         T* q = (T*)&o4;
 #pragma unroll
-        for (int j = 0; j < VEC; j++) q[j] = from_f<T>(ex(to_f<T>(e[j]) - m) * inv);
+        for (int j = 0; j < VEC; j++) {
+          if constexpr (KEEP_F) q[j] = from_f<T>(v[t][j] * inv);
+          else q[j] = from_f<T>(ex(to_f<T>(((const T*)&raw[t])[j]) - m) * inv);
+        }
         *(uint4*)(y + r * n + (int64_t)c * VEC) = o4;
       }
     }
