@@ -495,7 +495,7 @@ std::vector<int64_t> reduced_shape(const LcTensor* x, int a, bool keep) {
 // Fast-path dispatch: dense f16 / bf16 / f32 rows of at most 32 * VEC * 8
 // elements, n a multiple of the vector width. Returns false when it does not apply.
 // `maxv` vectors per lane at most (softmax keeps them in registers: 12; the
-// reductions only stream them: 16).
+// reductions only stream them: 24).
 bool row_vec_ok(int dtype, int64_t n, int64_t rows, int maxv) {
   if (!(dtype == LC_F16 || dtype == LC_BF16 || dtype == LC_F32) || rows <= 0) return false;
   const int vec = dtype == LC_F32 ? 4 : 8;
@@ -517,7 +517,7 @@ unsigned row_blk_grid(int64_t rows) { return (unsigned)std::min<int64_t>(rows, (
 int row_vec_maxv(int dtype, int64_t n) {
   const int vec = dtype == LC_F32 ? 4 : 8;
   const int per = (int)((n / vec + 31) / 32);
-  return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : per <= 12 ? 12 : 16;
+  return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : per <= 12 ? 12 : per <= 16 ? 16 : 24;
 }
 
 #define LC_ROWVEC_DISPATCH(KERNEL, T, MAXV_RT, BLOCKS, ...)                     \
@@ -563,7 +563,8 @@ void launch_reduce_vec(unsigned blocks, int maxv, int op, const T* x, char* out,
     case 4: launch_reduce_vec_op<T, 4>(blocks, op, x, out, odt, rows, n); break;
     case 8: launch_reduce_vec_op<T, 8>(blocks, op, x, out, odt, rows, n); break;
     case 12: launch_reduce_vec_op<T, 12>(blocks, op, x, out, odt, rows, n); break;
-    default: launch_reduce_vec_op<T, 16>(blocks, op, x, out, odt, rows, n); break;
+    case 16: launch_reduce_vec_op<T, 16>(blocks, op, x, out, odt, rows, n); break;
+    default: launch_reduce_vec_op<T, 24>(blocks, op, x, out, odt, rows, n); break;
   }
 }
 
@@ -616,7 +617,7 @@ LcTensor* reduce(int op, uint64_t xh, int axis, bool keep, const char* name) {
   if (y->numel() == 0) return y;
   LcTensor* c = contiguous(x);
   int d = x->dtype;
-  if (s.inner == 1 && op != R_ARGMAX && op != R_ARGMIN && row_vec_ok(d, s.n, s.outer, 16) && ((uintptr_t)c->data() & 15) == 0) {
+  if (s.inner == 1 && op != R_ARGMAX && op != R_ARGMIN && row_vec_ok(d, s.n, s.outer, 24) && ((uintptr_t)c->data() & 15) == 0) {
     const unsigned blocks = blocks_for(s.outer * 32, 256);
     const int mv = row_vec_maxv(d, s.n);
     const int n = (int)s.n;

@@ -1,7 +1,7 @@
 """The row fast paths (softmax, layerNorm, sum / mean / max / min over the
 last axis, meanPool) against float64 numpy, across the widths that select
 them (a multiple of the 16-byte vector: one warp per row up to 32 lanes x 12
-vectors for softmax / layerNorm and x 16 for the reductions, one 256-thread
+vectors for softmax / layerNorm and x 24 for the reductions, one 256-thread
 block per row up to 256 x 8 vectors) and the widths that fall back to the
 generic kernels, in f32 / f16 / bf16; NaN propagation of max / min; meanPool
 with masked-out and fully masked rows."""
@@ -15,8 +15,8 @@ from laya_js_b200.host import HostTensor, f32_to_bf16_bits, to_f32
 
 pytestmark = pytest.mark.gpu
 
-WIDTHS = {"f32": [4, 256, 1024, 1028, 770, 1152, 1536, 1540, 2048, 2304, 8192, 8196],
-          "f16": [8, 768, 1152, 2048, 2056, 770, 2304, 3072, 3080, 4096, 16384, 16392],
+WIDTHS = {"f32": [4, 256, 1024, 1028, 770, 1152, 1536, 1540, 2048, 2304, 3072, 3076, 8192, 8196],
+          "f16": [8, 768, 1152, 2048, 2056, 770, 2304, 3072, 3080, 4096, 6144, 6152, 16384, 16392],
           "bf16": [8, 512, 2048, 2056, 770, 1152, 3072, 4096, 16384]}
 EPS = {"f32": 1e-5, "f16": 2e-3, "bf16": 1.6e-2}
 
