@@ -147,3 +147,72 @@ def test_gloo_world2_encoder_worker_matches_one_process():
     for fail in (-1, 1):
         got = _spawn_encoder(fail)
         assert np.array_equal(got[0], want) and np.array_equal(got[1], want), f"fail_rank={fail}"
+
+
+def _store_rank(rank, world, port, fault, q):
+    """One rank of run_data_parallel_store over a TCPStore held by rank 0;
+    `fault` = (rank, kind): that rank's first worker call exits the process,
+    hangs, or raises."""
+    import time
+    from datetime import timedelta
+
+    from torch.distributed import TCPStore
+
+    from laya_js_b200.dp import run_data_parallel_store
+    store = TCPStore("127.0.0.1", port, world, rank == 0, timedelta(seconds=60), wait_for_workers=False)
+    calls = {"n": 0}
+
+    def worker(idx):
+        calls["n"] += 1
+        if fault[0] == rank and calls["n"] == 1:
+            if fault[1] == "exit":
+                os._exit(3)  # the process dies mid-run
+            if fault[1] == "hang":
+                time.sleep(600)
+            raise RuntimeError("injected worker failure")
+        return [i * i for i in idx]
+
+    res = run_data_parallel_store([float(L) for L in range(10, 40)], worker, rank, world, store, timeout_s=3.0)
+    q.put((rank, res))
+
+
+def _spawn_store(fault):
+    world, port = 3, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_store_rank, args=(r, world, port, fault, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    survivors = [r for r in range(world) if not (r == fault[0] and fault[1] in ("exit", "hang"))]
+    got = dict(q.get(timeout=120) for _ in survivors)
+    for r, p in enumerate(ps):
+        if r in survivors:
+            p.join(timeout=60)
+            assert p.exitcode == 0, f"rank {r} exit code {p.exitcode}"
+        elif fault[1] == "exit":
+            p.join(timeout=60)
+            assert p.exitcode == 3
+        else:
+            p.kill()  # the hung rank (a child of this test)
+            p.join(timeout=60)
+    return got
+
+
+def test_store_runner_survives_a_dead_rank():
+    """Rank 2's process exits inside its worker: rank 0 stops waiting for it
+    after the timeout and re-runs its prompts on ranks 0 and 1."""
+    got = _spawn_store((2, "exit"))
+    want = [i * i for i in range(30)]
+    assert set(got) == {0, 1} and got[0] == want and got[1] == want
+
+
+def test_store_runner_survives_a_hung_rank():
+    got = _spawn_store((1, "hang"))
+    want = [i * i for i in range(30)]
+    assert set(got) == {0, 2} and got[0] == want and got[2] == want
+
+
+def test_store_runner_reshards_a_raising_rank():
+    got = _spawn_store((1, "raise"))
+    want = [i * i for i in range(30)]
+    assert got == {0: want, 1: want, 2: want}
