@@ -86,6 +86,21 @@ def linear_flops_per_token(cfg: dict) -> float:
     return 2.0 * (H * 3 * H + H * H + H * 2 * I + I * H) * n
 
 
+def attention_flops(cfg: dict, lens) -> float:
+    """QKᵀ and P·V FLOPs of one forward over prompts of the given lengths:
+    4·H per visible (query, key) pair; global layers (every third, from the
+    first) see the whole prompt, sliding layers the keys within window/2."""
+    H, n = cfg["hidden_size"], cfg["num_hidden_layers"]
+    half = cfg.get("local_attention", 128) // 2
+    n_global = (n + 2) // 3
+    total = 0.0
+    for L in np.asarray(lens, np.int64):
+        i = np.arange(L)
+        pairs_local = float((np.minimum(i + half, L - 1) - np.maximum(i - half, 0) + 1).sum())
+        total += n_global * float(L) * float(L) + (n - n_global) * pairs_local
+    return 4.0 * H * total
+
+
 def measured_peaks() -> dict:
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
@@ -360,14 +375,27 @@ def large_leg(b, ev, steps: int, n_prompts: int = 1024) -> dict:
         b.dispose(p)
     step()
     ms = ev.time(step, steps)
+    # one more step with CUDA events around every kernel class (not timed above)
+    E.set_profiling(fused, True)
+    E.profile_read(fused)
+    step()
+    b.flush()
+    prof = E.profile_read(fused)
+    E.set_profiling(fused, False)
     T = int(cu[-1])
     flops = linear_flops_per_token(WL.LARGE) * T
+    aflops = attention_flops(WL.LARGE, lens)
     for t in (tids, thw, thb):
         b.dispose(t)
     fused.free()
     enc.dispose()
     return {"value": T * steps / (ms / 1e3), "unit": "tokens/s", "steps": steps, "ms_per_step": ms / steps, "tokens_per_step": T,
             "linear_tflops": flops / (ms / steps / 1e3) / 1e12,
+            "linear_tflops_note": "linear-layer FLOPs over the whole step's time (attention included)",
+            "kernel_ms_per_step": {k: v["ms"] for k, v in prof.items()},
+            "gemm_tflops": flops / (prof["gemm"]["ms"] / 1e3) / 1e12 if prof["gemm"]["ms"] > 0 else None,
+            "attention_tflops": aflops / (prof["attention"]["ms"] / 1e3) / 1e12 if prof["attention"]["ms"] > 0 else None,
+            "attention_tflop_per_step": aflops / 1e12,
             "config": f"configs[4]: ModernBERT-large/mmBERT shape bf16, 28 layers, the first {n_prompts} prompts of the 65,536 "
                       "log-uniform [16,4096] draw, 16-way head"}
 
