@@ -437,7 +437,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& args, const CUtenso
     const float4* rq = (const float4*)ep.rope_cs + (rope && live ? ep.pos[row] : 0);
     // the first unit's LayerNorm column sums (lane l: columns 2l, 2l+1)
     float2 wsp = make_float2(0.f, 0.f);
-    if (ep.ln_stats && mine) wsp = __ldg((const float2*)(ep.ln_wsum + n0 + u_lo * 64) + lane);
+    if (ep.ln_stats && mine && n0 + u_lo * 64 < ncols) wsp = __ldg((const float2*)(ep.ln_wsum + n0 + u_lo * 64) + lane);
     if (ahead && mine) {  // the residual blocks, in flight while the accumulator is computed
       if (lane == 0) bulk_wait_read0();  // earlier stores have read the buffers
       __syncwarp();
@@ -718,8 +718,8 @@ __device__ __forceinline__ void epilogue_split(const GemmArgs& args, const CUten
   const int gc = n0 + col;                                // accumulator column
   const bool rope = ep.kind == EPI_ROPE_QKV && n0 + unit * 64 < ep.rope_cols;
   const int nparts = args.N / 64;
-  float wsum[8];
-  if (ep.ln_stats) {
+  float wsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (ep.ln_stats && gc < (geglu ? 2 * args.N : args.N)) {  // a GeGLU tile may run past the weight rows
     const float4 w0 = __ldg((const float4*)(ep.ln_wsum + gc)), w1 = __ldg((const float4*)(ep.ln_wsum + gc) + 1);
     wsum[0] = w0.x, wsum[1] = w0.y, wsum[2] = w0.z, wsum[3] = w0.w, wsum[4] = w1.x, wsum[5] = w1.y, wsum[6] = w1.z, wsum[7] = w1.w;
   }
@@ -1687,9 +1687,12 @@ bool gemm_raw_q(const void* x, int64_t M, int64_t K, const GemmQuantB& q, int64_
   return true;
 }
 
+// GeGLU needs whole (gate, up) 64-column unit pairs in every tile that holds
+// data: Nacc % 128 == 0 is enough for 256-wide tiles (a last tile of 128
+// columns leaves its second half empty; configs[4]'s 2 x 2624 = 5248).
 int gemm_tile_n(int64_t Nacc, bool geglu) {
   int BN = (Nacc % 256 == 0 || Nacc > 1024) ? 256 : 128;
-  if (geglu && Nacc % BN) BN = 128;
+  if (geglu && Nacc % 128) BN = 128;
   return BN;
 }
 
