@@ -440,14 +440,18 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
 // Frees the CUDA graphs captured on an encoder (they reference its weights).
 void free_graphs_of(Encoder* e);
 
-// Workspace of one forward over T tokens: x [T,H] | h [T,H] | qkv [T,3H] |
-// pos [T] | LayerNorm row statistics [T][parts] (float2).
+// Workspace of one forward over T tokens: x [T,H] | h [T,H] | qkv [T,Q] |
+// pos [T] | LayerNorm row statistics [T][parts] (float2). The qkv region also
+// holds the GeGLU output [T,I], so Q = max(3H, I) (I > 3H for a narrow model
+// with a wide MLP, e.g. H 768 with I 2624).
+int64_t qkv_cols(const lc_encoder_config& c) { return std::max<int64_t>(3 * (int64_t)c.hidden_size, c.intermediate_size); }
+size_t pos_offset(const lc_encoder_config& c, int64_t T) { return (size_t)T * (2 * (size_t)c.hidden_size + (size_t)qkv_cols(c)) * 2; }
 int stats_parts(const lc_encoder_config& c) {
   const int pc = gemm_stats_part_cols(c.hidden_size);
   return (c.hidden_size + pc - 1) / pc;
 }
 size_t stats_offset(const lc_encoder_config& c, int64_t T) {
-  return ((size_t)T * c.hidden_size * 2 * 5 + (size_t)T * 4 + 255) & ~(size_t)255;
+  return (pos_offset(c, T) + (size_t)T * 4 + 255) & ~(size_t)255;
 }
 size_t workspace_bytes(const lc_encoder_config& c, int64_t T) {
   return stats_offset(c, T) + (size_t)T * stats_parts(c) * sizeof(float2);
@@ -492,7 +496,7 @@ void forward(Encoder* e, const int32_t* ids_dev, const int32_t* cu, int nseq, Lc
 }
 
 // The kernel sequence of one forward on prepared buffers: ws = x [T,H] | h [T,H] |
-// qkv [T,3H] | pos [T]; cu_dev / tiles_dev on the device. Enqueues work only
+// qkv [T,max(3H,I)] | pos [T] | row statistics; cu_dev / tiles_dev on the device. Enqueues work only
 // (no host synchronisation, no allocation once the encoder is warm), so a
 // stream capture of it replays the forward.
 void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const int32_t* cu_dev, const int4* tiles_dev, int ntiles,
@@ -504,7 +508,7 @@ void run_kernels(Encoder* e, char* ws, int64_t T, int nseq, int maxlen, const in
   void* x = ws;
   void* h = ws + (size_t)T * H * esz;
   void* qkv = ws + (size_t)2 * T * H * esz;
-  int32_t* pos = (int32_t*)(ws + (size_t)5 * T * H * esz);
+  int32_t* pos = (int32_t*)(ws + pos_offset(c, T));
   float2* stats = (float2*)(ws + stats_offset(c, T));
   const int parts = stats_parts(c), part_cols = gemm_stats_part_cols(H);
   // every kernel below waits for its predecessor on the device (pdl_wait)

@@ -97,6 +97,28 @@ def test_fused_encoder_matches_oracle(quant_bits, tol):
     enc.dispose()
 
 
+@pytest.mark.parametrize("inter", [576, 2624])
+def test_fused_encoder_geglu_width_not_a_multiple_of_256(inter):
+    """Wi's accumulator (2I columns of interleaved gate / up units) of 1152 and
+    5248 (configs[4]'s intermediate size): 256-wide CTA-pair tiles whose last
+    tile holds one 128-column unit pair and leaves its upper half empty. 1990
+    tokens, so the projections take the ordinary tiles, not the few-row
+    split-K clusters."""
+    cfg_json = {**small_base(2), "intermediate_size": inter}
+    b, W, cfg, enc = _model(cfg_json)
+    lens = np.array([1, 17, 64, 65, 130, 200, 300, 513, 700])
+    ids, cu = WL.token_batch(cfg_json, lens, seed=12)
+    fused = FusedEncoder(enc)
+    hid, _ = fused.forward(b.fromHost(HostTensor("i32", ids.shape, ids)), cu)
+    hid = to_f32(b.read(hid))
+    ref = np.concatenate(M.encoder_varlen(M.parse_config(cfg_json), _oracle_weights(W, 0),
+                                          [ids[cu[s]:cu[s + 1]] for s in range(len(lens))]))
+    err = float(np.abs(hid - ref).max())
+    assert err < 0.2, f"I={inter}: hidden max err {err}"
+    fused.free()
+    enc.dispose()
+
+
 def test_fused_matches_contract_path():
     """The fused varlen forward equals ModernBert.forward (padded, host masks) on valid tokens."""
     cfg_json = small_base(3)
