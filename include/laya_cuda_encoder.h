@@ -46,6 +46,11 @@ typedef struct {
  * the order above; for quant_bits != 0 each Linear weight (Wqkv, Wo, Wi,
  * mlp.Wo) is replaced by three consecutive handles (packed, scales, biases|0)
  * from lc_from_host_quantized. The encoder keeps its own references.
+ * Shapes: head dim 64 (hidden_size = 64 * num_heads), hidden_size a multiple
+ * of 64 up to 2048, intermediate_size a multiple of 32 (any size relative to
+ * hidden_size), f16 or bf16; the forwards take sequences of 1 to 8192 tokens.
+ * Other shapes return an error; the contract ops (ModernBert.forward) serve
+ * them.
  */
 int lc_encoder_create(uint64_t* enc, const lc_encoder_config* cfg, const int32_t* layer_kinds, const lc_tensor* weights, int nweights);
 int lc_encoder_free(uint64_t enc);
