@@ -25,6 +25,28 @@ def test_binding_signatures_resolve():
         assert getattr(lib, name).argtypes is not None or name in ("lc_destroy", "lc_last_error", "lc_flush")
 
 
+def test_typescript_ffi_table_matches_header():
+    """The TypeScript binding (ts/backend-cuda/src/ffi.ts SYMBOLS) declares each
+    entry's argument codes by hand; they must follow include/laya_cuda.h:
+    pointers 'p', 64-bit integers (tensor handles, int64 sizes) 'h', int 'i',
+    double 'd', size_t 'z'."""
+    import re
+    from pathlib import Path
+
+    src = (Path(_lib.__file__).resolve().parent / "ts" / "backend-cuda" / "src" / "ffi.ts").read_text()
+    alias = {k: re.findall(r'"(\w)"', v) for k, v in re.findall(r"const (\w+): A\[\] = (\[[^\]]*\]);", src)}
+    start = src.index("export const SYMBOLS")
+    table = {name: alias[spec] if spec in alias else re.findall(r'"(\w)"', spec)
+             for name, spec in re.findall(r"(lc_\w+):\s*(\[[^\]]*\]|\w+)", src[start:src.index("};", start)])}
+    assert len(table) >= 60
+    codes = {"lc_tensor": "h", "uint64_t": "h", "int64_t": "h", "int": "i", "int32_t": "i", "double": "d", "size_t": "z"}
+    decls = _lib.header_declarations()
+    for name, got in table.items():
+        assert name in decls, f"{name} is bound in ffi.ts but not declared in include/"
+        want = ["p" if t.endswith("*") else codes.get(t, "?" + t) for t in decls[name][1]]
+        assert got == want, f"{name}: ffi.ts {got}, header {want} ({decls[name][1]})"
+
+
 def test_lc_supports_without_device():
     lib = _lib.load()
     out = ctypes.c_int()
