@@ -25,19 +25,28 @@ def test_binding_signatures_resolve():
         assert getattr(lib, name).argtypes is not None or name in ("lc_destroy", "lc_last_error", "lc_flush")
 
 
+def _ts_sources():
+    from pathlib import Path
+    d = Path(_lib.__file__).resolve().parent / "ts" / "backend-cuda" / "src"
+    return (d / "ffi.ts").read_text(), (d / "index.ts").read_text()
+
+
+def _ts_symbol_table() -> dict[str, list[str]]:
+    """ffi.ts SYMBOLS: name -> argument codes (aliases OP1 / OP2 / RED expanded)."""
+    import re
+    src, _ = _ts_sources()
+    alias = {k: re.findall(r'"(\w)"', v) for k, v in re.findall(r"const (\w+): A\[\] = (\[[^\]]*\]);", src)}
+    start = src.index("export const SYMBOLS")
+    return {name: alias[spec] if spec in alias else re.findall(r'"(\w)"', spec)
+            for name, spec in re.findall(r"(lc_\w+):\s*(\[[^\]]*\]|\w+)", src[start:src.index("};", start)])}
+
+
 def test_typescript_ffi_table_matches_header():
     """The TypeScript binding (ts/backend-cuda/src/ffi.ts SYMBOLS) declares each
     entry's argument codes by hand; they must follow include/laya_cuda.h:
     pointers 'p', 64-bit integers (tensor handles, int64 sizes) 'h', int 'i',
     double 'd', size_t 'z'."""
-    import re
-    from pathlib import Path
-
-    src = (Path(_lib.__file__).resolve().parent / "ts" / "backend-cuda" / "src" / "ffi.ts").read_text()
-    alias = {k: re.findall(r'"(\w)"', v) for k, v in re.findall(r"const (\w+): A\[\] = (\[[^\]]*\]);", src)}
-    start = src.index("export const SYMBOLS")
-    table = {name: alias[spec] if spec in alias else re.findall(r'"(\w)"', spec)
-             for name, spec in re.findall(r"(lc_\w+):\s*(\[[^\]]*\]|\w+)", src[start:src.index("};", start)])}
+    table = _ts_symbol_table()
     assert len(table) >= 60
     codes = {"lc_tensor": "h", "uint64_t": "h", "int64_t": "h", "int": "i", "int32_t": "i", "double": "d", "size_t": "z"}
     decls = _lib.header_declarations()
@@ -45,6 +54,47 @@ def test_typescript_ffi_table_matches_header():
         assert name in decls, f"{name} is bound in ffi.ts but not declared in include/"
         want = ["p" if t.endswith("*") else codes.get(t, "?" + t) for t in decls[name][1]]
         assert got == want, f"{name}: ffi.ts {got}, header {want} ({decls[name][1]})"
+
+
+def _top_level_args(text: str, i: int) -> list[str]:
+    """Arguments of the call whose '(' is text[i], split at top-level commas."""
+    depth, cur, out = 0, "", []
+    for c in text[i:]:
+        if c in "([{":
+            depth += 1
+            if depth == 1:
+                continue
+        elif c in ")]}":
+            depth -= 1
+            if depth == 0:
+                out.append(cur.strip())
+                break
+        elif c == "," and depth == 1:
+            out.append(cur.strip())
+            cur = ""
+            continue
+        cur += c
+    return [a for a in out if a]
+
+
+def test_typescript_call_sites_pass_every_argument():
+    """index.ts calls the binding as op("lc_x", ...) (the output pointer is
+    prepended), N.call("lc_x", ...), or through un / bin / red (2, 3 and 4
+    arguments): each call's argument count must equal the entry's arity."""
+    import re
+    table = _ts_symbol_table()
+    _, src = _ts_sources()
+    sites = []
+    for kind, implicit in (("op", 1), ("N.call", 0)):
+        for m in re.finditer(r"\b" + re.escape(kind) + r'\(\s*"(lc_\w+)"', src):
+            args = _top_level_args(src, m.start() + len(kind))
+            sites.append((m.group(1), len(args) - 1 + implicit))
+    for helper, n in (("un", 2), ("bin", 3), ("red", 4)):
+        sites += [(name, n) for name in re.findall(r"\b" + helper + r'\(\s*"(lc_\w+)"\s*\)', src)]
+    assert len(sites) >= 60
+    for name, n in sites:
+        assert name in table, f"index.ts calls {name}, which ffi.ts does not bind"
+        assert n == len(table[name]), f"index.ts passes {n} arguments to {name}, which takes {len(table[name])}"
 
 
 def test_lc_supports_without_device():
