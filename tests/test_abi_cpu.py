@@ -97,6 +97,53 @@ def test_typescript_call_sites_pass_every_argument():
         assert n == len(table[name]), f"index.ts passes {n} arguments to {name}, which takes {len(table[name])}"
 
 
+def _ts_backend_members(src: str) -> set[str]:
+    """Top-level keys of the `const b = { ... }` object in index.ts (properties
+    `name: ...` and methods `name(...) {`, `async name(...)`, `name<R>(...)`)."""
+    import re
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = re.sub(r"//[^\n]*", "", src)
+    i = src.index("const b = {") + len("const b = ")
+    keys, tok, depth, generic = set(), "", 0, 0
+    for c in src[i:]:
+        if tok is not None and depth == 1:  # reading a member's key
+            if c == "<":
+                generic += 1
+                continue
+            if generic:
+                generic -= c == ">"
+                continue
+            if c in ":(":
+                m = re.fullmatch(r"\s*(?:async\s+)?(\w+)\s*", tok)
+                if m:
+                    keys.add(m.group(1))
+                tok = None  # skip to the next top-level comma
+            else:
+                tok += c
+        if c in "([{":
+            depth += 1
+        elif c in ")]}":
+            depth -= 1
+            if depth == 0:
+                break
+        elif c == "," and depth == 1:
+            tok = ""
+    return keys
+
+
+def test_typescript_and_python_backends_expose_the_same_methods():
+    """The two host mirrors of Backend<T> (ts/backend-cuda/src/index.ts and
+    laya_js_b200/backend.py) offer the same public members."""
+    import inspect
+
+    from laya_js_b200.backend import CudaBackend
+    _, src = _ts_sources()
+    ts = _ts_backend_members(src) - {"name"}
+    py = {n for n, _ in inspect.getmembers(CudaBackend, predicate=inspect.isfunction) if not n.startswith("_")}
+    assert len(ts) >= 55
+    assert ts == py, f"only in TypeScript: {sorted(ts - py)}; only in Python: {sorted(py - ts)}"
+
+
 def test_lc_supports_without_device():
     lib = _lib.load()
     out = ctypes.c_int()
