@@ -76,9 +76,11 @@ bool upload_settled(const LcStorage* st) { return st->upload_mark >= 0 && S().la
 // (a PdlScope). The contract's ops are launched serialised unless
 // LAYA_CUDA_PDL=1: every kernel launched through launch_chain waits for its
 // predecessor before touching memory, but with chaining on, a padded 4-bit
-// contract forward gave a 1024-token prompt's hidden rows that differed in
-// the last bits between processes (an ordering not yet found), and chaining
-// bought no measurable latency on the compiled predict path.
+// contract forward gave a 1024-token prompt's hidden rows that differed from
+// one process to the next (up to 5.4e-2 from the CPU reference, against
+// 1.1e-2 serialised, which is the same in every run; the ordering is not yet
+// found), and chaining made the padded 256-prompt forward slower, not faster
+// (71-72 ms against 65-68 ms).
 bool& pdl_flag() {
   static const bool dflt = [] {
     const char* v = getenv("LAYA_CUDA_PDL");
