@@ -176,3 +176,18 @@ def test_bf16_host_rounding():
     h = host("bf16", (4,), x)
     back = to_f32(h)
     assert back[0] == 1.0 and back[2] == np.float32(-3.296875) and np.isnan(back[3])
+
+
+def test_every_environment_setting_is_documented():
+    """Each LAYA_CUDA_* variable the library or the Python mirror reads is in
+    INTEGRATION.md's table of settings."""
+    import re
+    from pathlib import Path
+    pkg = Path(_lib.__file__).resolve().parent
+    read = set()
+    for f in list((pkg / "csrc").glob("*.cu")) + list((pkg / "csrc").glob("*.cuh")) + list(pkg.glob("*.py")):
+        read |= set(re.findall(r"""(?:getenv|environ\.get)\(\s*["'](LAYA_CUDA_\w+)["']""", f.read_text()))
+    assert {"LAYA_CUDA_LIB", "LAYA_CUDA_PDL"} <= read
+    doc = (pkg.parent / "INTEGRATION.md").read_text()
+    missing = sorted(v for v in read if f"`{v}`" not in doc)
+    assert not missing, f"settings read by the code but not in INTEGRATION.md: {missing}"
