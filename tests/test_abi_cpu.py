@@ -1,5 +1,8 @@
 """C-ABI checks that need no GPU: the library loads and exports every
-function include/*.h declares, and the host helpers mirror host.ts."""
+function include/*.h declares; the TypeScript binding (ffi.ts table, index.ts
+call sites, Backend members) agrees with the header and with the Python
+mirror; every environment setting is documented; the host helpers mirror
+host.ts."""
 from __future__ import annotations
 
 import ctypes
