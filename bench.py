@@ -101,11 +101,19 @@ def attention_flops(cfg: dict, lens) -> float:
     return 4.0 * H * total
 
 
+PEAK_SRC = {"measured": ("measured sustained bf16 (MEASURED_PEAKS.json)", "measured copy bandwidth (MEASURED_PEAKS.json)"),
+            "fallback": ("fallback: the pool's earlier sustained bf16 measurement (MEASURED_PEAKS.json absent or incomplete)",
+                         "fallback: the pool's earlier copy-bandwidth measurement (MEASURED_PEAKS.json absent or incomplete)")}
+
+
 def measured_peaks() -> dict:
+    """Roofline denominators: MEASURED_PEAKS.json (written per pod: sustained
+    bf16 GEMM TFLOP/s, copy GB/s), else the pool's earlier measurement
+    (1.4 PFLOP/s sustained, 6.65 TB/s), labelled "fallback"."""
     f = ROOT / "MEASURED_PEAKS.json"
-    if f.exists():
-        d = json.loads(f.read_text())
-        return {"bf16": d.get("bf16_tflops_sustained", 1417.5), "hbm": d.get("hbm_gbs", 6449.7), "src": "measured"}
+    d = json.loads(f.read_text()) if f.exists() else {}
+    if "bf16_tflops_sustained" in d and "hbm_gbs" in d:
+        return {"bf16": float(d["bf16_tflops_sustained"]), "hbm": float(d["hbm_gbs"]), "src": "measured"}
     return {"bf16": 1400.0, "hbm": 6650.0, "src": "fallback"}
 
 
@@ -440,7 +448,7 @@ def contract_leg(b, ev, enc, thw3, thb3, thw8, thb8) -> dict:
                     "row kernels) + CLS head, host buffers in and out, CUDA events on the library stream"}
 
 
-def microbench_leg(b, ev, hbm_peak: float) -> dict:
+def microbench_leg(b, ev, hbm_peak: float, peak_src: str = "measured copy bandwidth (MEASURED_PEAKS.json)") -> dict:
     """the tensor-backend op microbench — add, mul, GELU, row
     broadcast add, row sum / max, softmax and LayerNorm over [M, N] in f16 and
     f32, M in {1024, 16384, 262144}, N in {768, 1152, 2304}, values N(0, 1)
@@ -483,7 +491,7 @@ def microbench_leg(b, ev, hbm_peak: float) -> dict:
     return {"config": "configs[1]: add/mul/GELU/row-broadcast add/row sum/row max/softmax/LayerNorm, [M, N], "
                       "M in (1024, 16384, 262144), N in (768, 1152, 2304), f16 and f32, N(0, 1) seeded",
             "unit": "GB/s", "layout": "results[op/dtype][N] = GB/s at M = 1024, 16384, 262144",
-            "peak_gbs": hbm_peak, "peak_src": "measured copy bandwidth (MEASURED_PEAKS.json)",
+            "peak_gbs": hbm_peak, "peak_src": peak_src,
             "frac_of_peak_at_M262144": {"median": round(statistics.median(fracs), 3), "min": round(min(fracs), 3),
                                         "max": round(max(fracs), 3)},
             "results": out}
@@ -639,7 +647,7 @@ def main() -> None:
                      "traffic_src": "profiles/gemm_traffic_bench.md: ncu dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch",
                      "flop_per_launch": gemm_flops / max(g["launches"], 1),
                      "kernel": "k_gemm_pair (tcgen05 CTA-pair GEMMs: Wqkv+RoPE+folded LN, Wo+residual, Wi+GeGLU+folded LN, mlp.Wo+residual)",
-                     "peak_src": f"{peaks['src']} sustained bf16 (MEASURED_PEAKS.json)",
+                     "peak_src": PEAK_SRC[peaks["src"]][0],
                      "gemm_ms_per_step": g["ms"] / args.steps, "gemm_launches_per_step": g["launches"] / args.steps,
                      "timing": "CUDA events around every GEMM launch on the library stream, second timed region of K steps"},
         "kernel_ms_per_step": {k: v["ms"] / args.steps for k, v in prof.items()},
@@ -684,7 +692,7 @@ def main() -> None:
         except Exception as ex:  # noqa: BLE001
             line["large_bf16"] = f"failed: {ex}"
         try:
-            line["microbench"] = microbench_leg(b, ev, peaks["hbm"])
+            line["microbench"] = microbench_leg(b, ev, peaks["hbm"], PEAK_SRC[peaks["src"]][1])
         except Exception as ex:  # noqa: BLE001
             line["microbench"] = f"failed: {ex}"
         try:

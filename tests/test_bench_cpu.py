@@ -2,7 +2,8 @@
 count against the projection shapes, and the attention count against a
 brute-force count of visible (query, key) pairs over the layer kinds that
 parseModernBertConfig gives (global every third layer from the first,
-sliding layers seeing |i - j| <= window / 2)."""
+sliding layers seeing |i - j| <= window / 2); and the roofline denominators,
+which come from MEASURED_PEAKS.json only when it holds both figures."""
 from __future__ import annotations
 
 import sys
@@ -42,3 +43,15 @@ def test_attention_flops_against_pair_count(layers):
 def test_attention_flops_configs2_step():
     lens, _, _ = WL.cfg2_prompts()
     assert abs(bench.attention_flops(WL.BASE, lens) / 1e12 - 0.911) < 5e-4
+
+
+def test_peaks_fall_back_only_when_the_measured_file_lacks_them(tmp_path, monkeypatch):
+    import json
+    monkeypatch.setattr(bench, "ROOT", tmp_path)
+    assert bench.measured_peaks()["src"] == "fallback"  # no file
+    (tmp_path / "MEASURED_PEAKS.json").write_text(json.dumps({"hbm_gbs": 6000.0}))
+    assert bench.measured_peaks()["src"] == "fallback"  # sustained bf16 figure missing
+    (tmp_path / "MEASURED_PEAKS.json").write_text(json.dumps({"hbm_gbs": 6000.0, "bf16_tflops_sustained": 1300.0}))
+    p = bench.measured_peaks()
+    assert p == {"bf16": 1300.0, "hbm": 6000.0, "src": "measured"}
+    assert "MEASURED_PEAKS.json" in bench.PEAK_SRC[p["src"]][0]
